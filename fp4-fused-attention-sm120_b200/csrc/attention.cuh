@@ -1,0 +1,480 @@
+// attention.cuh -- warp-specialised FP4 fused attention forward for sm_100a.
+//
+// Computes, per (batch, head) slice and 128-row query tile,
+//     Out = softmax(Q K^T * scale) V
+// with Q, K pre-quantised to E2M1 + UE8M0 (block 32 along head_dim) and V in
+// FP16 -- the computation of the reference kernel fused_fp4_attention
+// (common.h:68-328), re-designed for Blackwell:
+//
+//   warp 0      TMA producer: Q tile once, then K tiles (codes + scale tiles)
+//               and V tiles through KST/VST-stage mbarrier rings.
+//   warp 1      MMA issuer (one thread): S_j = Q K_j^T with
+//               tcgen05.mma kind::mxf4 block_scale (scales in TMEM, copied with
+//               tcgen05.cp), then O += P_j V_j with tcgen05.mma kind::f16 whose
+//               A operand (P) is read from TMEM.  S is double-buffered in TMEM
+//               so S_{j+1} runs on the tensor cores while S_j is in softmax.
+//   warps 2-5   softmax warpgroup: thread = query row = TMEM lane.  tcgen05.ld
+//               of S_j, online max/sum in FP32 (log2 domain), P_j written back
+//               as FP16 into the S_j columns with tcgen05.st, lazy O rescale
+//               (only when the row max grows by more than 2^8), final O / l.
+//
+// TMEM columns (512 allocated): S0 [0,BN), S1 [BN,2BN), O [2BN, 2BN+D),
+// then the Q scale columns and KST stages of K scale columns.
+//
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
+// FP4ATTN_ETIMEOUT in the device error word, all roles leave their loops,
+// in-flight copies and MMAs are drained (bounded), TMEM is freed, and the CTA
+// returns.  Nothing traps.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ptx_sm100.cuh"
+
+namespace fp4attn {
+
+// Device error word: [0] status code, [1] wait site, [2] block x, [3] block y.
+__device__ int g_fp4attn_error[4];
+
+template <int D, int BN>
+struct FwdCfg {
+    static constexpr int BM = 128;                          // query rows per tile (MMA M)
+    static constexpr int DP = (D + 63) / 64 * 64;           // head_dim padded to the MMA K step
+    static constexpr int QK_ROW = DP / 2;                   // bytes per packed code row
+    static constexpr int CW = QK_ROW == 96 ? 32 : QK_ROW;   // swizzle chunk of a code row
+    static constexpr int NCH = QK_ROW / CW;
+    static constexpr int KSTEPS = DP / 64;                  // mxf4 MMAs per S tile
+    static constexpr int VCW = D == 32 ? 64 : 128;          // swizzle chunk of a V row (bytes)
+    static constexpr int VCH = (2 * D + VCW - 1) / VCW;     // V chunks (TMA boxes) per tile
+    static constexpr int SFA_ATOMS = (DP + 127) / 128;      // 512-B scale atoms per 128-row tile
+    static constexpr int SFB_ATOMS = BN == 128 ? SFA_ATOMS : (DP + 255) / 256;
+    static constexpr int SFB_COLS = 4 * SFB_ATOMS;
+    static constexpr int KST = 3;
+    static constexpr int VST = D > 128 && BN == 128 ? 2 : 3;
+    // TMEM
+    static constexpr int S_COL = 0;
+    static constexpr int O_COL = 2 * BN;
+    static constexpr int SFA_COL = O_COL + D;
+    static constexpr int SFB_COL = SFA_COL + 4 * SFA_ATOMS;
+    static constexpr int TMEM_USED = SFB_COL + KST * SFB_COLS;
+    static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
+    static_assert(D % 32 == 0 && D <= 256, "head_dim");
+    static_assert(BN == 128 || BN == 64, "BN");
+    // shared memory (offsets from a 1024-aligned base)
+    static constexpr int Q_BYTES = BM * QK_ROW;
+    static constexpr int QSF_BYTES = SFA_ATOMS * 512;
+    static constexpr int K_BYTES = BN * QK_ROW;
+    static constexpr int KSF_BYTES = SFB_ATOMS * 512;
+    static constexpr int V_BYTES = VCH * BN * VCW;
+    static constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_QSF = align1k(OFF_Q + Q_BYTES);
+    static constexpr int OFF_K = align1k(OFF_QSF + QSF_BYTES);
+    static constexpr int K_STRIDE = align1k(K_BYTES);
+    static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
+    static constexpr int OFF_V = align1k(OFF_KSF + KST * KSF_BYTES);
+    static constexpr int V_STRIDE = align1k(V_BYTES);
+    static constexpr int OFF_BAR = OFF_V + VST * V_STRIDE;
+    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
+    static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
+};
+
+struct FwdArgs {
+    int seq_q, seq_k;
+    int nq_tiles, nk_tiles;
+    float scale_log2;          // softmax_scale * log2(e)
+    void* out;                 // [slices, seq_q, D] (attention) or [slices, seq_q, seq_k] FP32 (scores)
+    const uint8_t* q_sf;       // [slices][nq_tiles][QSF_BYTES]
+    const uint8_t* k_sf;       // [slices][nk_tiles][KSF_BYTES]
+    unsigned long long timeout_ns;
+};
+
+enum WaitSite : int {
+    kSiteQFull = 1,
+    kSiteKFull,
+    kSiteKEmpty,
+    kSiteVFull,
+    kSiteVEmpty,
+    kSiteSFull,
+    kSitePFull,
+    kSitePvDone,
+    kSiteDrain,
+};
+
+struct WaitCtx {
+    volatile int* abort_flag;
+    unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ void record_timeout(int site)
+{
+    if (atomicCAS(&g_fp4attn_error[0], 0, 4 /*FP4ATTN_ETIMEOUT*/) == 0) {
+        g_fp4attn_error[1] = site;
+        g_fp4attn_error[2] = blockIdx.x;
+        g_fp4attn_error[3] = blockIdx.y;
+    }
+}
+
+// Bounded wait for the phase of `bar` with parity `parity`.  Returns false if
+// another role of this CTA already gave up, or if the bound expires (then it
+// raises the CTA's abort flag and records the site).
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, const WaitCtx& w, int site)
+{
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = ptx::globaltimer_ns();
+    for (uint32_t it = 1; it < (1u << 30); ++it) {
+        if (ptx::mbar_try_wait(bar, parity)) return true;
+        if ((it & 31u) == 0u) {
+            if (*w.abort_flag) return false;
+            if (ptx::globaltimer_ns() - t0 > w.timeout_ns) break;
+        }
+    }
+    *w.abort_flag = 1;
+    record_timeout(site);
+    return false;
+}
+
+// Drain wait used on the way out: ignores the abort flag, bounded by `ns`.
+__device__ __forceinline__ void drain_phase(uint64_t* bar, uint32_t parity, unsigned long long ns)
+{
+    const uint64_t t0 = ptx::globaltimer_ns();
+    for (uint32_t it = 0; it < (1u << 30); ++it) {
+        if (ptx::mbar_try_wait(bar, parity)) return;
+        if ((it & 31u) == 0u && ptx::globaltimer_ns() - t0 > ns) {
+            record_timeout(kSiteDrain);
+            return;
+        }
+    }
+}
+
+template <int D, int BN, typename OutT, bool kScores>
+__global__ void __launch_bounds__(192, 1)
+    fp4_attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const FwdArgs args)
+{
+    using C = FwdCfg<D, BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem + C::OFF_Q;
+    uint8_t* sQsf = smem + C::OFF_QSF;
+    uint8_t* sK = smem + C::OFF_K;
+    uint8_t* sKsf = smem + C::OFF_KSF;
+    uint8_t* sV = smem + C::OFF_V;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + C::KST;
+    uint64_t* v_full = k_empty + C::KST;
+    uint64_t* v_empty = v_full + C::VST;
+    uint64_t* s_full = v_empty + C::VST;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_done = p_full + 2;
+    uint64_t* drain_bar = pv_done + 1;
+
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int qt = blockIdx.x, slice = blockIdx.y;
+    const int q0 = qt * C::BM;
+    const int nk = args.nk_tiles;
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(q_full, 1);
+        for (int i = 0; i < C::KST; i++) {
+            ptx::mbar_init(&k_full[i], 1);
+            ptx::mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < C::VST; i++) {
+            ptx::mbar_init(&v_full[i], 1);
+            ptx::mbar_init(&v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            ptx::mbar_init(&s_full[i], 1);
+            ptx::mbar_init(&p_full[i], 128);
+        }
+        ptx::mbar_init(pv_done, 1);
+        ptx::mbar_init(drain_bar, 1);
+        abort_sh = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&tm_q);
+        ptx::prefetch_tmap(&tm_k);
+        if (!kScores) ptx::prefetch_tmap(&tm_v);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(&tmem_base_sh, 512);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const WaitCtx wctx{&abort_sh, args.timeout_ns};
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            ptx::mbar_arrive_expect_tx(q_full, C::Q_BYTES + C::QSF_BYTES);
+#pragma unroll
+            for (int c = 0; c < C::NCH; c++)
+                ptx::tma_load_3d(sQ + c * C::BM * C::CW, &tm_q, q_full, c * C::CW, q0, slice);
+            ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.nq_tiles + qt) * C::QSF_BYTES,
+                           C::QSF_BYTES, q_full);
+            int k_issued = 0, v_issued = 0;
+            for (int j = 0; j < nk; j++) {
+                const int ks = j % C::KST;
+                if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
+                ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::KSF_BYTES);
+#pragma unroll
+                for (int c = 0; c < C::NCH; c++)
+                    ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW, j * BN,
+                                     slice);
+                ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
+                               args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::KSF_BYTES, C::KSF_BYTES,
+                               &k_full[ks]);
+                k_issued = j + 1;
+                if (!kScores) {
+                    const int vs = j % C::VST;
+                    if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+#pragma unroll
+                    for (int c = 0; c < C::VCH; c++)
+                        ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
+                                         c * (C::VCW / 2), j * BN, slice);
+                    v_issued = j + 1;
+                }
+            }
+            // Every load this thread issued must land before the CTA exits.
+            const unsigned long long drain_ns = 2ull * args.timeout_ns;
+            drain_phase(q_full, 0, drain_ns);
+            for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
+                drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
+            for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
+                drain_phase(&v_full[i % C::VST], (i / C::VST) & 1, drain_ns);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::CW);
+            constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
+            const uint32_t sQ_a = ptx::smem_u32(sQ), sK_a = ptx::smem_u32(sK), sV_a = ptx::smem_u32(sV);
+            bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
+            if (ok) {
+                ptx::tc_fence_after();
+#pragma unroll
+                for (int at = 0; at < C::SFA_ATOMS; at++)
+                    ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL + 4 * at,
+                                              ptx::make_sdesc(ptx::smem_u32(sQsf + 512 * at), 0, 128, ptx::kSwizzleNone));
+            }
+            auto issue_s = [&](int j) -> bool {
+                const int ks = j % C::KST;
+                if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) return false;
+                ptx::tc_fence_after();
+                const uint32_t sfb_base = tmem + C::SFB_COL + ks * C::SFB_COLS;
+#pragma unroll
+                for (int at = 0; at < C::SFB_ATOMS; at++)
+                    ptx::tc_cp_32x128b_warpx4(
+                        sfb_base + 4 * at,
+                        ptx::make_sdesc(ptx::smem_u32(sKsf + ks * C::KSF_BYTES + 512 * at), 0, 128, ptx::kSwizzleNone));
+                const uint32_t s_tmem = tmem + C::S_COL + (j & 1) * BN;
+#pragma unroll
+                for (int kk = 0; kk < C::KSTEPS; kk++) {
+                    const int off = kk * 32, ch = off / C::CW, in = off % C::CW;
+                    const uint64_t adesc = ptx::make_sdesc(sQ_a + ch * C::BM * C::CW + in, 16, 8 * C::CW, qk_layout);
+                    const uint64_t bdesc =
+                        ptx::make_sdesc(sK_a + ks * C::K_STRIDE + ch * BN * C::CW + in, 16, 8 * C::CW, qk_layout);
+                    const uint32_t sf_id = 2u * (kk & 1);
+                    const uint32_t sfa = (tmem + C::SFA_COL + 4 * (kk >> 1)) | (sf_id << 30);
+                    const uint32_t sfb = (sfb_base + (BN == 128 ? 4 : 2) * (kk >> 1)) | (sf_id << 30);
+                    ptx::mma_mxf4(s_tmem, adesc, bdesc, ptx::idesc_mxf4(128, BN, sf_id, sf_id), sfa, sfb,
+                                  kk > 0 ? 1u : 0u);
+                }
+                ptx::tc_commit(&s_full[j & 1]);
+                ptx::tc_commit(&k_empty[ks]);
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < nk; j++) {
+                if (j + 1 < nk && !issue_s(j + 1)) break;
+                if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
+                if (kScores) continue;
+                const int vs = j % C::VST;
+                if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
+                ptx::tc_fence_after();
+                const uint32_t p_tmem = tmem + C::S_COL + (j & 1) * BN;
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t bdesc =
+                        ptx::make_sdesc(sV_a + vs * C::V_STRIDE + kk * 16 * C::VCW, BN * C::VCW, 8 * C::VCW, v_layout);
+                    ptx::mma_f16_ts(tmem + C::O_COL, p_tmem + kk * 8, bdesc, ptx::idesc_f16(128, D, true),
+                                    (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                ptx::tc_commit(&v_empty[vs]);
+                ptx::tc_commit(pv_done);
+            }
+            // Drain every tcgen05 op this thread issued before TMEM is freed.
+            ptx::tc_commit(drain_bar);
+            drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ softmax warpgroup
+        const int wq = warp & 3;                  // TMEM lane quarter this warp may access
+        const int row = wq * 32 + lane;           // query row within the tile
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const float c = args.scale_log2;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nk; j++) {
+            if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
+            ptx::tc_fence_after();
+            const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN;
+            uint32_t sr[BN / 32][32];
+#pragma unroll
+            for (int t = 0; t < BN / 32; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
+            ptx::tc_wait_ld();
+            const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+            if (kScores) {
+                const int grow = q0 + row;
+                if (grow < args.seq_q) {
+                    float* dst = reinterpret_cast<float*>(args.out) +
+                                 (static_cast<size_t>(slice) * args.seq_q + grow) * args.seq_k + static_cast<size_t>(j) * BN;
+#pragma unroll
+                    for (int t = 0; t < BN / 32; t++)
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
+                }
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&p_full[j & 1]);
+                continue;
+            }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < BN / 32; t++)
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    float v = __uint_as_float(sr[t][i]);
+                    if (32 * t + i >= valid) v = -INFINITY;
+                    sr[t][i] = __float_as_uint(v);
+                    mx = fmaxf(mx, v);
+                }
+            const float m_new = fmaxf(m, mx * c);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (j == 0) {
+                m = m_new;
+            } else if (m_new > m + 8.0f) {
+                alpha = ptx::ex2_approx(m - m_new);
+                m = m_new;
+                rescale = true;
+            }
+            float sum = 0.f;
+            uint32_t pk[BN / 64][32];
+#pragma unroll
+            for (int t = 0; t < BN / 32; t++)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float p0 = ptx::ex2_approx(fmaf(__uint_as_float(sr[t][i]), c, -m));
+                    const float p1 = ptx::ex2_approx(fmaf(__uint_as_float(sr[t][i + 1]), c, -m));
+                    sum += p0 + p1;
+                    __half2 h = __floats2half2_rn(p0, p1);
+                    pk[t / 2][(t % 2) * 16 + i / 2] = *reinterpret_cast<uint32_t*>(&h);
+                }
+            l = l * alpha + sum;
+#pragma unroll
+            for (int t = 0; t < BN / 64; t++) ptx::tmem_st32(s_tm + 32 * t, pk[t]);
+            ptx::tc_wait_st();
+            if (j > 0) {
+                // O += P_{j-1} V_{j-1} must have landed before O is rescaled (and
+                // waiting every phase keeps this barrier's parity unambiguous).
+                if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
+                ptx::tc_fence_after();
+                if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+                    for (int t = 0; t < D / 32; t++) {
+                        uint32_t o[32];
+                        const uint32_t o_tm = tmem + lane_off + C::O_COL + 32 * t;
+                        ptx::tmem_ld32(o_tm, o);
+                        ptx::tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        ptx::tmem_st32(o_tm, o);
+                    }
+                    ptx::tc_wait_st();
+                }
+            }
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&p_full[j & 1]);
+        }
+        if (!kScores && ok) {
+            if (wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone)) {
+                ptx::tc_fence_after();
+                const float inv_l = 1.0f / l;
+                const int grow = q0 + row;
+                OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D;
+#pragma unroll 1
+                for (int t = 0; t < D / 32; t++) {
+                    uint32_t o[32];
+                    ptx::tmem_ld32(tmem + lane_off + C::O_COL + 32 * t, o);
+                    ptx::tc_wait_ld();
+                    if (grow < args.seq_q) {
+                        if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                float4 v = make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
+                                                       __uint_as_float(o[i + 2]) * inv_l,
+                                                       __uint_as_float(o[i + 3]) * inv_l);
+                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + 32 * t + i) = v;
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                uint32_t w[4];
+#pragma unroll
+                                for (int k = 0; k < 4; k++) {
+                                    __half2 h = __floats2half2_rn(__uint_as_float(o[i + 2 * k]) * inv_l,
+                                                                  __uint_as_float(o[i + 2 * k + 1]) * inv_l);
+                                    w[k] = *reinterpret_cast<uint32_t*>(&h);
+                                }
+                                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + 32 * t + i) =
+                                    make_uint4(w[0], w[1], w[2], w[3]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
+// A CTA that waits on an mbarrier nothing completes, so that its bounded wait
+// expires: exercises the timeout path (error word + clean exit) on purpose.
+__global__ void timeout_selftest_kernel(unsigned long long timeout_ns)
+{
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_sh;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        abort_sh = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    const WaitCtx w{&abort_sh, timeout_ns};
+    if (threadIdx.x == 0) (void)wait_phase(&bar, 0, w, kSiteQFull);
+    __syncthreads();
+}
+
+}  // namespace fp4attn

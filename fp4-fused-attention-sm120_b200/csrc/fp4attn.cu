@@ -1,0 +1,424 @@
+// fp4attn.cu -- the C ABI of libfp4attn.so (declared in include/fp4attn.h):
+// argument checking, workspace layout, TMA tensor maps and kernel dispatch.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/fp4attn.h"
+#include "attention.cuh"
+#include "quantize.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+#define FP4_CUDA(call)                                                                              \
+    do {                                                                                            \
+        cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess) return fail(FP4ATTN_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+constexpr int kSupportedDims[] = {32, 64, 96, 128, 160, 256};
+
+bool supported_dim(int d)
+{
+    for (int x : kSupportedDims)
+        if (x == d) return true;
+    return false;
+}
+
+int block_n_for(int d) { return d == 256 ? 64 : 128; }
+int padded_dim(int d) { return (d + 63) / 64 * 64; }
+int sfa_atoms(int d) { return (padded_dim(d) + 127) / 128; }
+int sf_tile_bytes(int d, int tile_rows)
+{
+    return tile_rows == 128 ? 512 * sfa_atoms(d) : 512 * ((padded_dim(d) + 255) / 256);
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct Workspace {
+    size_t q_codes, k_codes, q_sf, k_sf, v16, total;
+};
+
+Workspace plan_workspace(int64_t slices, int sq, int sk, int d, int in_dtype)
+{
+    const int dp = padded_dim(d), bn = block_n_for(d);
+    const int64_t nq = (sq + 127) / 128, nk = (sk + bn - 1) / bn;
+    Workspace w{};
+    size_t off = 0;
+    w.q_codes = off;
+    off = align256(off + static_cast<size_t>(slices) * sq * (dp / 2));
+    w.k_codes = off;
+    off = align256(off + static_cast<size_t>(slices) * sk * (dp / 2));
+    w.q_sf = off;
+    off = align256(off + static_cast<size_t>(slices) * nq * sf_tile_bytes(d, 128));
+    w.k_sf = off;
+    off = align256(off + static_cast<size_t>(slices) * nk * sf_tile_bytes(d, bn));
+    w.v16 = off;
+    if (in_dtype == FP4ATTN_F32) off = align256(off + static_cast<size_t>(slices) * sk * d * 2);
+    w.total = off;
+    return w;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D tensor map over [slices][rows][inner] with a (box_inner, box_rows, 1)
+// box; rows past `rows` read as zero.
+int make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
+                uint64_t rows, uint64_t slices, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw)
+{
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(FP4ATTN_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {inner, rows, slices};
+    cuuint64_t strides[2] = {inner * elem_bytes, inner * rows * elem_bytes};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FP4ATTN_ECUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return FP4ATTN_OK;
+}
+
+CUtensorMapSwizzle swizzle_for(int bytes)
+{
+    return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+int device_ready()
+{
+    static std::once_flag once;
+    static int status = FP4ATTN_OK;
+    static std::string msg;
+    std::call_once(once, [] {
+        int dev = 0;
+        cudaDeviceProp prop;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+            status = FP4ATTN_ECUDA;
+            msg = "no CUDA device";
+            return;
+        }
+        if (prop.major != 10) {
+            status = FP4ATTN_EUNSUPPORTED;
+            msg = "libfp4attn requires an sm_100 (B200-class) GPU; found sm_" + std::to_string(prop.major) +
+                  std::to_string(prop.minor);
+            return;
+        }
+        if (cudaMemcpyToSymbol(fp4attn::kLog2CeilCompat, kLog2CeilCompatInit, sizeof kLog2CeilCompatInit) !=
+            cudaSuccess) {
+            status = FP4ATTN_ECUDA;
+            msg = "could not upload the scale table";
+        }
+    });
+    if (status != FP4ATTN_OK) return fail(status, "%s", msg.c_str());
+    return FP4ATTN_OK;
+}
+
+unsigned long long wait_timeout_ns()
+{
+    static unsigned long long ns = [] {
+        const char* s = getenv("FP4ATTN_WAIT_TIMEOUT_MS");
+        long ms = s ? atol(s) : 2000;
+        if (ms < 1) ms = 1;
+        return static_cast<unsigned long long>(ms) * 1000000ull;
+    }();
+    return ns;
+}
+
+int grid_for(int64_t work, int per_block = 256)
+{
+    int64_t b = (work + per_block - 1) / per_block;
+    if (b > 148 * 32) b = 148 * 32;
+    return static_cast<int>(b < 1 ? 1 : b);
+}
+
+template <typename InT>
+int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slices, int seq, int d, int tile_rows,
+                       int ocp, cudaStream_t st)
+{
+    fp4attn::QuantTileArgs a;
+    a.slices = slices;
+    a.seq = seq;
+    a.head_dim = d;
+    a.padded_dim = padded_dim(d);
+    a.tile_rows = tile_rows;
+    a.ntiles = (seq + tile_rows - 1) / tile_rows;
+    a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
+    a.ocp_mode = ocp;
+    const int64_t work = slices * static_cast<int64_t>(a.ntiles) * tile_rows * (a.padded_dim / 32);
+    fp4attn::quantize_tiles_kernel<InT><<<grid_for(work), 256, 0, st>>>(static_cast<const InT*>(x), codes, sf, a);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+template <int D, int BN, typename OutT, bool kScores>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
+               int64_t slices, cudaStream_t st)
+{
+    using C = fp4attn::FwdCfg<D, BN>;
+    auto kern = fp4attn::fp4_attention_fwd_kernel<D, BN, OutT, kScores>;
+    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
+    dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
+    kern<<<grid, 192, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+template <int D, bool kScores>
+int dispatch_out(int out_dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                 const fp4attn::FwdArgs& a, int64_t slices, cudaStream_t st)
+{
+    constexpr int BN = D == 256 ? 64 : 128;
+    if (kScores) return launch_fwd<D, BN, float, true>(tq, tk, tv, a, slices, st);
+    if (out_dtype == FP4ATTN_F32) return launch_fwd<D, BN, float, false>(tq, tk, tv, a, slices, st);
+    return launch_fwd<D, BN, __half, false>(tq, tk, tv, a, slices, st);
+}
+
+template <bool kScores>
+int dispatch_dim(int d, int out_dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                 const fp4attn::FwdArgs& a, int64_t slices, cudaStream_t st)
+{
+    switch (d) {
+        case 32: return dispatch_out<32, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+        case 64: return dispatch_out<64, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+        case 96: return dispatch_out<96, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+        case 128: return dispatch_out<128, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+        case 160: return dispatch_out<160, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+        case 256: return dispatch_out<256, kScores>(out_dtype, tq, tk, tv, a, slices, st);
+    }
+    return fail(FP4ATTN_EUNSUPPORTED, "head_dim %d not compiled", d);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_problem(const void* Q, const void* K, const void* V, const void* Out, int in_dtype, int out_dtype, int batch,
+                  int heads, int sq, int sk, int d, int scale_mode, bool need_v)
+{
+    if (!Q || !K || !Out || (need_v && !V)) return fail(FP4ATTN_EINVAL, "null tensor pointer");
+    if (!aligned16(Q) || !aligned16(K) || !aligned16(Out) || (need_v && !aligned16(V)))
+        return fail(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned");
+    if (in_dtype != FP4ATTN_F32 && in_dtype != FP4ATTN_F16) return fail(FP4ATTN_EINVAL, "in_dtype %d", in_dtype);
+    if (out_dtype != FP4ATTN_F32 && out_dtype != FP4ATTN_F16) return fail(FP4ATTN_EINVAL, "out_dtype %d", out_dtype);
+    if (scale_mode != FP4ATTN_SCALE_REFERENCE && scale_mode != FP4ATTN_SCALE_OCP)
+        return fail(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
+    if (batch < 1 || heads < 1 || sq < 1 || sk < 1)
+        return fail(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads, sq,
+                    sk);
+    if (!supported_dim(d)) return fail(FP4ATTN_EUNSUPPORTED, "head_dim %d is not one of 32/64/96/128/160/256", d);
+    if (static_cast<int64_t>(batch) * heads > 65535) return fail(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
+    return FP4ATTN_OK;
+}
+
+// Quantise Q and K into the workspace and build the three tensor maps.
+int prepare(const void* Q, const void* K, const void* V, int in_dtype, int64_t slices, int sq, int sk, int d,
+            int scale_mode, uint8_t* ws, const Workspace& w, bool need_v, CUtensorMap* tq, CUtensorMap* tk,
+            CUtensorMap* tv, cudaStream_t st)
+{
+    const int dp = padded_dim(d), bn = block_n_for(d);
+    const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
+    int rc;
+    if (in_dtype == FP4ATTN_F16) {
+        if ((rc = launch_quant_tiles<__half>(Q, ws + w.q_codes, ws + w.q_sf, slices, sq, d, 128, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<__half>(K, ws + w.k_codes, ws + w.k_sf, slices, sk, d, bn, ocp, st))) return rc;
+    } else {
+        if ((rc = launch_quant_tiles<float>(Q, ws + w.q_codes, ws + w.q_sf, slices, sq, d, 128, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<float>(K, ws + w.k_codes, ws + w.k_sf, slices, sk, d, bn, ocp, st))) return rc;
+    }
+    const int cw = dp / 2 == 96 ? 32 : dp / 2;
+    if ((rc = make_map_3d(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.q_codes, dp / 2, sq, slices, cw, 128,
+                          swizzle_for(cw))))
+        return rc;
+    if ((rc = make_map_3d(tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, dp / 2, sk, slices, cw, bn,
+                          swizzle_for(cw))))
+        return rc;
+    *tv = *tk;
+    if (need_v) {
+        const void* v16 = V;
+        if (in_dtype == FP4ATTN_F32) {
+            const int64_t n4 = slices * static_cast<int64_t>(sk) * d / 4;
+            fp4attn::f32_to_f16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4*>(V),
+                                                                     reinterpret_cast<uint2*>(ws + w.v16), n4);
+            FP4_CUDA(cudaGetLastError());
+            v16 = ws + w.v16;
+        }
+        const int vcw = d == 32 ? 64 : 128;
+        if ((rc = make_map_3d(tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v16, d, sk, slices, vcw / 2, bn,
+                              swizzle_for(vcw))))
+            return rc;
+    }
+    return FP4ATTN_OK;
+}
+
+int run(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads,
+        int sq, int sk, int d, float softmax_scale, int scale_mode, void* workspace, size_t ws_bytes, void* stream,
+        bool scores)
+{
+    g_last_error.clear();
+    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, sq, sk, d, scale_mode, !scores);
+    if (rc) return rc;
+    if ((rc = device_ready())) return rc;
+    const int64_t slices = static_cast<int64_t>(batch) * heads;
+    const Workspace w = plan_workspace(slices, sq, sk, d, scores ? FP4ATTN_F16 : in_dtype);
+    if (!workspace || ws_bytes < w.total)
+        return fail(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w.total, workspace ? ws_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    CUtensorMap tq, tk, tv;
+    if ((rc = prepare(Q, K, V, in_dtype, slices, sq, sk, d, scale_mode, ws, w, !scores, &tq, &tk, &tv, st))) return rc;
+    const int bn = block_n_for(d);
+    fp4attn::FwdArgs a;
+    a.seq_q = sq;
+    a.seq_k = sk;
+    a.nq_tiles = (sq + 127) / 128;
+    a.nk_tiles = (sk + bn - 1) / bn;
+    const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(d));
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = Out;
+    a.q_sf = ws + w.q_sf;
+    a.k_sf = ws + w.k_sf;
+    a.timeout_ns = wait_timeout_ns();
+    if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, slices, st);
+    return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, slices, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8_t* codes, uint8_t* scales,
+                     int scale_mode, int layout, void* stream)
+{
+    g_last_error.clear();
+    if (!x || !codes || !scales) return fail(FP4ATTN_EINVAL, "null pointer");
+    if (!aligned16(x) || !aligned16(codes)) return fail(FP4ATTN_EINVAL, "x and codes must be 16-byte aligned");
+    if (rows < 0 || head_dim < 32 || head_dim % 32) return fail(FP4ATTN_EINVAL, "rows >= 0, head_dim a multiple of 32");
+    if (dtype != FP4ATTN_F32 && dtype != FP4ATTN_F16) return fail(FP4ATTN_EINVAL, "dtype %d", dtype);
+    if (scale_mode != FP4ATTN_SCALE_REFERENCE && scale_mode != FP4ATTN_SCALE_OCP)
+        return fail(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
+    if (layout != FP4ATTN_LAYOUT_ROWMAJOR) return fail(FP4ATTN_EINVAL, "layout %d", layout);
+    int rc = device_ready();
+    if (rc) return rc;
+    if (rows == 0) return FP4ATTN_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t work = rows * (head_dim / 32);
+    const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
+    if (dtype == FP4ATTN_F16)
+        fp4attn::quantize_rowmajor_kernel<__half>
+            <<<grid_for(work), 256, 0, st>>>(static_cast<const __half*>(x), rows, head_dim, codes, scales, ocp);
+    else
+        fp4attn::quantize_rowmajor_kernel<float>
+            <<<grid_for(work), 256, 0, st>>>(static_cast<const float*>(x), rows, head_dim, codes, scales, ocp);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+size_t fp4attn_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype)
+{
+    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || !supported_dim(head_dim)) return 0;
+    if (in_dtype != FP4ATTN_F32 && in_dtype != FP4ATTN_F16) return 0;
+    return plan_workspace(static_cast<int64_t>(batch) * heads, seq_q, seq_k, head_dim, in_dtype).total;
+}
+
+int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype, int batch,
+                    int heads, int seq_q, int seq_k, int head_dim, float softmax_scale, int scale_mode,
+                    void* workspace, size_t workspace_bytes, void* stream)
+{
+    return run(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, scale_mode,
+               workspace, workspace_bytes, stream, false);
+}
+
+int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, int batch, int heads, int seq_q,
+                         int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes,
+                         void* stream)
+{
+    g_last_error.clear();
+    return run(Q, K, nullptr, S, in_dtype, FP4ATTN_F32, batch, heads, seq_q, seq_k, head_dim, 1.0f, scale_mode,
+               workspace, workspace_bytes, stream, true);
+}
+
+int fp4attn_status_query(void* stream)
+{
+    g_last_error.clear();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    FP4_CUDA(cudaStreamSynchronize(st));
+    int host[4] = {0, 0, 0, 0};
+    FP4_CUDA(cudaMemcpyFromSymbol(host, fp4attn::g_fp4attn_error, sizeof host));
+    if (host[0] == 0) return FP4ATTN_OK;
+    const int zero[4] = {0, 0, 0, 0};
+    FP4_CUDA(cudaMemcpyToSymbol(fp4attn::g_fp4attn_error, zero, sizeof zero));
+    return fail(host[0], "device wait expired at site %d (block %d,%d)", host[1], host[2], host[3]);
+}
+
+int fp4attn_selftest_timeout(unsigned timeout_us, void* stream)
+{
+    g_last_error.clear();
+    int rc = device_ready();
+    if (rc) return rc;
+    if (timeout_us < 1 || timeout_us > 10000000u) return fail(FP4ATTN_EINVAL, "timeout_us in [1, 1e7]");
+    fp4attn::timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<unsigned long long>(timeout_us) * 1000ull);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+const char* fp4attn_error_string(int status)
+{
+    switch (status) {
+        case FP4ATTN_OK: return "ok";
+        case FP4ATTN_EINVAL: return "invalid argument";
+        case FP4ATTN_EUNSUPPORTED: return "unsupported head_dim or device";
+        case FP4ATTN_ECUDA: return "CUDA error";
+        case FP4ATTN_ETIMEOUT: return "device wait timed out";
+        case FP4ATTN_EWORKSPACE: return "workspace missing or too small";
+    }
+    return "unknown status";
+}
+
+const char* fp4attn_last_error(void) { return g_last_error.c_str(); }
+
+int fp4attn_supported_head_dims(int* dims, int cap)
+{
+    int n = 0;
+    for (int x : kSupportedDims) {
+        if (dims && n < cap) dims[n] = x;
+        n++;
+    }
+    return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,213 @@
+// quantize.cuh -- the E2M1 + UE8M0 quantiser (sm_100a), bit-exact with the
+// reference's encode_fp4_e2m1 / compute_scale_ue8m0 (common.h:21-48) and its
+// quantisation loop (common.h:115-123, :160-168).
+//
+// One thread per 32-element block: it reads the block (64 B of FP16 or 128 B
+// of FP32), finds max|x|, forms the scale byte, and writes 16 bytes of packed
+// codes (element 2i in the low nibble) plus the scale byte.  The kernel is
+// HBM-bound: 2 (or 4) bytes in and 0.53 bytes out per element.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "log2_compat.h"
+
+namespace fp4attn {
+
+// See gen_log2_compat.c: largest mantissa remainder, per binade, for which the
+// reference's host build (glibc log2f) rounds ceil(log2(y)) down to p.
+__constant__ uint8_t kLog2CeilCompat[FP4ATTN_LOG2_COMPAT_ENTRIES];
+
+// compute_scale_ue8m0 (common.h:39-48) on the block maximum `amax` (>= +0):
+// exponent = ceilf(log2f(y)) as the reference's host build evaluates it,
+// byte = (uint8)(exponent + 127).  y = 0 or +inf make the reference's float
+// -> int conversion produce INT_MIN, whose low byte after +127 is 0x7F.
+__device__ __forceinline__ uint32_t scale_byte(float amax, int ocp_mode)
+{
+    const float y = ocp_mode ? amax / 6.0f : amax;
+    const uint32_t b = __float_as_uint(y);
+    const uint32_t e = b >> 23;
+    if (b == 0u || e == 0xFFu) return 127u;
+    int p;
+    uint32_t rem;
+    if (e == 0u) {  // subnormal: y = b * 2^-149
+        const int msb = 31 - __clz(b);
+        p = msb - 149;
+        rem = b - (1u << msb);
+    } else {
+        p = static_cast<int>(e) - 127;
+        rem = b & 0x7FFFFFu;
+    }
+    const int c = (rem == 0u || rem <= kLog2CeilCompat[p + 149]) ? p : p + 1;
+    return static_cast<uint32_t>(c + 127) & 0xFFu;
+}
+
+// encode_fp4_e2m1 (common.h:21-36) without the <<2 container shift: the
+// magnitude index is the number of thresholds (>=, ties up) below |q|, and the
+// sign bit is (q < 0).  NaN fails every comparison and encodes as 0.
+__device__ __forceinline__ uint32_t encode_e2m1(float q)
+{
+    const float a = fabsf(q);
+    const uint32_t n = (a >= 0.25f) + (a >= 0.75f) + (a >= 1.25f) + (a >= 1.75f) + (a >= 2.5f) + (a >= 3.5f) +
+                       (a >= 5.0f);
+    return n | (q < 0.f ? 8u : 0u);
+}
+
+// Exactly 2^-s for s in [-127, 127] (2^-127 is the subnormal 1 << 22).
+__device__ __forceinline__ float exact_pow2_neg(int s)
+{
+    const int k = -s;
+    return k >= -126 ? __uint_as_float(static_cast<uint32_t>(k + 127) << 23) : __uint_as_float(1u << 22);
+}
+
+template <typename InT>
+__device__ __forceinline__ void load_block32(const InT* src, float (&v)[32]);
+
+template <>
+__device__ __forceinline__ void load_block32<__half>(const __half* src, float (&v)[32])
+{
+    const uint4* p = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint4 u = __ldg(p + i);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float2 f = __half22float2(h[k]);
+            v[i * 8 + 2 * k] = f.x;
+            v[i * 8 + 2 * k + 1] = f.y;
+        }
+    }
+}
+
+template <>
+__device__ __forceinline__ void load_block32<float>(const float* src, float (&v)[32])
+{
+    const float4* p = reinterpret_cast<const float4*>(src);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float4 f = __ldg(p + i);
+        v[i * 4 + 0] = f.x;
+        v[i * 4 + 1] = f.y;
+        v[i * 4 + 2] = f.z;
+        v[i * 4 + 3] = f.w;
+    }
+}
+
+// Quantises one block; returns the reference scale byte and fills 16 bytes of
+// packed codes (the common.h:118-122 loop: x / exp2f(scale - 127), encoded).
+__device__ __forceinline__ uint32_t quantize_block32(const float (&v)[32], int ocp_mode, uint4& packed)
+{
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const float a = fabsf(v[i]);
+        amax = a > amax ? a : amax;  // NaN never wins, as in common.h:44
+    }
+    const uint32_t sb = scale_byte(amax, ocp_mode);
+    const int s = static_cast<int>(sb) - 127;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (s != 128) {  // s == 128: the reference divides by exp2f(128) = inf, every code is 0
+        const float inv = exact_pow2_neg(s);  // x * 2^-s rounds exactly like x / 2^s
+#pragma unroll
+        for (int i = 0; i < 32; i++) w[i / 8] |= encode_e2m1(v[i] * inv) << (4 * (i % 8));
+    }
+    packed = make_uint4(w[0], w[1], w[2], w[3]);
+    return sb;
+}
+
+// Byte offset of scale (row rr of a tile, scale index b along head_dim) inside
+// one tile of the tensor-core scale layout.  For 128-row tiles a 512-byte atom
+// holds 128 rows x 4 scales: byte = (rr%32)*16 + (rr/32)*4 + b%4, atoms in
+// b/4 order.  For 64-row tiles an atom holds 64 rows x 8 scales:
+// byte = (rr%32)*16 + ((b/4)%2)*8 + (rr/32)*4 + b%4, atoms in b/8 order.
+// tcgen05.cp.32x128b.warpx4 moves one atom into 4 TMEM columns exactly as the
+// block-scaled MMA reads them (row m at column m/32, byte = scale index).
+__host__ __device__ __forceinline__ uint32_t sf_tile_offset(int tile_rows, int rr, int b)
+{
+    if (tile_rows == 128) return static_cast<uint32_t>((b / 4) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + (b % 4));
+    return static_cast<uint32_t>((b / 8) * 512 + (rr % 32) * 16 + ((b / 4) % 2) * 8 + (rr / 32) * 4 + (b % 4));
+}
+
+struct QuantTileArgs {
+    int64_t slices;
+    int seq;         // rows per slice
+    int head_dim;    // D (multiple of 32)
+    int padded_dim;  // DP, multiple of 64 (the MMA's K step)
+    int tile_rows;   // 128 or 64
+    int ntiles;      // ceil(seq / tile_rows)
+    int sf_tile_bytes;
+    int ocp_mode;
+};
+
+// Quantise into the layout the attention kernel loads with TMA:
+// codes [slices][seq][DP/2] (blocks beyond D are zero) and scale tiles
+// [slices][ntiles][sf_tile_bytes].  Rows past seq inside the last tile get
+// scale 127 so the (zero-filled) padding never multiplies an undefined scale.
+// A reference scale of 255 only occurs with all-zero codes and is stored as
+// 254, which the MMA reads as a finite 2^127 (255 would be NaN in E8M0).
+template <typename InT>
+__global__ void __launch_bounds__(256) quantize_tiles_kernel(const InT* __restrict__ x, uint8_t* __restrict__ codes,
+                                                             uint8_t* __restrict__ sf, QuantTileArgs a)
+{
+    const int nb = a.padded_dim / 32;
+    const int64_t seq_pad = static_cast<int64_t>(a.ntiles) * a.tile_rows;
+    const int64_t total = a.slices * seq_pad * nb;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int b = static_cast<int>(idx % nb);
+        const int64_t rowp = idx / nb;
+        const int64_t slice = rowp / seq_pad;
+        const int r = static_cast<int>(rowp % seq_pad);
+        uint32_t sb = 127u;
+        if (r < a.seq) {
+            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+            const int64_t row = slice * a.seq + r;
+            if (b * 32 < a.head_dim) {
+                float v[32];
+                load_block32<InT>(x + row * a.head_dim + b * 32, v);
+                sb = quantize_block32(v, a.ocp_mode, packed);
+                if (sb == 255u) sb = 254u;
+            }
+            *reinterpret_cast<uint4*>(codes + row * (a.padded_dim / 2) + b * 16) = packed;
+        }
+        const int tile = r / a.tile_rows, rr = r % a.tile_rows;
+        sf[(slice * a.ntiles + tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
+            static_cast<uint8_t>(sb);
+    }
+}
+
+// Row-major quantisation for the public fp4attn_quantize: codes rows x D/2,
+// scales rows x D/32, raw reference bytes (255 kept).
+template <typename InT>
+__global__ void __launch_bounds__(256) quantize_rowmajor_kernel(const InT* __restrict__ x, int64_t rows, int head_dim,
+                                                                uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                                                                int ocp_mode)
+{
+    const int nb = head_dim / 32;
+    const int64_t total = rows * nb;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v[32];
+        load_block32<InT>(x + idx * 32, v);
+        uint4 packed;
+        const uint32_t sb = quantize_block32(v, ocp_mode, packed);
+        *reinterpret_cast<uint4*>(codes + idx * 16) = packed;
+        sf[idx] = static_cast<uint8_t>(sb);
+    }
+}
+
+// FP32 -> FP16 (round to nearest even) for V when the caller passes FP32.
+__global__ void __launch_bounds__(256) f32_to_f16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst,
+                                                         int64_t n4)
+{
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 f = src[i];
+        __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+        dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+}
+
+}  // namespace fp4attn

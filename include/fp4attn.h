@@ -1,0 +1,140 @@
+/*
+ * fp4attn.h -- C ABI of libfp4attn.so, the sm_100a (B200) FP4 fused attention.
+ *
+ * Drop-in boundary for the reference florianmattana/fp4-fused-attention-sm120.
+ * The reference exposes no library: its public surface is the header
+ * common.h -- the encoders encode_fp4_e2m1 / compute_scale_ue8m0
+ * (common.h:21-48), the kernel template
+ *     template<int HEAD_DIM> __global__ void fused_fp4_attention(
+ *         const float* Q, const float* K, float* Out, const float* V,
+ *         int seq_q, int seq_k, int heads)                      (common.h:68-77)
+ * launched as <<<batch*heads, NUM_THREADS>>> (tests/test_attention.cu:160-161),
+ * and the constants BLOCK_ELEMENT / BQ (common.h:15, :18).  Each entry point
+ * below names the reference interface it replaces.
+ *
+ * Conventions: all pointers are device pointers unless stated; tensors are
+ * contiguous [batch, heads, seq, head_dim] (the reference layout,
+ * common.h:99-102); `stream` is a cudaStream_t (0 = legacy default stream).
+ * Every call is asynchronous on `stream` and returns an fp4attn_status code;
+ * a non-zero code means nothing was launched.  The library keeps no state
+ * between calls except a per-device error word (fp4attn_status_query) and
+ * cached function attributes.  Calls on different streams may run
+ * concurrently; the caller owns all buffers.
+ */
+#ifndef FP4ATTN_H
+#define FP4ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- constants kept from the reference (common.h:12, :15, :18) ---------- */
+#define FP4ATTN_BLOCK_ELEMENT 32 /* elements per UE8M0 scale (BLOCK_ELEMENT) */
+#define FP4ATTN_BQ 64            /* the reference's fixed Q tile (BQ)         */
+
+/* ---- status codes ------------------------------------------------------- */
+typedef enum {
+    FP4ATTN_OK = 0,
+    FP4ATTN_EINVAL = 1,       /* bad shape, dtype, pointer alignment or size  */
+    FP4ATTN_EUNSUPPORTED = 2, /* head_dim not compiled / no sm_100 device     */
+    FP4ATTN_ECUDA = 3,        /* a CUDA runtime or driver call failed          */
+    FP4ATTN_ETIMEOUT = 4,     /* a kernel's bounded wait expired (reported by  */
+                              /* fp4attn_status_query after the stream syncs) */
+    FP4ATTN_EWORKSPACE = 5    /* workspace missing or too small               */
+} fp4attn_status;
+
+/* ---- element types ------------------------------------------------------ */
+typedef enum { FP4ATTN_F32 = 0, FP4ATTN_F16 = 1 } fp4attn_dtype;
+
+/* ---- UE8M0 scale rules -------------------------------------------------- */
+typedef enum {
+    /* The reference rule, bit-exact with compute_scale_ue8m0 (common.h:39-48)
+     * as built on the host with glibc: byte = (uint8)(ceil(log2(max|x|)) + 127),
+     * an all-zero block gives 127. */
+    FP4ATTN_SCALE_REFERENCE = 0,
+    /* OCP-MX style: byte = (uint8)(ceil(log2(max|x| / 6)) + 127).  Not part of
+     * the reference; offered because it uses the full E2M1 range. */
+    FP4ATTN_SCALE_OCP = 1
+} fp4attn_scale_mode;
+
+/* ---- layouts of quantised output ---------------------------------------- */
+typedef enum {
+    /* codes: rows x head_dim/2 bytes, two E2M1 codes per byte, element 2i in
+     * the low nibble; scales: rows x head_dim/32 bytes, row-major. */
+    FP4ATTN_LAYOUT_ROWMAJOR = 0
+} fp4attn_layout;
+
+/* Quantise `rows` rows of `head_dim` elements (head_dim % 32 == 0) to E2M1
+ * codes plus one UE8M0 scale per 32 elements.
+ * Replaces: the per-tile quantisation inside the reference kernel
+ * (common.h:108-124 for Q, :159-169 for K) built from encode_fp4_e2m1 and
+ * compute_scale_ue8m0 (common.h:21-48).  The reference returns each code in an
+ * 8-bit container (code << 2, common.h:35); this packs two codes per byte.
+ * x: device, dtype elements; codes: rows*head_dim/2 bytes; scales:
+ * rows*head_dim/32 bytes. */
+int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8_t* codes,
+                     uint8_t* scales, int scale_mode, int layout, void* stream);
+
+/* Bytes of device workspace fp4attn_forward needs for this problem (the
+ * quantised Q/K tiles, their scale tiles, and an FP16 copy of V when V is
+ * FP32).  Returns 0 for an invalid shape. */
+size_t fp4attn_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype);
+
+/* Out = softmax(Q K^T * softmax_scale) V per (batch, head) slice, with Q and K
+ * quantised to E2M1 + UE8M0 (block 32 along head_dim) and V, P in FP16 on the
+ * tensor cores (FP32 accumulation).
+ * Replaces: fused_fp4_attention<HEAD_DIM><<<batch*heads, 128>>>(Q, K, Out, V,
+ * seq_q, seq_k, heads) (common.h:68-77; tests/test_attention.cu:160-161).
+ * Differences, by design: any seq_q >= 1 (the reference computes only the
+ * first 64 query rows, common.h:96-102) and any seq_k >= 1 (the reference
+ * needs seq_k % 64 == 0, common.h:67); head_dim is a runtime argument among
+ * {32, 64, 96, 128, 160, 256}; inputs and output may be FP32 (as in the
+ * reference) or FP16.
+ * Q: [batch, heads, seq_q, head_dim]; K, V: [batch, heads, seq_k, head_dim];
+ * Out: [batch, heads, seq_q, head_dim] of out_dtype; all 16-byte aligned.
+ * softmax_scale <= 0 selects 1/sqrt(head_dim) (common.h:130).
+ * workspace: device memory of at least fp4attn_workspace_size(...) bytes,
+ * 256-byte aligned; it must not be used by another call in flight. */
+int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                    int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                    int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
+ * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
+ * power-of-two scales are exact, S is checkable bit for bit.
+ * Replaces: the reference's debug kernel debug_mma (common.h:331-398), which
+ * computes one 64x64 tile of Q K^T on FP4 codes. */
+int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, int batch, int heads,
+                         int seq_q, int seq_k, int head_dim, int scale_mode, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device error word that kernels set when a bounded
+ * wait expires.  Synchronises `stream` first.  Returns FP4ATTN_OK or
+ * FP4ATTN_ETIMEOUT (or FP4ATTN_ECUDA if the query itself fails).  The
+ * reference has no device-side error reporting (callers only poll
+ * cudaGetLastError, tests/test_attention.cu:103-105). */
+int fp4attn_status_query(void* stream);
+
+/* Test hook for the failure path: launches one CTA that waits on an mbarrier
+ * nothing will complete, with the given bound, so that the bounded wait runs
+ * out and sets the error word.  No fault, trap or hang is involved. */
+int fp4attn_selftest_timeout(unsigned timeout_us, void* stream);
+
+/* Static description of a status code. */
+const char* fp4attn_error_string(int status);
+
+/* Detail of the last failure on the calling host thread ("" if none). */
+const char* fp4attn_last_error(void);
+
+/* Head dims compiled into this library, written to `dims` (up to `cap`);
+ * returns how many there are. */
+int fp4attn_supported_head_dims(int* dims, int cap);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* FP4ATTN_H */
