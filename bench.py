@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Benchmark of the FP4 fused attention path on B200 (one process per GPU).
+
+Metric: fused FP4 attention TFLOPS = 4 * B * H * seq_q * seq_k * head_dim / t
+(the reference's formula, tests/benchmark.cu:85-86), plus the fraction of the
+mixed FP4/FP16 tensor roofline.  One step = one pass of the path over this
+rank's shard: quantise Q and K (E2M1 + UE8M0/32) and run the attention kernel,
+inputs resident in HBM.  Default workload: the prefill-sized single-GPU case,
+batch 2, heads 32, seq_q = seq_k = 4096, head_dim 128, FP16 in/out.  Under
+torchrun each rank runs that workload's 64 (batch x head) slices as its shard
+of a job with 64*N slices (weak scaling, no collective on the data path; NCCL
+only carries the barrier and the max-over-ranks of the timings).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="prefill_4k")
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def mixed_roofline(w, bf16_tflops):
+    """Mixed FP4/FP16 tensor roofline for this workload's FLOPs: QK^T at the
+    dense FP4 peak (4x the dense FP16 peak, NVIDIA's ratio for B200) and P.V at
+    the dense FP16 peak, the FP16 peak being the measured bf16 GEMM figure.
+    Returns the equivalent peak in TFLOP/s for the whole 4*B*H*sq*sk*d."""
+    f_half = w.flops() / 2
+    t = f_half / (4 * bf16_tflops) + f_half / bf16_tflops
+    return w.flops() / t
+
+
+class ClockSampler:
+    """nvidia-smi samples (100 ms) of SM clock and throttle reasons."""
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [l for (t, l) in self.lines if t0 <= t <= t1]
+        if not rows:  # region shorter than the sampling period: nearest samples
+            rows = [l for (t, l) in sorted(self.lines, key=lambda x: abs(x[0] - (t0 + t1) / 2))[:2]]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            f = [x.strip() for x in r.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                sm.append(float(f[2]))
+                mx = float(f[3])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[6:10]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def profile_traffic(workload):
+    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"fp4_attention_fwd_{workload}.md"
+    if p.exists():
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+class CpuReference:
+    """The reference's CPU path (oracle/_ref: its quantiser and cpu_attention,
+    tests/test_attention.cu:33-54, one slice per std::thread) on a bounded
+    sample of the workload: one slice per host thread, each with a prefix of
+    its query rows against all seq_k keys.  Falls back to the oracle port when
+    _ref was not built (kind "port")."""
+
+    def __init__(self, w, threads=None):
+        import numpy as np
+        import oracle
+        self.w = w
+        self.oracle = oracle
+        self.threads = threads or os.cpu_count() or 1
+        self.kind = "reference" if oracle.ref_available() else "port"
+        rng = np.random.default_rng(0)
+        n = self.threads
+        shape = (n, w.seq_k, w.head_dim)
+        self.K = (rng.standard_normal(shape, dtype=np.float32) * w.std).astype(np.float16).astype(np.float32)
+        self.V = (rng.standard_normal(shape, dtype=np.float32) * w.std).astype(np.float16).astype(np.float32)
+        self.Qfull = (rng.standard_normal((n, w.seq_q, w.head_dim), dtype=np.float32) * w.std
+                      ).astype(np.float16).astype(np.float32)
+        self.rows = 1
+
+    def run(self, rows):
+        Q = self.Qfull[:, :rows].copy()
+        t = time.perf_counter()
+        if self.kind == "reference":
+            self.oracle.ref_fp4_attention(Q, self.K, self.V, threads=self.threads)
+        else:
+            self.oracle.fp4_attention(Q, self.K, self.V, threads=self.threads)
+        dt = time.perf_counter() - t
+        return 4.0 * self.threads * rows * self.w.seq_k * self.w.head_dim / dt / 1e12, dt
+
+    def calibrate(self, budget_s):
+        _, t1 = self.run(2)
+        self.rows = int(max(1, min(self.w.seq_q, 2 * budget_s / max(t1, 1e-6))))
+        return self.rows
+
+    def sample(self):
+        return f"{self.threads} slices x {self.rows} query rows x {self.w.seq_k} keys x d{self.w.head_dim}"
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def reference_arm(args, world, rank):
+    import fp4attn_b200.workloads as wl
+    if rank != 0:
+        return
+    w = wl.WORKLOADS[args.workload]
+    cpu = CpuReference(w)
+    cpu.calibrate(max(0.02, 60.0 / max(1, args.steps + args.warmup)))
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, _ = cpu.run(cpu.rows)
+        if i >= args.warmup:
+            rates.append(r)
+    value = statistics.median(rates)
+    cores, kind, sample = cpu.threads, cpu.kind, cpu.sample()
+    line = {
+        "impl": "reference", "metric": "fused FP4 attention TFLOPS", "value": value, "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU, FP4-dequantised Q/K)", "data": "synthetic",
+        "config": {"workload": w.name, "shape": w.describe(), "per_gpu_slices": w.slices},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    import torch
+    import fp4attn_b200 as fa
+    import fp4attn_b200.workloads as wl
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    base = wl.WORKLOADS[args.workload]
+    strong = args.workload == "box_sharded_8k"
+    if strong:  # fixed 512-slice job split over the ranks
+        job = base
+        lo, hi = fa.shard_range(job.slices, world, rank)
+    else:  # weak scaling: each rank runs the workload as its shard of a world-times larger batch
+        job = wl.Workload(base.name, base.batch * world, base.heads, base.seq_q, base.seq_k, base.head_dim,
+                          base.std, base.outlier_frac, base.outlier_mult, base.out_dtype)
+        lo, hi = rank * base.slices, (rank + 1) * base.slices
+    n = hi - lo
+    Q, K, V = wl.make_inputs(job, args.seed, slices=(lo, hi), device=dev)
+    Q, K, V = Q[None], K[None], V[None]  # [1, n, seq, d]: batch x head slices flattened
+    odt = torch.float16 if base.out_dtype == "float16" else torch.float32
+    out = torch.empty((1, n, base.seq_q, base.head_dim), dtype=odt, device=dev)
+    ws = torch.empty(fa.workspace_size(1, n, base.seq_q, base.seq_k, base.head_dim), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    shard = wl.Workload(base.name, 1, n, base.seq_q, base.seq_k, base.head_dim)
+    flops_rank = shard.flops()
+
+    def step(ev_a=None, ev_b=None):
+        fa.prepare(Q, K, V, ws)
+        if ev_a is not None:
+            ev_a.record(stream)
+        fa.attend(V, out, ws, fa.F16, 1, n, base.seq_q, base.seq_k, base.head_dim)
+        if ev_b is not None:
+            ev_b.record(stream)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if fa.status_query() != fa.OK:
+        raise SystemExit("warm-up reported a device timeout")
+
+    props = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local))
+    sampler.start()
+    time.sleep(0.5)
+    # per-step events around the attention kernel alone (the dominant kernel)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(*kev[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t_wall1 = time.time()
+    time.sleep(0.3)
+    sampler.stop()
+    status = fa.status_query()
+    ms_total = e0.elapsed_time(e1)
+    kern_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+
+    # end to end through the public API with host buffers: H2D of Q, K, V from
+    # pinned memory, prepare + attend, D2H of the output, every step
+    hQ, hK, hV = (x.cpu().pin_memory() for x in (Q, K, V))
+    hO = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+
+    def e2e_step():
+        dQ.copy_(hQ, non_blocking=True)
+        dK.copy_(hK, non_blocking=True)
+        dV.copy_(hV, non_blocking=True)
+        fa.fused_fp4_attention_into(dQ, dK, dV, out, ws)
+        hO.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    x1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = x0.elapsed_time(x1) / args.e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in (hQ, hK, hV))
+    d2h = hO.numel() * hO.element_size()
+
+    times = torch.tensor([ms_total, kern_ms, e2e_ms, float(status)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms_total, kern_ms, e2e_ms, status_max = times.tolist()
+    ms_step = ms_total / args.steps
+    total_flops = flops_rank * world
+    value = total_flops / (ms_step * 1e-3) / 1e12
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        bf16, hbm, peak_src = measured_peaks()
+        w_shard = wl.Workload(base.name, 1, n, base.seq_q, base.seq_k, base.head_dim)
+        peak = mixed_roofline(w_shard, bf16)
+        achieved = flops_rank / (kern_ms * 1e-3) / 1e12
+        traffic = profile_traffic(args.workload)
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            ref = CpuReference(base)
+            ref.calibrate(10.0)
+            r, _ = ref.run(ref.rows)
+            cpu = {"value": r, "unit": "TFLOPS", "cores": ref.threads, "kind": ref.kind, "sample": ref.sample()}
+        in_bytes = sum(t.numel() * t.element_size() for t in (Q, K, V))
+        line = {
+            "metric": "fused FP4 attention TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "e2m1 (QK^T) + f16 (PV)",
+            "data": "synthetic (seeded N(0,1) FP16 on device)",
+            "config": {"workload": base.name, "shape": base.describe(), "slices_per_gpu": n,
+                       "job_slices": job.slices, "parallelism": f"slice-shard x{world}",
+                       "l2": f"inputs {in_bytes / 2**20:.0f} MiB > 126 MiB L2; no flush"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_basis": f"mixed: QK^T at 4x and PV at 1x the {peak_src} bf16 dense "
+                                       f"{bf16:g} TFLOP/s",
+                         "kernel": "fp4_attention_fwd_kernel", "kernel_ms": kern_ms},
+            "frac_of_mixed_roofline_step": value / world / peak,
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms},
+            "gpu_launches": 3 * args.steps,
+            "clocks": sampler.summary(t_wall0, t_wall1),
+            "device_status": int(status_max),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -18,7 +18,7 @@ import pathlib
 __all__ = [
     "BLOCK_ELEMENT", "BQ", "Fp4AttnError", "lib", "lib_path", "quantize", "workspace_size",
     "fused_fp4_attention", "fused_fp4_attention_into", "debug_scores", "status_query",
-    "selftest_timeout", "supported_head_dims", "SCALE_REFERENCE", "SCALE_OCP",
+    "selftest_timeout", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
 ]
 
 BLOCK_ELEMENT = 32  # common.h:15
@@ -63,6 +63,10 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_workspace_size.restype = sz
     L.fp4attn_forward.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, vp, sz, vp]
     L.fp4attn_forward.restype = i32
+    L.fp4attn_prepare.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]
+    L.fp4attn_prepare.restype = i32
+    L.fp4attn_attend.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, vp, sz, vp]
+    L.fp4attn_attend.restype = i32
     L.fp4attn_debug_scores.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]
     L.fp4attn_debug_scores.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
@@ -174,6 +178,35 @@ def fused_fp4_attention_into(Q, K, V, out, workspace, softmax_scale=None, scale_
                                _stream_ptr(stream))
     _check(rc, "fp4attn_forward")
     return out
+
+
+def prepare(Q, K, V, workspace, scale_mode="reference", stream=None):
+    """Quantise Q and K (and stage V) into `workspace` (fp4attn_prepare)."""
+    B, H, Sq, Sk, D = _check_qkv(Q, K, V)
+    rc = lib().fp4attn_prepare(Q.data_ptr(), K.data_ptr(), V.data_ptr(), _dtype_code(Q), B, H, Sq, Sk, D,
+                               _scale_mode(scale_mode), workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+    _check(rc, "fp4attn_prepare")
+
+
+def attend(V, out, workspace, in_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale=None, stream=None):
+    """The attention kernel on a prepared workspace (fp4attn_attend)."""
+    rc = lib().fp4attn_attend(V.data_ptr(), out.data_ptr(), in_dtype, _dtype_code(out), batch, heads, seq_q, seq_k,
+                              head_dim, float(softmax_scale or 0.0), workspace.data_ptr(), workspace.numel(),
+                              _stream_ptr(stream))
+    _check(rc, "fp4attn_attend")
+    return out
+
+
+def shard_range(n_slices: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous (batch x head) slice range [lo, hi) of `rank` out of
+    `world` GPUs.  Slices are independent, and in [batch, heads, seq,
+    head_dim] layout a slice range is one contiguous byte range of Q, K, V and
+    Out, so a shard needs no data from any other GPU."""
+    if world < 1 or not 0 <= rank < world or n_slices < 0:
+        raise ValueError("bad shard request")
+    base, extra = divmod(n_slices, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
 
 
 def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode="reference", stream=None):

@@ -243,64 +243,79 @@ int check_problem(const void* Q, const void* K, const void* V, const void* Out, 
     return FP4ATTN_OK;
 }
 
-// Quantise Q and K into the workspace and build the three tensor maps.
-int prepare(const void* Q, const void* K, const void* V, int in_dtype, int64_t slices, int sq, int sk, int d,
-            int scale_mode, uint8_t* ws, const Workspace& w, bool need_v, CUtensorMap* tq, CUtensorMap* tk,
-            CUtensorMap* tv, cudaStream_t st)
+struct Problem {
+    int64_t slices;
+    int sq, sk, d;
+    Workspace w;
+};
+
+int check_workspace(const Problem& p, const void* workspace, size_t ws_bytes)
 {
-    const int dp = padded_dim(d), bn = block_n_for(d);
+    if (!workspace || ws_bytes < p.w.total)
+        return fail(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", p.w.total, workspace ? ws_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
+    return FP4ATTN_OK;
+}
+
+int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int batch, int heads, int sq, int sk, int d,
+               int scale_mode, void* workspace, size_t ws_bytes, void* stream, bool need_v)
+{
+    int rc = check_problem(Q, K, V, Q, in_dtype, FP4ATTN_F32, batch, heads, sq, sk, d, scale_mode, need_v);
+    if (rc) return rc;
+    if ((rc = device_ready())) return rc;
+    Problem p{static_cast<int64_t>(batch) * heads, sq, sk, d, {}};
+    p.w = plan_workspace(p.slices, sq, sk, d, need_v ? in_dtype : FP4ATTN_F16);
+    if ((rc = check_workspace(p, workspace, ws_bytes))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const int bn = block_n_for(d);
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
-    int rc;
     if (in_dtype == FP4ATTN_F16) {
-        if ((rc = launch_quant_tiles<__half>(Q, ws + w.q_codes, ws + w.q_sf, slices, sq, d, 128, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<__half>(K, ws + w.k_codes, ws + w.k_sf, slices, sk, d, bn, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<__half>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<__half>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, ocp, st))) return rc;
     } else {
-        if ((rc = launch_quant_tiles<float>(Q, ws + w.q_codes, ws + w.q_sf, slices, sq, d, 128, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<float>(K, ws + w.k_codes, ws + w.k_sf, slices, sk, d, bn, ocp, st))) return rc;
-    }
-    const int cw = dp / 2 == 96 ? 32 : dp / 2;
-    if ((rc = make_map_3d(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.q_codes, dp / 2, sq, slices, cw, 128,
-                          swizzle_for(cw))))
-        return rc;
-    if ((rc = make_map_3d(tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, dp / 2, sk, slices, cw, bn,
-                          swizzle_for(cw))))
-        return rc;
-    *tv = *tk;
-    if (need_v) {
-        const void* v16 = V;
-        if (in_dtype == FP4ATTN_F32) {
-            const int64_t n4 = slices * static_cast<int64_t>(sk) * d / 4;
+        if ((rc = launch_quant_tiles<float>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<float>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, ocp, st))) return rc;
+        if (need_v) {
+            const int64_t n4 = p.slices * static_cast<int64_t>(sk) * d / 4;
             fp4attn::f32_to_f16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4*>(V),
-                                                                     reinterpret_cast<uint2*>(ws + w.v16), n4);
+                                                                     reinterpret_cast<uint2*>(ws + p.w.v16), n4);
             FP4_CUDA(cudaGetLastError());
-            v16 = ws + w.v16;
         }
-        const int vcw = d == 32 ? 64 : 128;
-        if ((rc = make_map_3d(tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v16, d, sk, slices, vcw / 2, bn,
-                              swizzle_for(vcw))))
-            return rc;
     }
     return FP4ATTN_OK;
 }
 
-int run(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads,
-        int sq, int sk, int d, float softmax_scale, int scale_mode, void* workspace, size_t ws_bytes, void* stream,
-        bool scores)
+int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int sq, int sk, int d,
+              float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores)
 {
-    g_last_error.clear();
-    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, sq, sk, d, scale_mode, !scores);
+    const void* dummy = workspace;
+    int rc = check_problem(dummy, dummy, V, Out, in_dtype, out_dtype, batch, heads, sq, sk, d, FP4ATTN_SCALE_REFERENCE,
+                           !scores);
     if (rc) return rc;
     if ((rc = device_ready())) return rc;
-    const int64_t slices = static_cast<int64_t>(batch) * heads;
-    const Workspace w = plan_workspace(slices, sq, sk, d, scores ? FP4ATTN_F16 : in_dtype);
-    if (!workspace || ws_bytes < w.total)
-        return fail(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w.total, workspace ? ws_bytes : 0);
-    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
+    Problem p{static_cast<int64_t>(batch) * heads, sq, sk, d, {}};
+    p.w = plan_workspace(p.slices, sq, sk, d, scores ? FP4ATTN_F16 : in_dtype);
+    if ((rc = check_workspace(p, workspace, ws_bytes))) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    const int dp = padded_dim(d), bn = block_n_for(d);
+    const int cw = dp / 2 == 96 ? 32 : dp / 2;
     CUtensorMap tq, tk, tv;
-    if ((rc = prepare(Q, K, V, in_dtype, slices, sq, sk, d, scale_mode, ws, w, !scores, &tq, &tk, &tv, st))) return rc;
-    const int bn = block_n_for(d);
+    if ((rc = make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + p.w.q_codes, dp / 2, sq, p.slices, cw, 128,
+                          swizzle_for(cw))))
+        return rc;
+    if ((rc = make_map_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + p.w.k_codes, dp / 2, sk, p.slices, cw, bn,
+                          swizzle_for(cw))))
+        return rc;
+    tv = tk;
+    if (!scores) {
+        const void* v16 = in_dtype == FP4ATTN_F32 ? static_cast<const void*>(ws + p.w.v16) : V;
+        const int vcw = d == 32 ? 64 : 128;
+        if ((rc = make_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v16, d, sk, p.slices, vcw / 2, bn,
+                              swizzle_for(vcw))))
+            return rc;
+    }
     fp4attn::FwdArgs a;
     a.seq_q = sq;
     a.seq_k = sk;
@@ -309,11 +324,11 @@ int run(const void* Q, const void* K, const void* V, void* Out, int in_dtype, in
     const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(d));
     a.scale_log2 = scale * 1.4426950408889634f;
     a.out = Out;
-    a.q_sf = ws + w.q_sf;
-    a.k_sf = ws + w.k_sf;
+    a.q_sf = ws + p.w.q_sf;
+    a.k_sf = ws + p.w.k_sf;
     a.timeout_ns = wait_timeout_ns();
-    if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, slices, st);
-    return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, slices, st);
+    if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
+    return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, p.slices, st);
 }
 
 }  // namespace
@@ -354,12 +369,34 @@ size_t fp4attn_workspace_size(int batch, int heads, int seq_q, int seq_k, int he
     return plan_workspace(static_cast<int64_t>(batch) * heads, seq_q, seq_k, head_dim, in_dtype).total;
 }
 
+int fp4attn_prepare(const void* Q, const void* K, const void* V, int in_dtype, int batch, int heads, int seq_q,
+                    int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    return do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace, workspace_bytes,
+                      stream, true);
+}
+
+int fp4attn_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q, int seq_k,
+                   int head_dim, float softmax_scale, const void* workspace, size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false);
+}
+
 int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype, int batch,
                     int heads, int seq_q, int seq_k, int head_dim, float softmax_scale, int scale_mode,
                     void* workspace, size_t workspace_bytes, void* stream)
 {
-    return run(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, scale_mode,
-               workspace, workspace_bytes, stream, false);
+    g_last_error.clear();
+    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, true);
+    if (rc) return rc;
+    if ((rc = do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
+                         workspace_bytes, stream, true)))
+        return rc;
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false);
 }
 
 int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, int batch, int heads, int seq_q,
@@ -367,8 +404,14 @@ int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, i
                          void* stream)
 {
     g_last_error.clear();
-    return run(Q, K, nullptr, S, in_dtype, FP4ATTN_F32, batch, heads, seq_q, seq_k, head_dim, 1.0f, scale_mode,
-               workspace, workspace_bytes, stream, true);
+    int rc = check_problem(Q, K, nullptr, S, in_dtype, FP4ATTN_F32, batch, heads, seq_q, seq_k, head_dim, scale_mode,
+                           false);
+    if (rc) return rc;
+    if ((rc = do_prepare(Q, K, nullptr, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
+                         workspace_bytes, stream, false)))
+        return rc;
+    return do_attend(nullptr, S, in_dtype, FP4ATTN_F32, batch, heads, seq_q, seq_k, head_dim, 1.0f, workspace,
+                     workspace_bytes, stream, true);
 }
 
 int fp4attn_status_query(void* stream)

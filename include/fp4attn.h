@@ -102,6 +102,20 @@ int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int 
                     int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
                     int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The two halves of fp4attn_forward, for callers that quantise once and
+ * attend many times (e.g. a fixed K/V) or time the attention kernel alone.
+ * fp4attn_prepare quantises Q and K into `workspace` (and, for FP32 input,
+ * stores an FP16 copy of V there).  Replaces: the quantisation prologue of the
+ * reference kernel (common.h:108-124 for Q, :146-169 for K and V). */
+int fp4attn_prepare(const void* Q, const void* K, const void* V, int in_dtype, int batch, int heads, int seq_q,
+                    int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Runs the attention kernel on a workspace filled by fp4attn_prepare with the
+ * same shape and in_dtype.  V is read directly when in_dtype is FP16.
+ * Replaces: the main loop of the reference kernel (common.h:140-327). */
+int fp4attn_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q, int seq_k,
+                   int head_dim, float softmax_scale, const void* workspace, size_t workspace_bytes, void* stream);
+
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
  * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
  * power-of-two scales are exact, S is checkable bit for bit.

@@ -1,0 +1,104 @@
+"""The C ABI boundary without a GPU: the library loads, exports every entry
+point include/fp4attn.h declares, and rejects bad arguments before touching
+the device (the reference returns no errors at all; common.h:68-77)."""
+import ctypes
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fp4attn.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fp4attn_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for want in ("fp4attn_quantize", "fp4attn_forward", "fp4attn_workspace_size", "fp4attn_debug_scores",
+                 "fp4attn_status_query", "fp4attn_error_string", "fp4attn_last_error"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol(fa):
+    L = fa.lib()
+    missing = [n for n in declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_nm_lists_symbols_as_c_linkage(fa):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(fa.lib_path())], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r" T (fp4attn_\w+)", out))
+    assert set(declared_functions()) <= exported
+
+
+@pytest.mark.parametrize("compiler,lang", [("gcc", "c"), ("g++", "c++")])
+def test_header_compiles_as_c_and_cpp(tmp_path, compiler, lang):
+    src = tmp_path / ("t.c" if lang == "c" else "t.cpp")
+    src.write_text('#include "fp4attn.h"\nint main(void){ return FP4ATTN_OK + FP4ATTN_BLOCK_ELEMENT - 32; }\n')
+    subprocess.run([compiler, "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src), "-o", str(tmp_path / "t")],
+                   check=True)
+
+
+def test_error_strings(fa):
+    L = fa.lib()
+    for code in range(6):
+        assert L.fp4attn_error_string(code)
+    assert L.fp4attn_error_string(99) == b"unknown status"
+
+
+def test_supported_head_dims(fa):
+    assert fa.supported_head_dims() == [32, 64, 96, 128, 160, 256]
+
+
+def test_workspace_size_host_only(fa):
+    ws = fa.workspace_size(2, 32, 4096, 4096, 128)
+    # Q and K codes (64 B per row) + scale tiles (512 B per 128 rows)
+    assert ws == 2 * 64 * 4096 * 64 + 2 * 64 * 32 * 512
+    assert fa.workspace_size(1, 1, 1, 1, 100) == 0
+    assert fa.workspace_size(0, 1, 1, 1, 128) == 0
+    assert fa.workspace_size(1, 1, 64, 128, 128, fa.F32) > fa.workspace_size(1, 1, 64, 128, 128, fa.F16)
+
+
+def _fwd(fa, **kw):
+    args = dict(Q=16, K=16, V=16, O=16, ind=fa.F16, outd=fa.F32, B=1, H=1, sq=64, sk=128, d=128, scale=0.0,
+                mode=0, ws=256, wsb=1 << 30, stream=None)
+    args.update(kw)
+    return fa.lib().fp4attn_forward(args["Q"], args["K"], args["V"], args["O"], args["ind"], args["outd"],
+                                    args["B"], args["H"], args["sq"], args["sk"], args["d"], args["scale"],
+                                    args["mode"], args["ws"], args["wsb"], args["stream"])
+
+
+def test_forward_rejects_bad_arguments_before_the_device(fa):
+    assert _fwd(fa, Q=None) == fa.EINVAL
+    assert b"null" in fa.lib().fp4attn_last_error()
+    assert _fwd(fa, Q=17) == fa.EINVAL          # misaligned
+    assert _fwd(fa, ind=7) == fa.EINVAL
+    assert _fwd(fa, outd=7) == fa.EINVAL
+    assert _fwd(fa, mode=3) == fa.EINVAL
+    assert _fwd(fa, sq=0) == fa.EINVAL
+    assert _fwd(fa, sk=0) == fa.EINVAL
+    assert _fwd(fa, B=-1) == fa.EINVAL
+    assert _fwd(fa, d=100) == fa.EUNSUPPORTED
+    assert _fwd(fa, d=512) == fa.EUNSUPPORTED
+    assert _fwd(fa, B=300, H=300) == fa.EINVAL  # batch*heads > 65535
+
+
+def test_quantize_rejects_bad_arguments(fa):
+    L = fa.lib()
+    assert L.fp4attn_quantize(None, fa.F16, 1, 128, 16, 16, 0, 0, None) == fa.EINVAL
+    assert L.fp4attn_quantize(16, fa.F16, 1, 100, 16, 16, 0, 0, None) == fa.EINVAL
+    assert L.fp4attn_quantize(16, 5, 1, 128, 16, 16, 0, 0, None) == fa.EINVAL
+    assert L.fp4attn_quantize(16, fa.F16, 1, 128, 16, 16, 9, 0, None) == fa.EINVAL
+    assert L.fp4attn_quantize(16, fa.F16, 1, 128, 16, 16, 0, 4, None) == fa.EINVAL
+
+
+def test_python_wrapper_errors_carry_detail(fa):
+    err = fa.Fp4AttnError(fa.EINVAL, "fp4attn_forward", "null tensor pointer")
+    assert "invalid argument" in str(err) and "null tensor pointer" in str(err)

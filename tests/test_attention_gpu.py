@@ -1,0 +1,204 @@
+"""GPU FP4 attention vs the oracle (the reference's cpu_attention on the
+reference-quantised Q and K, tests/test_attention.cu:33-54) and vs golden
+vectors made by the reference's own code.
+
+Tolerance (written here, from the spec of the path): cosine >= 0.9999
+(computed in double) and max |out - oracle| <= 2e-2.  The GPU rounds P and V
+to FP16 for the tensor cores; the oracle keeps them in FP32."""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAXABS = 2e-2
+
+
+def run_fwd(fa, Q, K, V, in_dtype=torch.float16, out_dtype=torch.float32, mode="reference", scale=None):
+    """Q/K/V: [slices, seq, d] numpy float32; runs as [1, slices, seq, d]."""
+    t = [torch.from_numpy(np.ascontiguousarray(a)).to(in_dtype).cuda()[None] for a in (Q, K, V)]
+    out = fa.fused_fp4_attention(*t, out_dtype=out_dtype, scale_mode=mode, softmax_scale=scale)
+    assert fa.status_query() == fa.OK
+    return out[0].float().cpu().numpy()
+
+
+def assert_close(got, want, cos_min=COS_MIN, maxabs=MAXABS):
+    assert np.isfinite(got).all()
+    cos = oracle.cosine(got, want)
+    err = float(np.abs(got - want).max())
+    assert cos >= cos_min and err <= maxabs, (cos, err)
+
+
+@pytest.mark.parametrize("name", list(gi.ATTN_CASES))
+def test_golden_cases(fa, cuda, golden_dir, name):
+    g = np.load(golden_dir / f"attn_{name}.npz")
+    Q, K, V = gi.attn_inputs(name)
+    out = run_fwd(fa, Q, K, V)
+    assert_close(out[g["slices"]], g["out"])
+    assert_close(out, oracle.fp4_attention(Q, K, V))
+
+
+@pytest.mark.parametrize("name", list(gi.DISCRETE_CASES))
+def test_reference_test_fixtures(fa, cuda, golden_dir, name):
+    """The reference's test_attention.cu inputs and shapes, compared with its
+    unquantised CPU reference as that test does (there at cosine >= 0.99)."""
+    d, sk, B, H = gi.DISCRETE_CASES[name]
+    Q, K, V = gi.discrete_inputs(d, sk, B, H)
+    g = np.load(golden_dir / f"discrete_{name}.npz")["out"]
+    out = run_fwd(fa, Q, K, V, in_dtype=torch.float32)
+    assert_close(out, g)
+
+
+@pytest.mark.parametrize("in_dtype,out_dtype", [(torch.float32, torch.float32), (torch.float16, torch.float16),
+                                                (torch.float32, torch.float16), (torch.float16, torch.float32)])
+def test_dtypes(fa, cuda, in_dtype, out_dtype):
+    Q, K, V = gi.attn_inputs("cpu_check")
+    out = run_fwd(fa, Q, K, V, in_dtype, out_dtype)
+    assert_close(out, oracle.fp4_attention(Q, K, V))
+
+
+def test_ocp_scale_mode(fa, cuda):
+    Q, K, V = gi.attn_inputs("short_head_long_key")
+    out = run_fwd(fa, Q, K, V, mode="ocp")
+    assert_close(out, oracle.fp4_attention(Q, K, V, scale_mode=1))
+
+
+def test_explicit_softmax_scale(fa, cuda):
+    Q, K, V = gi.attn_inputs("d32")
+    out = run_fwd(fa, Q, K, V, scale=0.05)
+    assert_close(out, oracle.fp4_attention(Q, K, V, scale=0.05))
+
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 160, 256])
+@pytest.mark.parametrize("sq,sk", [(1, 1), (64, 65), (129, 127), (200, 513)])
+def test_shapes(fa, cuda, d, sq, sk):
+    g = torch.Generator().manual_seed(d * 7 + sq + sk)
+    Q, K, V = [(torch.randn(2, s, d, generator=g)).half().float().numpy() for s in (sq, sk, sk)]
+    out = run_fwd(fa, Q, K, V)
+    assert_close(out, oracle.fp4_attention(Q, K, V))
+
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 160, 256])
+def test_scores_bit_exact(fa, cuda, d):
+    """S = Q K^T of FP4 codes with power-of-two scales is exact in FP32 here,
+    so the tcgen05 block-scaled product must equal the oracle bit for bit
+    (the reference's debug_mma, common.h:331-398, for whole problems)."""
+    g = torch.Generator().manual_seed(d)
+    Q = torch.randn(1, 3, 130, d, generator=g).half()
+    K = torch.randn(1, 3, 200, d, generator=g).half()
+    S = fa.debug_scores(Q.cuda(), K.cuda())
+    assert fa.status_query() == fa.OK
+    S = S.cpu().numpy()
+    for h in range(3):
+        want = oracle.fp4_scores(Q[0, h].float().numpy(), K[0, h].float().numpy())
+        assert np.array_equal(S[0, h], want)
+
+
+def test_zero_inputs_give_mean_of_v(fa, cuda):
+    Q = np.zeros((2, 70, 128), np.float32)
+    K = np.zeros((2, 300, 128), np.float32)
+    V = torch.randn(2, 300, 128, generator=torch.Generator().manual_seed(3)).half().float().numpy()
+    out = run_fwd(fa, Q, K, V)
+    want = np.broadcast_to(V.mean(axis=1, keepdims=True), out.shape)
+    assert_close(out, want)
+
+
+def test_large_outliers(fa, cuda):
+    g = torch.Generator().manual_seed(9)
+    Q, K, V = [torch.randn(4, 256, 128, generator=g) for _ in range(3)]
+    Q[:, :, ::17] *= 300
+    K[:, ::5, 3] *= 200
+    Q, K, V = [x.half().float().numpy() for x in (Q, K, V)]
+    out = run_fwd(fa, Q, K, V)
+    assert_close(out, oracle.fp4_attention(Q, K, V))
+
+
+def test_timeout_path_reports_and_recovers(fa, cuda):
+    """A bounded wait that nothing completes: the kernel records
+    FP4ATTN_ETIMEOUT and returns; the context stays usable."""
+    assert fa.selftest_timeout(2000) == fa.ETIMEOUT
+    assert fa.status_query() == fa.OK  # the query cleared the word
+    Q, K, V = gi.attn_inputs("d32")
+    assert_close(run_fwd(fa, Q, K, V), oracle.fp4_attention(Q, K, V))
+
+
+def test_misaligned_pointer_rejected(fa, cuda):
+    x = torch.zeros(1, 1, 65, 128, dtype=torch.float16, device="cuda")
+    bad = x.view(-1)[1:1 + 64 * 128].view(1, 1, 64, 128)
+    with pytest.raises(fa.Fp4AttnError) as e:
+        fa.fused_fp4_attention(bad, bad, bad)
+    assert e.value.code == fa.EINVAL
+
+
+def test_workspace_too_small(fa, cuda):
+    Q = torch.zeros(1, 1, 64, 128, dtype=torch.float16, device="cuda")
+    out = torch.empty_like(Q)
+    ws = torch.empty(16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(fa.Fp4AttnError) as e:
+        fa.fused_fp4_attention_into(Q, Q, Q, out, ws)
+    assert e.value.code == fa.EWORKSPACE
+
+
+# ------------------------------------------------- full-size workloads
+# At these sizes the full oracle would take minutes, so sampled query rows of
+# sampled slices are checked against the oracle computed for just those rows,
+# and every output is checked for a size-independent property: each output is
+# a convex combination of V rows, so it lies inside V's per-column range.
+def _full_size(fa, name, n_slices_checked=3, rows_per_slice=6, seed=42):
+    import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS[name]
+    Q, K, V = wl.make_inputs(w, seed)
+    odt = torch.float16 if w.out_dtype == "float16" else torch.float32
+    out = fa.fused_fp4_attention(Q[None], K[None], V[None], out_dtype=odt)[0]
+    assert fa.status_query() == fa.OK
+    assert torch.isfinite(out).all()
+    vmin, vmax = V.float().amin(dim=1, keepdim=True), V.float().amax(dim=1, keepdim=True)
+    tol = 1e-2 + 1e-3 * V.float().abs().amax()
+    assert (out.float() >= vmin - tol).all() and (out.float() <= vmax + tol).all()
+    rng = np.random.default_rng(seed)
+    sl = rng.choice(w.slices, size=min(n_slices_checked, w.slices), replace=False)
+    s_of, rows = [], []
+    for s in sl:
+        for r in rng.choice(w.seq_q, size=rows_per_slice, replace=False):
+            s_of.append(int(s)); rows.append(int(r))
+    s_of, rows = np.array(s_of, np.int32), np.array(rows, np.int32)
+    uniq = sorted(set(s_of.tolist()))
+    remap = {s: i for i, s in enumerate(uniq)}
+    Qc = Q[uniq].float().cpu().numpy(); Kc = K[uniq].float().cpu().numpy(); Vc = V[uniq].float().cpu().numpy()
+    want = oracle.fp4_attention_rows(Qc, Kc, Vc, np.array([remap[s] for s in s_of], np.int32), rows)
+    got = out.float()[torch.from_numpy(s_of).long(), torch.from_numpy(rows).long()].cpu().numpy()
+    if odt == torch.float16:
+        want = want.astype(np.float16).astype(np.float32)
+    assert_close(got, want)
+
+
+def test_full_prefill_4k(fa, cuda):
+    _full_size(fa, "prefill_4k")
+
+
+def test_full_odd_d96(fa, cuda):
+    _full_size(fa, "odd_d96")
+
+
+def test_full_odd_d256(fa, cuda):
+    _full_size(fa, "odd_d256")
+
+
+def test_full_box_sharded_8k_one_gpu_shard(fa, cuda):
+    """The 512-slice box-scale workload as one GPU of eight runs it (64 slices)."""
+    import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS["box_sharded_8k"]
+    Q, K, V = wl.make_inputs(w, 7, slices=(448, 512))
+    out = fa.fused_fp4_attention(Q[None], K[None], V[None], out_dtype=torch.float32)[0]
+    assert fa.status_query() == fa.OK
+    assert torch.isfinite(out).all()
+    idx = [0, 63]
+    rows = np.array([5, 8000], np.int32)
+    want = oracle.fp4_attention_rows(Q[idx].float().cpu().numpy(), K[idx].float().cpu().numpy(),
+                                     V[idx].float().cpu().numpy(), np.array([0, 1], np.int32), rows)
+    got = out[torch.tensor(idx), torch.from_numpy(rows).long()].cpu().numpy()
+    assert_close(got, want)
