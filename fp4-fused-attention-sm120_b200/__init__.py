@@ -73,6 +73,8 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_status_query.restype = i32
     L.fp4attn_selftest_timeout.argtypes = [ctypes.c_uint, vp]
     L.fp4attn_selftest_timeout.restype = i32
+    L.fp4attn_selftest_exp2.argtypes = [vp, vp, i64, vp]
+    L.fp4attn_selftest_exp2.restype = i32
     L.fp4attn_error_string.argtypes = [i32]
     L.fp4attn_error_string.restype = ctypes.c_char_p
     L.fp4attn_last_error.argtypes = []
@@ -231,6 +233,17 @@ def debug_scores(Q, K, scale_mode="reference", stream=None):
                                     _scale_mode(scale_mode), ws.data_ptr(), ws.numel(), _stream_ptr(stream))
     _check(rc, "fp4attn_debug_scores")
     return S
+
+
+def selftest_exp2(x, stream=None):
+    """2^x on the device by the softmax's FMA-pipe polynomial (test hook)."""
+    torch = _torch()
+    if x.dtype != torch.float32 or not x.is_cuda or not x.is_contiguous() or x.numel() % 2:
+        raise ValueError("x must be a contiguous float32 CUDA tensor with an even number of elements")
+    y = torch.empty_like(x)
+    _check(lib().fp4attn_selftest_exp2(x.data_ptr(), y.data_ptr(), x.numel(), _stream_ptr(stream)),
+           "fp4attn_selftest_exp2")
+    return y
 
 
 def status_query(stream=None) -> int:

@@ -13,10 +13,13 @@
 //               tcgen05.cp), then O += P_j V_j with tcgen05.mma kind::f16 whose
 //               A operand (P) is read from TMEM.  S is double-buffered in TMEM
 //               so S_{j+1} runs on the tensor cores while S_j is in softmax.
-//   warps 2-5   softmax warpgroup: thread = query row = TMEM lane.  tcgen05.ld
-//               of S_j, online max/sum in FP32 (log2 domain), P_j written back
-//               as FP16 into the S_j columns with tcgen05.st, lazy O rescale
-//               (only when the row max grows by more than 2^8), final O / l.
+//   warps 2-9   two softmax warpgroups; thread = query row = TMEM lane, and
+//               each warpgroup owns half of the S_j columns (and half of O's).
+//               tcgen05.ld of its S_j half, partial row max exchanged with the
+//               partner warp through shared memory, online max/sum in FP32
+//               (log2 domain), P_j written back as FP16 into the S_j columns
+//               with tcgen05.st, lazy O rescale (only when the row max grows by
+//               more than 2^8), final O / l for its half of the columns.
 //
 // TMEM columns (512 allocated): S0 [0,BN), S1 [BN,2BN), O [2BN, 2BN+D),
 // then the Q scale columns and KST stages of K scale columns.
@@ -76,7 +79,9 @@ struct FwdCfg {
     static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
     static constexpr int OFF_V = align1k(OFF_KSF + KST * KSF_BYTES);
     static constexpr int V_STRIDE = align1k(V_BYTES);
-    static constexpr int OFF_BAR = OFF_V + VST * V_STRIDE;
+    static constexpr int OFF_RED = OFF_V + VST * V_STRIDE;   // [2 parity][2 halves][128 rows] f32 row maxima
+    static constexpr int OFF_REDL = OFF_RED + 2 * 2 * 128 * 4; // [2 halves][128 rows] f32 row sums
+    static constexpr int OFF_BAR = OFF_REDL + 2 * 128 * 4;
     static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
 };
@@ -149,8 +154,8 @@ __device__ __forceinline__ void drain_phase(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
-template <int D, int BN, typename OutT, bool kScores>
-__global__ void __launch_bounds__(192, 1)
+template <int D, int BN, typename OutT, bool kScores, int kPoly8 = 3>
+__global__ void __launch_bounds__(320, 1)
     fp4_attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const FwdArgs args)
 {
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&s_full[i], 1);
-            ptx::mbar_init(&p_full[i], 128);
+            ptx::mbar_init(&p_full[i], 256);
         }
         ptx::mbar_init(pv_done, 1);
         ptx::mbar_init(drain_bar, 1);
@@ -323,10 +328,17 @@ __global__ void __launch_bounds__(192, 1)
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------------------ softmax warpgroup
-        const int wq = warp & 3;                  // TMEM lane quarter this warp may access
-        const int row = wq * 32 + lane;           // query row within the tile
+        // ------------------------------------------------------------ softmax warpgroups
+        constexpr int HC = BN / 2;                 // S columns per warpgroup
+        constexpr int HD = D / 2;                  // O columns per warpgroup
+        constexpr int OCH = HD % 32 == 0 ? 32 : 16;  // O column chunk
+        const int half = (warp - 2) / 4;           // which half of the columns
+        const int wq = warp & 3;                   // TMEM lane quarter this warp may access
+        const int row = wq * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t pair_bar = 1 + wq;          // the two warps (one per half) of this lane quarter
+        float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+        float* red_l = reinterpret_cast<float*>(smem + C::OFF_REDL);
         const float c = args.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -334,18 +346,19 @@ __global__ void __launch_bounds__(192, 1)
             if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
             ptx::tc_fence_after();
             const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN;
-            uint32_t sr[BN / 32][32];
+            uint32_t sr[HC / 32 > 0 ? HC / 32 : 1][32];
 #pragma unroll
-            for (int t = 0; t < BN / 32; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
+            for (int t = 0; t < HC / 32; t++) ptx::tmem_ld32(s_tm + half * HC + 32 * t, sr[t]);
             ptx::tc_wait_ld();
-            const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+            const int valid = args.seq_k - j * BN - half * HC;  // keys of this half-tile that exist
             if (kScores) {
                 const int grow = q0 + row;
                 if (grow < args.seq_q) {
                     float* dst = reinterpret_cast<float*>(args.out) +
-                                 (static_cast<size_t>(slice) * args.seq_q + grow) * args.seq_k + static_cast<size_t>(j) * BN;
+                                 (static_cast<size_t>(slice) * args.seq_q + grow) * args.seq_k +
+                                 static_cast<size_t>(j) * BN + half * HC;
 #pragma unroll
-                    for (int t = 0; t < BN / 32; t++)
+                    for (int t = 0; t < HC / 32; t++)
 #pragma unroll
                         for (int i = 0; i < 32; i++)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
@@ -354,16 +367,35 @@ __global__ void __launch_bounds__(192, 1)
                 ptx::mbar_arrive(&p_full[j & 1]);
                 continue;
             }
-            float mx = -INFINITY;
+            if (valid < HC) {
 #pragma unroll
-            for (int t = 0; t < BN / 32; t++)
+                for (int t = 0; t < HC / 32; t++)
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    float v = __uint_as_float(sr[t][i]);
-                    if (32 * t + i >= valid) v = -INFINITY;
-                    sr[t][i] = __float_as_uint(v);
-                    mx = fmaxf(mx, v);
+                    for (int i = 0; i < 32; i++)
+                        if (32 * t + i >= valid) sr[t][i] = __float_as_uint(-INFINITY);
+            }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int t = 0; t < HC / 32; t++)
+#pragma unroll
+                for (int i = 0; i < 32; i += 8) {
+                    mx4[(i >> 3) & 3] = ptx::fmax3(mx4[(i >> 3) & 3], __uint_as_float(sr[t][i]), __uint_as_float(sr[t][i + 1]));
+                    mx4[((i >> 3) + 1) & 3] =
+                        ptx::fmax3(mx4[((i >> 3) + 1) & 3], __uint_as_float(sr[t][i + 2]), __uint_as_float(sr[t][i + 3]));
+                    mx4[((i >> 3) + 2) & 3] =
+                        ptx::fmax3(mx4[((i >> 3) + 2) & 3], __uint_as_float(sr[t][i + 4]), __uint_as_float(sr[t][i + 5]));
+                    mx4[((i >> 3) + 3) & 3] =
+                        ptx::fmax3(mx4[((i >> 3) + 3) & 3], __uint_as_float(sr[t][i + 6]), __uint_as_float(sr[t][i + 7]));
                 }
+            float mx = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+            // Exchange the partial row max with the partner warp.  The barrier
+            // also orders this warp's S loads before the partner's P stores,
+            // which overwrite S columns this half read.
+            red[((j & 1) * 2 + half) * 128 + row] = mx;
+            ptx::tc_fence_before();
+            ptx::named_bar_sync(pair_bar, 64);
+            ptx::tc_fence_after();
+            mx = fmaxf(mx, red[((j & 1) * 2 + (1 - half)) * 128 + row]);
             const float m_new = fmaxf(m, mx * c);
             float alpha = 1.f;
             bool rescale = false;
@@ -374,21 +406,29 @@ __global__ void __launch_bounds__(192, 1)
                 m = m_new;
                 rescale = true;
             }
-            float sum = 0.f;
-            uint32_t pk[BN / 64][32];
+            float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            uint32_t pk[HC / 2];
+            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
 #pragma unroll
-            for (int t = 0; t < BN / 32; t++)
+            for (int t = 0; t < HC / 32; t++)
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    const float p0 = ptx::ex2_approx(fmaf(__uint_as_float(sr[t][i]), c, -m));
-                    const float p1 = ptx::ex2_approx(fmaf(__uint_as_float(sr[t][i + 1]), c, -m));
-                    sum += p0 + p1;
-                    __half2 h = __floats2half2_rn(p0, p1);
-                    pk[t / 2][(t % 2) * 16 + i / 2] = *reinterpret_cast<uint32_t*>(&h);
+                    const float2 x = ptx::ffma2(make_float2(__uint_as_float(sr[t][i]), __uint_as_float(sr[t][i + 1])), c2, nm2);
+                    // kPoly8 of every 8 column pairs take 2^x on the FMA pipe, the
+                    // rest on MUFU, so both pipes share the exponentials.
+                    const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
+                                                              : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                    sum2[(i >> 1) & 1] = ptx::fadd2(sum2[(i >> 1) & 1], p);
+                    pk[t * 16 + i / 2] = ptx::pack_half2(p.x, p.y);
                 }
-            l = l * alpha + sum;
-#pragma unroll
-            for (int t = 0; t < BN / 64; t++) ptx::tmem_st32(s_tm + 32 * t, pk[t]);
+            l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
+            // P (FP16 pairs) into the first BN/2 columns of this S buffer.
+            const uint32_t p_tm = s_tm + half * (HC / 2);
+            if constexpr (HC / 2 == 32) {
+                ptx::tmem_st32(p_tm, *reinterpret_cast<uint32_t(*)[32]>(pk));
+            } else {
+                ptx::tmem_st16(p_tm, *reinterpret_cast<uint32_t(*)[16]>(pk));
+            }
             ptx::tc_wait_st();
             if (j > 0) {
                 // O += P_{j-1} V_{j-1} must have landed before O is rescaled (and
@@ -397,14 +437,23 @@ __global__ void __launch_bounds__(192, 1)
                 ptx::tc_fence_after();
                 if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-                    for (int t = 0; t < D / 32; t++) {
-                        uint32_t o[32];
-                        const uint32_t o_tm = tmem + lane_off + C::O_COL + 32 * t;
-                        ptx::tmem_ld32(o_tm, o);
-                        ptx::tc_wait_ld();
+                    for (int t = 0; t < HD / OCH; t++) {
+                        const uint32_t o_tm = tmem + lane_off + C::O_COL + half * HD + OCH * t;
+                        if constexpr (OCH == 32) {
+                            uint32_t o[32];
+                            ptx::tmem_ld32(o_tm, o);
+                            ptx::tc_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        ptx::tmem_st32(o_tm, o);
+                            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                            ptx::tmem_st32(o_tm, o);
+                        } else {
+                            uint32_t o[16];
+                            ptx::tmem_ld16(o_tm, o);
+                            ptx::tc_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                            ptx::tmem_st16(o_tm, o);
+                        }
                     }
                     ptx::tc_wait_st();
                 }
@@ -413,28 +462,36 @@ __global__ void __launch_bounds__(192, 1)
             ptx::mbar_arrive(&p_full[j & 1]);
         }
         if (!kScores && ok) {
+            red_l[half * 128 + row] = l;
+            ptx::named_bar_sync(pair_bar, 64);
+            const float l_tot = l + red_l[(1 - half) * 128 + row];
             if (wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone)) {
                 ptx::tc_fence_after();
-                const float inv_l = 1.0f / l;
+                const float inv_l = 1.0f / l_tot;
                 const int grow = q0 + row;
-                OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D;
+                OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D +
+                            half * HD;
 #pragma unroll 1
-                for (int t = 0; t < D / 32; t++) {
-                    uint32_t o[32];
-                    ptx::tmem_ld32(tmem + lane_off + C::O_COL + 32 * t, o);
+                for (int t = 0; t < HD / OCH; t++) {
+                    uint32_t o[OCH];
+                    if constexpr (OCH == 32) {
+                        ptx::tmem_ld32(tmem + lane_off + C::O_COL + half * HD + OCH * t, o);
+                    } else {
+                        ptx::tmem_ld16(tmem + lane_off + C::O_COL + half * HD + OCH * t, o);
+                    }
                     ptx::tc_wait_ld();
                     if (grow < args.seq_q) {
                         if constexpr (sizeof(OutT) == 4) {
 #pragma unroll
-                            for (int i = 0; i < 32; i += 4) {
+                            for (int i = 0; i < OCH; i += 4) {
                                 float4 v = make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
                                                        __uint_as_float(o[i + 2]) * inv_l,
                                                        __uint_as_float(o[i + 3]) * inv_l);
-                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + 32 * t + i) = v;
+                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + OCH * t + i) = v;
                             }
                         } else {
 #pragma unroll
-                            for (int i = 0; i < 32; i += 8) {
+                            for (int i = 0; i < OCH; i += 8) {
                                 uint32_t w[4];
 #pragma unroll
                                 for (int k = 0; k < 4; k++) {
@@ -442,7 +499,7 @@ __global__ void __launch_bounds__(192, 1)
                                                                   __uint_as_float(o[i + 2 * k + 1]) * inv_l);
                                     w[k] = *reinterpret_cast<uint32_t*>(&h);
                                 }
-                                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + 32 * t + i) =
+                                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + OCH * t + i) =
                                     make_uint4(w[0], w[1], w[2], w[3]);
                             }
                         }
@@ -458,6 +515,15 @@ __global__ void __launch_bounds__(192, 1)
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, 512);
     }
+}
+
+// Evaluates the FMA-pipe exponential used by the softmax on n inputs (pairs),
+// so tests can hold it to its error bound.
+__global__ void exp2_poly_selftest_kernel(const float2* __restrict__ x, float2* __restrict__ y, int64_t n2)
+{
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n2;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = ptx::exp2_poly3(x[i]);
 }
 
 // A CTA that waits on an mbarrier nothing completes, so that its bounded wait

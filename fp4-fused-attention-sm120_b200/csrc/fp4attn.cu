@@ -178,24 +178,50 @@ int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slice
     a.ntiles = (seq + tile_rows - 1) / tile_rows;
     a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
     a.ocp_mode = ocp;
-    const int64_t work = slices * static_cast<int64_t>(a.ntiles) * tile_rows * (a.padded_dim / 32);
+    const int64_t work = slices * static_cast<int64_t>(a.ntiles) * tile_rows * (a.padded_dim / 32) * 4;
     fp4attn::quantize_tiles_kernel<InT><<<grid_for(work), 256, 0, st>>>(static_cast<const InT*>(x), codes, sf, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
+}
+
+template <int D, int BN, typename OutT, bool kScores, int kPoly8>
+int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
+                    int64_t slices, cudaStream_t st)
+{
+    using C = fp4attn::FwdCfg<D, BN>;
+    auto kern = fp4attn::fp4_attention_fwd_kernel<D, BN, OutT, kScores, kPoly8>;
+    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
+    dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
+    kern<<<grid, 320, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+// Share of the exponentials computed by the FMA-pipe polynomial, in eighths
+// (FP4ATTN_POLY8 overrides it for the FP16-output D=128 kernel, for tuning).
+int poly8_setting()
+{
+    static int v = [] {
+        const char* s = getenv("FP4ATTN_POLY8");
+        return s ? atoi(s) : -1;
+    }();
+    return v;
 }
 
 template <int D, int BN, typename OutT, bool kScores>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                int64_t slices, cudaStream_t st)
 {
-    using C = fp4attn::FwdCfg<D, BN>;
-    auto kern = fp4attn::fp4_attention_fwd_kernel<D, BN, OutT, kScores>;
-    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
-    dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
-    kern<<<grid, 192, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
-    FP4_CUDA(cudaGetLastError());
-    return FP4ATTN_OK;
+    if constexpr (D == 128 && !kScores && sizeof(OutT) == 2) {
+        switch (poly8_setting()) {
+            case 0: return launch_fwd_poly<D, BN, OutT, kScores, 0>(tq, tk, tv, a, slices, st);
+            case 2: return launch_fwd_poly<D, BN, OutT, kScores, 2>(tq, tk, tv, a, slices, st);
+            case 4: return launch_fwd_poly<D, BN, OutT, kScores, 4>(tq, tk, tv, a, slices, st);
+            default: break;
+        }
+    }
+    return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
 }
 
 template <int D, bool kScores>
@@ -339,6 +365,7 @@ int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8
                      int scale_mode, int layout, void* stream)
 {
     g_last_error.clear();
+    if (rows == 0 && head_dim >= 32 && head_dim % 32 == 0) return FP4ATTN_OK;
     if (!x || !codes || !scales) return fail(FP4ATTN_EINVAL, "null pointer");
     if (!aligned16(x) || !aligned16(codes)) return fail(FP4ATTN_EINVAL, "x and codes must be 16-byte aligned");
     if (rows < 0 || head_dim < 32 || head_dim % 32) return fail(FP4ATTN_EINVAL, "rows >= 0, head_dim a multiple of 32");
@@ -350,7 +377,7 @@ int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8
     if (rc) return rc;
     if (rows == 0) return FP4ATTN_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int64_t work = rows * (head_dim / 32);
+    const int64_t work = rows * (head_dim / 32) * 4;
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
     if (dtype == FP4ATTN_F16)
         fp4attn::quantize_rowmajor_kernel<__half>
@@ -435,6 +462,20 @@ int fp4attn_selftest_timeout(unsigned timeout_us, void* stream)
     if (timeout_us < 1 || timeout_us > 10000000u) return fail(FP4ATTN_EINVAL, "timeout_us in [1, 1e7]");
     fp4attn::timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<unsigned long long>(timeout_us) * 1000ull);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+int fp4attn_selftest_exp2(const float* x, float* y, int64_t n, void* stream)
+{
+    g_last_error.clear();
+    int rc = device_ready();
+    if (rc) return rc;
+    if (n < 0 || n % 2 || (n && (!x || !y)) || !aligned16(x) || !aligned16(y))
+        return fail(FP4ATTN_EINVAL, "n must be even and >= 0, x and y 16-byte aligned");
+    if (n == 0) return FP4ATTN_OK;
+    fp4attn::exp2_poly_selftest_kernel<<<grid_for(n / 2), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float2*>(x), reinterpret_cast<float2*>(y), n / 2);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }

@@ -2,16 +2,18 @@
 // reference's encode_fp4_e2m1 / compute_scale_ue8m0 (common.h:21-48) and its
 // quantisation loop (common.h:115-123, :160-168).
 //
-// One thread per 32-element block: it reads the block (64 B of FP16 or 128 B
-// of FP32), finds max|x|, forms the scale byte, and writes 16 bytes of packed
-// codes (element 2i in the low nibble) plus the scale byte.  The kernel is
-// HBM-bound: 2 (or 4) bytes in and 0.53 bytes out per element.
+// Four lanes per 32-element block, eight elements per lane: the lanes reduce
+// max|x| with two shuffles, form the scale byte, and each writes 4 bytes of
+// packed codes (element 2i in the low nibble); lane 0 of the group writes the
+// scale byte.  The kernel is HBM-bound: 2 (or 4) bytes in and 0.53 bytes out
+// per element.
 #pragma once
 
 #include <cuda_fp16.h>
 #include <cstdint>
 
 #include "log2_compat.h"
+#include "ptx_sm100.cuh"
 
 namespace fp4attn {
 
@@ -61,59 +63,77 @@ __device__ __forceinline__ float exact_pow2_neg(int s)
     return k >= -126 ? __uint_as_float(static_cast<uint32_t>(k + 127) << 23) : __uint_as_float(1u << 22);
 }
 
+// Each block of 32 elements is handled by 4 consecutive lanes, 8 elements
+// (16 B of FP16 or 32 B of FP32) per lane, so a warp's loads are contiguous.
 template <typename InT>
-__device__ __forceinline__ void load_block32(const InT* src, float (&v)[32]);
+__device__ __forceinline__ void load8(const InT* src, float (&v)[8]);
 
 template <>
-__device__ __forceinline__ void load_block32<__half>(const __half* src, float (&v)[32])
+__device__ __forceinline__ void load8<__half>(const __half* src, float (&v)[8])
 {
-    const uint4* p = reinterpret_cast<const uint4*>(src);
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(src));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        uint4 u = __ldg(p + i);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            float2 f = __half22float2(h[k]);
-            v[i * 8 + 2 * k] = f.x;
-            v[i * 8 + 2 * k + 1] = f.y;
-        }
+    for (int k = 0; k < 4; k++) {
+        float2 f = __half22float2(h[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
     }
 }
 
 template <>
-__device__ __forceinline__ void load_block32<float>(const float* src, float (&v)[32])
+__device__ __forceinline__ void load8<float>(const float* src, float (&v)[8])
 {
     const float4* p = reinterpret_cast<const float4*>(src);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        float4 f = __ldg(p + i);
-        v[i * 4 + 0] = f.x;
-        v[i * 4 + 1] = f.y;
-        v[i * 4 + 2] = f.z;
-        v[i * 4 + 3] = f.w;
-    }
+    float4 a = __ldg(p), b = __ldg(p + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// Quantises one block; returns the reference scale byte and fills 16 bytes of
-// packed codes (the common.h:118-122 loop: x / exp2f(scale - 127), encoded).
-__device__ __forceinline__ uint32_t quantize_block32(const float (&v)[32], int ocp_mode, uint4& packed)
+// One lane's share of a 32-element block: the block maximum is reduced over
+// the 4 lanes of the group (all 32 lanes of the warp must call this), then the
+// reference scale byte is formed and this lane's 8 elements are encoded
+// (the common.h:118-122 loop: x / exp2f(scale - 127), encoded) into 4 bytes.
+__device__ __forceinline__ uint32_t quantize8(const float (&v)[8], int ocp_mode, uint32_t& packed)
 {
     float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; i++) {
+    for (int i = 0; i < 8; i++) {
         const float a = fabsf(v[i]);
         amax = a > amax ? a : amax;  // NaN never wins, as in common.h:44
     }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, amax, o);
+        amax = other > amax ? other : amax;
+    }
     const uint32_t sb = scale_byte(amax, ocp_mode);
     const int s = static_cast<int>(sb) - 127;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    uint32_t w = 0u;
     if (s != 128) {  // s == 128: the reference divides by exp2f(128) = inf, every code is 0
         const float inv = exact_pow2_neg(s);  // x * 2^-s rounds exactly like x / 2^s
+        float q[8];
 #pragma unroll
-        for (int i = 0; i < 32; i++) w[i / 8] |= encode_e2m1(v[i] * inv) << (4 * (i % 8));
+        for (int i = 0; i < 8; i++) q[i] = v[i] * inv;
+        // Fast path: the hardware E2M1 conversion rounds to nearest, ties to
+        // even, saturating at 6.  That equals the reference's ties-up
+        // thresholds except at exact ties (0.25, 1.25, 2.5, 5), at -0.0 and at
+        // NaN.  All of those have the 21 low mantissa bits zero (or are NaN),
+        // so such lanes redo their 8 elements with the exact encoder.
+        w = ptx::cvt_e2m1x8(q);
+        bool exact = false;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t b = __float_as_uint(q[i]);
+            exact |= ((b << 11) == 0u && b != 0u) || ((b & 0x7FFFFFFFu) > 0x7F800000u);
+        }
+        if (exact) {
+            w = 0u;
+#pragma unroll
+            for (int i = 0; i < 8; i++) w |= encode_e2m1(q[i]) << (4 * i);
+        }
     }
-    packed = make_uint4(w[0], w[1], w[2], w[3]);
+    packed = w;
     return sb;
 }
 
@@ -153,28 +173,34 @@ __global__ void __launch_bounds__(256) quantize_tiles_kernel(const InT* __restri
 {
     const int nb = a.padded_dim / 32;
     const int64_t seq_pad = static_cast<int64_t>(a.ntiles) * a.tile_rows;
-    const int64_t total = a.slices * seq_pad * nb;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(idx % nb);
-        const int64_t rowp = idx / nb;
+    const int64_t total = a.slices * seq_pad * nb * 4;  // 4 lanes per block
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t base = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) & ~int64_t(31); base < total;
+         base += stride) {
+        const int64_t idx = base + lane;
+        const bool active = idx < total;  // uniform per group of 4 (total % 4 == 0)
+        const int sub = static_cast<int>(idx & 3);
+        const int64_t blk = idx >> 2;
+        const int b = static_cast<int>(blk % nb);
+        const int64_t rowp = blk / nb;
         const int64_t slice = rowp / seq_pad;
         const int r = static_cast<int>(rowp % seq_pad);
-        uint32_t sb = 127u;
-        if (r < a.seq) {
-            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
-            const int64_t row = slice * a.seq + r;
-            if (b * 32 < a.head_dim) {
-                float v[32];
-                load_block32<InT>(x + row * a.head_dim + b * 32, v);
-                sb = quantize_block32(v, a.ocp_mode, packed);
-                if (sb == 255u) sb = 254u;
-            }
-            *reinterpret_cast<uint4*>(codes + row * (a.padded_dim / 2) + b * 16) = packed;
+        const bool real = active && r < a.seq;
+        const int64_t row = slice * a.seq + r;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const bool has_data = real && b * 32 < a.head_dim;
+        if (has_data) load8<InT>(x + row * a.head_dim + b * 32 + sub * 8, v);
+        uint32_t packed;
+        uint32_t sb = quantize8(v, a.ocp_mode, packed);
+        if (!has_data) sb = 127u;
+        if (sb == 255u) sb = 254u;
+        if (real) *reinterpret_cast<uint32_t*>(codes + row * (a.padded_dim / 2) + b * 16 + sub * 4) = packed;
+        if (active && sub == 0) {
+            const int tile = r / a.tile_rows, rr = r % a.tile_rows;
+            sf[(slice * a.ntiles + tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
+                static_cast<uint8_t>(sb);
         }
-        const int tile = r / a.tile_rows, rr = r % a.tile_rows;
-        sf[(slice * a.ntiles + tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
-            static_cast<uint8_t>(sb);
     }
 }
 
@@ -185,16 +211,21 @@ __global__ void __launch_bounds__(256) quantize_rowmajor_kernel(const InT* __res
                                                                 uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
                                                                 int ocp_mode)
 {
-    const int nb = head_dim / 32;
-    const int64_t total = rows * nb;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float v[32];
-        load_block32<InT>(x + idx * 32, v);
-        uint4 packed;
-        const uint32_t sb = quantize_block32(v, ocp_mode, packed);
-        *reinterpret_cast<uint4*>(codes + idx * 16) = packed;
-        sf[idx] = static_cast<uint8_t>(sb);
+    const int64_t total = rows * (head_dim / 32) * 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t base = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) & ~int64_t(31); base < total;
+         base += stride) {
+        const int64_t idx = base + lane;
+        const bool active = idx < total;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (active) load8<InT>(x + idx * 8, v);
+        uint32_t packed;
+        const uint32_t sb = quantize8(v, ocp_mode, packed);
+        if (active) {
+            *reinterpret_cast<uint32_t*>(codes + idx * 4) = packed;
+            if ((idx & 3) == 0) sf[idx >> 2] = static_cast<uint8_t>(sb);
+        }
     }
 }
 

@@ -137,6 +137,11 @@ int fp4attn_status_query(void* stream);
  * out and sets the error word.  No fault, trap or hang is involved. */
 int fp4attn_selftest_timeout(unsigned timeout_us, void* stream);
 
+/* Test hook: y[i] = 2^x[i] computed by the FMA-pipe polynomial the softmax
+ * uses for part of its exponentials (n even, 16-byte aligned device arrays).
+ * No counterpart in the reference, whose softmax calls expf (common.h:236). */
+int fp4attn_selftest_exp2(const float* x, float* y, int64_t n, void* stream);
+
 /* Static description of a status code. */
 const char* fp4attn_error_string(int status);
 

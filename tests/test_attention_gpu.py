@@ -202,3 +202,17 @@ def test_full_box_sharded_8k_one_gpu_shard(fa, cuda):
                                      V[idx].float().cpu().numpy(), np.array([0, 1], np.int32), rows)
     got = out[torch.tensor(idx), torch.from_numpy(rows).long()].cpu().numpy()
     assert_close(got, want)
+
+
+def test_fma_pipe_exp2_error_bound(fa, cuda):
+    """The polynomial 2^x the softmax computes on the FMA pipe for part of
+    the exponentials: relative error <= 7.6e-5 (the degree-3 minimax bound of
+    fit_exp2_poly.py) over the softmax's input range, 0 for -inf and far below
+    2^-126 for arguments under -127."""
+    x = torch.cat([torch.linspace(-126.0, 8.0, 2_000_000), torch.tensor([-200.0, -1e30, float("-inf"), 0.0])])
+    y = fa.selftest_exp2(x.cuda()).cpu().double()
+    want = torch.exp2(x.double())
+    body = x > -126.0
+    rel = ((y[body] - want[body]).abs() / want[body]).max().item()
+    assert rel <= 7.6e-5, rel
+    assert (y[~body] < 2.0 ** -125).all() and (y[~body] >= 0).all()
