@@ -82,7 +82,9 @@ struct FwdCfg {
     static constexpr int OFF_RED = OFF_V + VST * V_STRIDE;   // [2 parity][2 halves][128 rows] f32 row maxima
     static constexpr int OFF_REDL = OFF_RED + 2 * 2 * 128 * 4; // [2 halves][128 rows] f32 row sums
     static constexpr int OFF_BAR = OFF_REDL + 2 * 128 * 4;
-    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
+    // q_full, K ring, V ring, s_full[2], p_full[2], pv_done, drain, and the
+    // row-max exchange barriers xchg[4 quarters][2 halves][2 parities]
+    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1 + 16;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
 };
 
@@ -106,6 +108,7 @@ enum WaitSite : int {
     kSitePFull,
     kSitePvDone,
     kSiteDrain,
+    kSiteXchg,
 };
 
 struct WaitCtx {
@@ -154,8 +157,10 @@ __device__ __forceinline__ void drain_phase(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
+// 320 threads; 184 registers each (58,880 of the SM's 65,536) keeps the two
+// S tiles of the pipelined softmax in registers without spilling.
 template <int D, int BN, typename OutT, bool kScores, int kPoly8 = 3>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __maxnreg__(184)
     fp4_attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const FwdArgs args)
 {
@@ -177,6 +182,7 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* p_full = s_full + 2;
     uint64_t* pv_done = p_full + 2;
     uint64_t* drain_bar = pv_done + 1;
+    uint64_t* xchg = drain_bar + 1;
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
@@ -202,6 +208,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         ptx::mbar_init(pv_done, 1);
         ptx::mbar_init(drain_bar, 1);
+        for (int i = 0; i < 16; i++) ptx::mbar_init(&xchg[i], 32);
         abort_sh = 0;
         ptx::fence_mbar_init();
     }
@@ -330,140 +337,185 @@ __global__ void __launch_bounds__(320, 1)
     } else {
         // ------------------------------------------------------------ softmax warpgroups
         constexpr int HC = BN / 2;                 // S columns per warpgroup
+        constexpr int NT = HC / 32;                // 32-column chunks per warpgroup
         constexpr int HD = D / 2;                  // O columns per warpgroup
         constexpr int OCH = HD % 32 == 0 ? 32 : 16;  // O column chunk
         const int half = (warp - 2) / 4;           // which half of the columns
         const int wq = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = wq * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-        const uint32_t pair_bar = 1 + wq;          // the two warps (one per half) of this lane quarter
         float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
         float* red_l = reinterpret_cast<float*>(smem + C::OFF_REDL);
         const float c = args.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < nk; j++) {
-            if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
-            ptx::tc_fence_after();
-            const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN;
-            uint32_t sr[HC / 32 > 0 ? HC / 32 : 1][32];
+        if (kScores) {
+            for (int j = 0; j < nk; j++) {
+                if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t sr[NT][32];
 #pragma unroll
-            for (int t = 0; t < HC / 32; t++) ptx::tmem_ld32(s_tm + half * HC + 32 * t, sr[t]);
-            ptx::tc_wait_ld();
-            const int valid = args.seq_k - j * BN - half * HC;  // keys of this half-tile that exist
-            if (kScores) {
+                for (int t = 0; t < NT; t++)
+                    ptx::tmem_ld32(tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC + 32 * t, sr[t]);
+                ptx::tc_wait_ld();
+                const int valid = args.seq_k - j * BN - half * HC;
                 const int grow = q0 + row;
                 if (grow < args.seq_q) {
                     float* dst = reinterpret_cast<float*>(args.out) +
                                  (static_cast<size_t>(slice) * args.seq_q + grow) * args.seq_k +
                                  static_cast<size_t>(j) * BN + half * HC;
 #pragma unroll
-                    for (int t = 0; t < HC / 32; t++)
+                    for (int t = 0; t < NT; t++)
 #pragma unroll
                         for (int i = 0; i < 32; i++)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&p_full[j & 1]);
-                continue;
             }
-            if (valid < HC) {
-#pragma unroll
-                for (int t = 0; t < HC / 32; t++)
-#pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (32 * t + i >= valid) sr[t][i] = __float_as_uint(-INFINITY);
-            }
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int t = 0; t < HC / 32; t++)
-#pragma unroll
-                for (int i = 0; i < 32; i += 8) {
-                    mx4[(i >> 3) & 3] = ptx::fmax3(mx4[(i >> 3) & 3], __uint_as_float(sr[t][i]), __uint_as_float(sr[t][i + 1]));
-                    mx4[((i >> 3) + 1) & 3] =
-                        ptx::fmax3(mx4[((i >> 3) + 1) & 3], __uint_as_float(sr[t][i + 2]), __uint_as_float(sr[t][i + 3]));
-                    mx4[((i >> 3) + 2) & 3] =
-                        ptx::fmax3(mx4[((i >> 3) + 2) & 3], __uint_as_float(sr[t][i + 4]), __uint_as_float(sr[t][i + 5]));
-                    mx4[((i >> 3) + 3) & 3] =
-                        ptx::fmax3(mx4[((i >> 3) + 3) & 3], __uint_as_float(sr[t][i + 6]), __uint_as_float(sr[t][i + 7]));
-                }
-            float mx = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
-            // Exchange the partial row max with the partner warp.  The barrier
-            // also orders this warp's S loads before the partner's P stores,
-            // which overwrite S columns this half read.
-            red[((j & 1) * 2 + half) * 128 + row] = mx;
-            ptx::tc_fence_before();
-            ptx::named_bar_sync(pair_bar, 64);
-            ptx::tc_fence_after();
-            mx = fmaxf(mx, red[((j & 1) * 2 + (1 - half)) * 128 + row]);
-            const float m_new = fmaxf(m, mx * c);
+        } else {
+            // Software-pipelined over K tiles: while the exponentials of S_j
+            // run, the TMEM load of S_{j+1} is in flight; its partial row max
+            // is then published to the partner warp (the other half of the
+            // columns, same rows) through an mbarrier, and collected only after
+            // this warp has finished with P_j, so neither warp idles at the
+            // exchange.  Exchange barriers and slots alternate with tile parity.
+            uint32_t sA[NT][32], sB[NT][32];
             float alpha = 1.f;
             bool rescale = false;
-            if (j == 0) {
-                m = m_new;
-            } else if (m_new > m + 8.0f) {
-                alpha = ptx::ex2_approx(m - m_new);
-                m = m_new;
-                rescale = true;
-            }
-            float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            uint32_t pk[HC / 2];
-            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+            auto load_s = [&](int j, uint32_t (&buf)[NT][32]) {
+                const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC;
 #pragma unroll
-            for (int t = 0; t < HC / 32; t++)
+                for (int t = 0; t < NT; t++) ptx::tmem_ld32(s_tm + 32 * t, buf[t]);
+            };
+            // Mask missing keys, reduce this half's row max, publish it.
+            auto publish_max = [&](int j, uint32_t (&buf)[NT][32]) -> float {
+                const int valid = args.seq_k - j * BN - half * HC;
+                if (valid < HC) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float2 x = ptx::ffma2(make_float2(__uint_as_float(sr[t][i]), __uint_as_float(sr[t][i + 1])), c2, nm2);
-                    // kPoly8 of every 8 column pairs take 2^x on the FMA pipe, the
-                    // rest on MUFU, so both pipes share the exponentials.
-                    const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
-                                                              : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
-                    sum2[(i >> 1) & 1] = ptx::fadd2(sum2[(i >> 1) & 1], p);
-                    pk[t * 16 + i / 2] = ptx::pack_half2(p.x, p.y);
+                    for (int t = 0; t < NT; t++)
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            if (32 * t + i >= valid) buf[t][i] = __float_as_uint(-INFINITY);
                 }
-            l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
-            // P (FP16 pairs) into the first BN/2 columns of this S buffer.
-            const uint32_t p_tm = s_tm + half * (HC / 2);
-            if constexpr (HC / 2 == 32) {
-                ptx::tmem_st32(p_tm, *reinterpret_cast<uint32_t(*)[32]>(pk));
-            } else {
-                ptx::tmem_st16(p_tm, *reinterpret_cast<uint32_t(*)[16]>(pk));
-            }
-            ptx::tc_wait_st();
-            if (j > 0) {
-                // O += P_{j-1} V_{j-1} must have landed before O is rescaled (and
-                // waiting every phase keeps this barrier's parity unambiguous).
-                if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int t = 0; t < NT; t++)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                        mx4[(i >> 1) & 3] =
+                            ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(buf[t][i]), __uint_as_float(buf[t][i + 1]));
+                const float pm = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+                red[((j & 1) * 2 + half) * 128 + row] = pm;
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&xchg[(wq * 2 + half) * 2 + (j & 1)]);
+                return pm;
+            };
+            // Collect the partner's partial max and update the running max.
+            auto collect_max = [&](int j, float pm) -> bool {
+                if (!wait_phase(&xchg[(wq * 2 + (1 - half)) * 2 + (j & 1)], (j >> 1) & 1, wctx, kSiteXchg))
+                    return false;
                 ptx::tc_fence_after();
-                if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-                    for (int t = 0; t < HD / OCH; t++) {
-                        const uint32_t o_tm = tmem + lane_off + C::O_COL + half * HD + OCH * t;
-                        if constexpr (OCH == 32) {
-                            uint32_t o[32];
-                            ptx::tmem_ld32(o_tm, o);
-                            ptx::tc_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                            ptx::tmem_st32(o_tm, o);
-                        } else {
-                            uint32_t o[16];
-                            ptx::tmem_ld16(o_tm, o);
-                            ptx::tc_wait_ld();
-#pragma unroll
-                            for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                            ptx::tmem_st16(o_tm, o);
-                        }
-                    }
-                    ptx::tc_wait_st();
+                const float mx = fmaxf(pm, red[((j & 1) * 2 + (1 - half)) * 128 + row]);
+                const float m_new = fmaxf(m, mx * c);
+                alpha = 1.f;
+                rescale = false;
+                if (j == 0) {
+                    m = m_new;
+                } else if (m_new > m + 8.0f) {
+                    alpha = ptx::ex2_approx(m - m_new);
+                    m = m_new;
+                    rescale = true;
                 }
+                return true;
+            };
+            // One pipelined step: exponentials of S_j (in cur) while S_{j+1}
+            // (into nxt) is loading.
+            auto step = [&](int j, uint32_t (&cur)[NT][32], uint32_t (&nxt)[NT][32]) -> bool {
+                const bool more = j + 1 < nk;
+                if (more) {
+                    if (!wait_phase(&s_full[(j + 1) & 1], ((j + 1) >> 1) & 1, wctx, kSiteSFull)) return false;
+                    ptx::tc_fence_after();
+                    load_s(j + 1, nxt);
+                }
+                const uint32_t p_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * (HC / 2);
+                float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 x =
+                            ptx::ffma2(make_float2(__uint_as_float(cur[t][i]), __uint_as_float(cur[t][i + 1])), c2, nm2);
+                        // kPoly8 of every 8 column pairs take 2^x on the FMA pipe,
+                        // the rest on MUFU, so both pipes share the exponentials.
+                        const float2 p = ((i >> 1) & 7) < kPoly8
+                                             ? ptx::exp2_poly3(x)
+                                             : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                        sum2[(i >> 1) & 1] = ptx::fadd2(sum2[(i >> 1) & 1], p);
+                        pk[i / 2] = ptx::pack_half2(p.x, p.y);
+                    }
+                    ptx::tmem_st16(p_tm + 16 * t, pk);  // P_j (FP16 pairs) over S_j's first columns
+                }
+                l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
+                float pm = 0.f;
+                if (more) {
+                    ptx::tc_wait_ld();
+                    pm = publish_max(j + 1, nxt);
+                }
+                ptx::tc_wait_st();
+                if (j > 0) {
+                    // O += P_{j-1} V_{j-1} must have landed before O is rescaled (and
+                    // waiting every phase keeps this barrier's parity unambiguous).
+                    if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) return false;
+                    ptx::tc_fence_after();
+                    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+                        for (int t = 0; t < HD / OCH; t++) {
+                            const uint32_t o_tm = tmem + lane_off + C::O_COL + half * HD + OCH * t;
+                            if constexpr (OCH == 32) {
+                                uint32_t o[32];
+                                ptx::tmem_ld32(o_tm, o);
+                                ptx::tc_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                                ptx::tmem_st32(o_tm, o);
+                            } else {
+                                uint32_t o[16];
+                                ptx::tmem_ld16(o_tm, o);
+                                ptx::tc_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                                ptx::tmem_st16(o_tm, o);
+                            }
+                        }
+                        ptx::tc_wait_st();
+                    }
+                }
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&p_full[j & 1]);
+                if (more && !collect_max(j + 1, pm)) return false;
+                return true;
+            };
+            // prologue: S_0 and its row max
+            if (!wait_phase(&s_full[0], 0, wctx, kSiteSFull)) {
+                ok = false;
+            } else {
+                ptx::tc_fence_after();
+                load_s(0, sA);
+                ptx::tc_wait_ld();
+                const float pm = publish_max(0, sA);
+                ok = collect_max(0, pm);
             }
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&p_full[j & 1]);
+            for (int j = 0; ok && j < nk; j += 2) {
+                if (!step(j, sA, sB)) { ok = false; break; }
+                if (j + 1 < nk && !step(j + 1, sB, sA)) { ok = false; break; }
+            }
         }
         if (!kScores && ok) {
             red_l[half * 128 + row] = l;
-            ptx::named_bar_sync(pair_bar, 64);
+            ptx::named_bar_sync(1 + wq, 64);
             const float l_tot = l + red_l[(1 - half) * 128 + row];
             if (wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone)) {
                 ptx::tc_fence_after();

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -175,11 +176,21 @@ int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slice
     a.head_dim = d;
     a.padded_dim = padded_dim(d);
     a.tile_rows = tile_rows;
+    a.tile_shift = tile_rows == 128 ? 7 : 6;
     a.ntiles = (seq + tile_rows - 1) / tile_rows;
     a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
     a.ocp_mode = ocp;
-    const int64_t work = slices * static_cast<int64_t>(a.ntiles) * tile_rows * (a.padded_dim / 32) * 4;
-    fp4attn::quantize_tiles_kernel<InT><<<grid_for(work), 256, 0, st>>>(static_cast<const InT*>(x), codes, sf, a);
+    const int per_slice = a.ntiles * tile_rows * (a.padded_dim / 32) * 4;
+    const int gx = static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
+    dim3 grid(gx, static_cast<unsigned>(slices));
+    const InT* xp = static_cast<const InT*>(x);
+    switch (a.padded_dim / 32) {
+        case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
+        case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
+        case 6: fp4attn::quantize_tiles_kernel<InT, 6><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
+        case 8: fp4attn::quantize_tiles_kernel<InT, 8><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
+        default: return fail(FP4ATTN_EUNSUPPORTED, "padded head_dim %d", a.padded_dim);
+    }
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }

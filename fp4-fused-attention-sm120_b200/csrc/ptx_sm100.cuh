@@ -329,13 +329,14 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
 // 1.5 * 2^23 addition trick, f = x - n in [-0.5, 0.5], p(f) the degree-3
 // minimax polynomial for 2^f (relative error <= 7.5e-5, coefficients from
 // fit_exp2_poly.py), and 2^n applied by adding n to the exponent field.  x is
-// clamped at -127 first, so -inf and very small arguments give 0 (or a value
-// below 2^-126), as ex2 would after FP16 rounding.
+// clamped at -126 first: p(f) can be below 1 (exponent field 126), so any
+// n >= -126 keeps the sum's exponent field >= 0, and -inf or very small
+// arguments give a value below 2^-125 (zero after FP16 rounding).
 __device__ __forceinline__ float2 exp2_poly3(float2 x)
 {
     constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    x.x = fmaxf(x.x, -127.0f);
-    x.y = fmaxf(x.y, -127.0f);
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
     const float2 j = fadd2(x, make_float2(kMagic, kMagic));
     const float2 n = fadd2(j, make_float2(-kMagic, -kMagic));
     const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);

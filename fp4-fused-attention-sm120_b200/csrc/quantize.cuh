@@ -94,6 +94,19 @@ __device__ __forceinline__ void load8<float>(const float* src, float (&v)[8])
 // the 4 lanes of the group (all 32 lanes of the warp must call this), then the
 // reference scale byte is formed and this lane's 8 elements are encoded
 // (the common.h:118-122 loop: x / exp2f(scale - 127), encoded) into 4 bytes.
+//
+// Encoding uses the hardware E2M1 conversion, which rounds to nearest with
+// ties to even and saturates at 6; the reference rounds ties up (away from
+// zero).  The two differ only at exact ties (|q| = 0.25, 1.25, 2.5, 5), at
+// -0.0 (the reference gives code 0) and at NaN (code 0).
+//  * kFromHalf (values came from FP16, so q has at most 11 significant bits):
+//    q * (1 + 2^-12) + 0 moves every exact tie above its threshold and no
+//    other value across one (a non-tie is at least 2^-11 relative away from
+//    any threshold), and turns -0.0 into +0.0; only a NaN in the block (seen
+//    through the block sum) takes the exact path.
+//  * FP32 input: a lane whose values include a possible tie (21 low mantissa
+//    bits zero), -0.0 or NaN redoes its 8 elements with the exact encoder.
+template <bool kFromHalf>
 __device__ __forceinline__ uint32_t quantize8(const float (&v)[8], int ocp_mode, uint32_t& packed)
 {
     float amax = 0.f;
@@ -113,24 +126,42 @@ __device__ __forceinline__ uint32_t quantize8(const float (&v)[8], int ocp_mode,
     if (s != 128) {  // s == 128: the reference divides by exp2f(128) = inf, every code is 0
         const float inv = exact_pow2_neg(s);  // x * 2^-s rounds exactly like x / 2^s
         float q[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) q[i] = v[i] * inv;
-        // Fast path: the hardware E2M1 conversion rounds to nearest, ties to
-        // even, saturating at 6.  That equals the reference's ties-up
-        // thresholds except at exact ties (0.25, 1.25, 2.5, 5), at -0.0 and at
-        // NaN.  All of those have the 21 low mantissa bits zero (or are NaN),
-        // so such lanes redo their 8 elements with the exact encoder.
-        w = ptx::cvt_e2m1x8(q);
         bool exact = false;
+        if constexpr (kFromHalf) {
+            const float2 inv2 = make_float2(inv, inv);
+            const float2 nudge = make_float2(1.0f + 0x1p-12f, 1.0f + 0x1p-12f), zero = make_float2(0.f, 0.f);
+            float2 sum = zero;
+            float qq[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t b = __float_as_uint(q[i]);
-            exact |= ((b << 11) == 0u && b != 0u) || ((b & 0x7FFFFFFFu) > 0x7F800000u);
-        }
-        if (exact) {
-            w = 0u;
+            for (int i = 0; i < 8; i += 2) {
+                const float2 t = ptx::fmul2(make_float2(v[i], v[i + 1]), inv2);
+                qq[i] = t.x;
+                qq[i + 1] = t.y;
+                const float2 u = ptx::ffma2(t, nudge, zero);
+                q[i] = u.x;
+                q[i + 1] = u.y;
+                sum = ptx::fadd2(sum, make_float2(v[i], v[i + 1]));
+            }
+            w = ptx::cvt_e2m1x8(q);
+            if (isnan(sum.x + sum.y)) {
+                w = 0u;
 #pragma unroll
-            for (int i = 0; i < 8; i++) w |= encode_e2m1(q[i]) << (4 * i);
+                for (int i = 0; i < 8; i++) w |= encode_e2m1(qq[i]) << (4 * i);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[i] = v[i] * inv;
+            w = ptx::cvt_e2m1x8(q);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t b = __float_as_uint(q[i]);
+                exact |= ((b << 11) == 0u && b != 0u) || ((b & 0x7FFFFFFFu) > 0x7F800000u);
+            }
+            if (exact) {
+                w = 0u;
+#pragma unroll
+                for (int i = 0; i < 8; i++) w |= encode_e2m1(q[i]) << (4 * i);
+            }
         }
     }
     packed = w;
@@ -156,6 +187,7 @@ struct QuantTileArgs {
     int head_dim;    // D (multiple of 32)
     int padded_dim;  // DP, multiple of 64 (the MMA's K step)
     int tile_rows;   // 128 or 64
+    int tile_shift;  // log2(tile_rows)
     int ntiles;      // ceil(seq / tile_rows)
     int sf_tile_bytes;
     int ocp_mode;
@@ -167,38 +199,36 @@ struct QuantTileArgs {
 // scale 127 so the (zero-filled) padding never multiplies an undefined scale.
 // A reference scale of 255 only occurs with all-zero codes and is stored as
 // 254, which the MMA reads as a finite 2^127 (255 would be NaN in E8M0).
-template <typename InT>
+// Grid: x covers one slice's padded rows (4 lanes per block, kNB blocks of 32
+// per row), y is the slice, so all index arithmetic is 32-bit with a
+// compile-time divisor.
+template <typename InT, int kNB>
 __global__ void __launch_bounds__(256) quantize_tiles_kernel(const InT* __restrict__ x, uint8_t* __restrict__ codes,
                                                              uint8_t* __restrict__ sf, QuantTileArgs a)
 {
-    const int nb = a.padded_dim / 32;
-    const int64_t seq_pad = static_cast<int64_t>(a.ntiles) * a.tile_rows;
-    const int64_t total = a.slices * seq_pad * nb * 4;  // 4 lanes per block
-    const int lane = threadIdx.x & 31;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t base = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) & ~int64_t(31); base < total;
-         base += stride) {
-        const int64_t idx = base + lane;
-        const bool active = idx < total;  // uniform per group of 4 (total % 4 == 0)
-        const int sub = static_cast<int>(idx & 3);
-        const int64_t blk = idx >> 2;
-        const int b = static_cast<int>(blk % nb);
-        const int64_t rowp = blk / nb;
-        const int64_t slice = rowp / seq_pad;
-        const int r = static_cast<int>(rowp % seq_pad);
-        const bool real = active && r < a.seq;
-        const int64_t row = slice * a.seq + r;
+    const int seq_pad = a.ntiles * a.tile_rows;
+    const int total = seq_pad * kNB * 4;  // lanes per slice; a multiple of 32
+    const int64_t slice = blockIdx.y;
+    const InT* xs = x + slice * a.seq * a.head_dim;
+    uint8_t* cs = codes + slice * a.seq * (kNB * 16);
+    uint8_t* fs = sf + slice * a.ntiles * a.sf_tile_bytes;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+        const int sub = idx & 3;
+        const int blk = idx >> 2;
+        const int b = blk % kNB;
+        const int r = blk / kNB;
+        const bool real = r < a.seq;
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         const bool has_data = real && b * 32 < a.head_dim;
-        if (has_data) load8<InT>(x + row * a.head_dim + b * 32 + sub * 8, v);
+        if (has_data) load8<InT>(xs + static_cast<int64_t>(r) * a.head_dim + b * 32 + sub * 8, v);
         uint32_t packed;
-        uint32_t sb = quantize8(v, a.ocp_mode, packed);
+        uint32_t sb = quantize8<sizeof(InT) == 2>(v, a.ocp_mode, packed);
         if (!has_data) sb = 127u;
         if (sb == 255u) sb = 254u;
-        if (real) *reinterpret_cast<uint32_t*>(codes + row * (a.padded_dim / 2) + b * 16 + sub * 4) = packed;
-        if (active && sub == 0) {
-            const int tile = r / a.tile_rows, rr = r % a.tile_rows;
-            sf[(slice * a.ntiles + tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
+        if (real) *reinterpret_cast<uint32_t*>(cs + static_cast<int64_t>(r) * (kNB * 16) + b * 16 + sub * 4) = packed;
+        if (sub == 0) {
+            const int tile = r >> a.tile_shift, rr = r & (a.tile_rows - 1);
+            fs[static_cast<int64_t>(tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
                 static_cast<uint8_t>(sb);
         }
     }
@@ -221,7 +251,7 @@ __global__ void __launch_bounds__(256) quantize_rowmajor_kernel(const InT* __res
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (active) load8<InT>(x + idx * 8, v);
         uint32_t packed;
-        const uint32_t sb = quantize8(v, ocp_mode, packed);
+        const uint32_t sb = quantize8<sizeof(InT) == 2>(v, ocp_mode, packed);
         if (active) {
             *reinterpret_cast<uint32_t*>(codes + idx * 4) = packed;
             if ((idx & 3) == 0) sf[idx >> 2] = static_cast<uint8_t>(sb);
