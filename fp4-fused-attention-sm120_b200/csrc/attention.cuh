@@ -10,19 +10,23 @@
 //               and V tiles through KST/VST-stage mbarrier rings.
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T with
 //               tcgen05.mma kind::mxf4 block_scale (scales in TMEM, copied with
-//               tcgen05.cp), then O += P_j V_j with tcgen05.mma kind::f16 whose
-//               A operand (P) is read from TMEM.  S is double-buffered in TMEM
-//               so S_{j+1} runs on the tensor cores while S_j is in softmax.
-//   warps 2-9   two softmax warpgroups; thread = query row = TMEM lane, and
+//               tcgen05.cp), and O += P_j V_j with tcgen05.mma kind::f16 whose
+//               A operand (P) is read from TMEM.  S is double-buffered and P
+//               has its own columns, so S_{j+2} is issued as soon as the
+//               softmax has loaded S_j -- the tensor cores run ahead of the
+//               softmax instead of waiting behind P.V.
+//   warps 2-3   idle (they complete the control warpgroup for setmaxnreg)
+//   warps 4-11  two softmax warpgroups; thread = query row = TMEM lane, and
 //               each warpgroup owns half of the S_j columns (and half of O's).
-//               tcgen05.ld of its S_j half, partial row max exchanged with the
-//               partner warp through shared memory, online max/sum in FP32
-//               (log2 domain), P_j written back as FP16 into the S_j columns
-//               with tcgen05.st, lazy O rescale (only when the row max grows by
-//               more than 2^8), final O / l for its half of the columns.
+//               Software-pipelined over K tiles: the TMEM load of S_{j+1} and
+//               its partial row max (exchanged with the partner warp through
+//               shared memory and an mbarrier) overlap the exponentials of
+//               S_j.  Online max/sum in FP32 (log2 domain), P_j stored as FP16
+//               with tcgen05.st, lazy O rescale (only when the row max grows
+//               by more than 2^8), final O / l for its half of the columns.
 //
 // TMEM columns (512 allocated): S0 [0,BN), S1 [BN,2BN), O [2BN, 2BN+D),
-// then the Q scale columns and KST stages of K scale columns.
+// P [.., +BN/2), then the Q scale columns and KST stages of K scale columns.
 //
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // FP4ATTN_ETIMEOUT in the device error word, all roles leave their loops,
@@ -59,7 +63,8 @@ struct FwdCfg {
     // TMEM
     static constexpr int S_COL = 0;
     static constexpr int O_COL = 2 * BN;
-    static constexpr int SFA_COL = O_COL + D;
+    static constexpr int P_COL = O_COL + D;                 // BN/2 columns of FP16 pairs
+    static constexpr int SFA_COL = P_COL + BN / 2;
     static constexpr int SFB_COL = SFA_COL + 4 * SFA_ATOMS;
     static constexpr int TMEM_USED = SFB_COL + KST * SFB_COLS;
     static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
@@ -82,9 +87,9 @@ struct FwdCfg {
     static constexpr int OFF_RED = OFF_V + VST * V_STRIDE;   // [2 parity][2 halves][128 rows] f32 row maxima
     static constexpr int OFF_REDL = OFF_RED + 2 * 2 * 128 * 4; // [2 halves][128 rows] f32 row sums
     static constexpr int OFF_BAR = OFF_REDL + 2 * 128 * 4;
-    // q_full, K ring, V ring, s_full[2], p_full[2], pv_done, drain, and the
-    // row-max exchange barriers xchg[4 quarters][2 halves][2 parities]
-    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1 + 16;
+    // q_full, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done, drain,
+    // and the row-max exchange barriers xchg[4 quarters][2 halves][2 parities]
+    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 2 + 1 + 1 + 16;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
 };
 
@@ -109,6 +114,7 @@ enum WaitSite : int {
     kSitePvDone,
     kSiteDrain,
     kSiteXchg,
+    kSiteSFree,
 };
 
 struct WaitCtx {
@@ -157,10 +163,24 @@ __device__ __forceinline__ void drain_phase(uint64_t* bar, uint32_t parity, unsi
     }
 }
 
-// 320 threads; 184 registers each (58,880 of the SM's 65,536) keeps the two
-// S tiles of the pipelined softmax in registers without spilling.
+// Thread layout: 384 threads = 3 warpgroups.  Each SM sub-partition has its
+// own quarter of the register file and hosts one warp of every warpgroup, so
+// at launch every thread gets 168 registers (3 x 168 x 32 <= 16384).  The
+// control warpgroup then gives registers back (setmaxnreg.dec to kCtlRegs) and
+// the two softmax warpgroups take them (setmaxnreg.inc to kSmRegs):
+// 128 x 80 + 256 x 208 = 63,488 <= 384 x 168 = 64,512, and per sub-partition
+// 80 + 2 x 208 = 496 registers x 32 lanes <= 16,384.  The host checks the
+// launch register count before every launch (a shortfall would make
+// setmaxnreg.inc wait for registers that never free up).
+constexpr int kFwdThreads = 384;
+constexpr int kCtlRegs = 80;
+constexpr int kSmRegs = 208;
+constexpr int kLaunchRegs = 168;
+static_assert(128 * kCtlRegs + 256 * kSmRegs <= kFwdThreads * kLaunchRegs, "register split exceeds the launch pool");
+static_assert((kCtlRegs + 2 * kSmRegs) * 32 <= 16384, "register split exceeds a sub-partition");
+
 template <int D, int BN, typename OutT, bool kScores, int kPoly8 = 3>
-__global__ void __maxnreg__(184)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const FwdArgs args)
 {
@@ -178,9 +198,10 @@ __global__ void __maxnreg__(184)
     uint64_t* k_empty = k_full + C::KST;
     uint64_t* v_full = k_empty + C::KST;
     uint64_t* v_empty = v_full + C::VST;
-    uint64_t* s_full = v_empty + C::VST;
-    uint64_t* p_full = s_full + 2;
-    uint64_t* pv_done = p_full + 2;
+    uint64_t* s_full = v_empty + C::VST;  // S_j computed (tcgen05.commit)
+    uint64_t* s_free = s_full + 2;        // S_j loaded by all 256 softmax threads
+    uint64_t* p_full = s_free + 2;        // P_j stored and O rescaled (256 threads)
+    uint64_t* pv_done = p_full + 2;       // O += P_j V_j complete (tcgen05.commit)
     uint64_t* drain_bar = pv_done + 1;
     uint64_t* xchg = drain_bar + 1;
 
@@ -204,6 +225,7 @@ __global__ void __maxnreg__(184)
         }
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&s_full[i], 1);
+            ptx::mbar_init(&s_free[i], 256);
             ptx::mbar_init(&p_full[i], 256);
         }
         ptx::mbar_init(pv_done, 1);
@@ -227,120 +249,134 @@ __global__ void __maxnreg__(184)
     const uint32_t tmem = tmem_base_sh;
     const WaitCtx wctx{&abort_sh, args.timeout_ns};
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ producer
-        if (lane == 0) {
-            ptx::mbar_arrive_expect_tx(q_full, C::Q_BYTES + C::QSF_BYTES);
-#pragma unroll
-            for (int c = 0; c < C::NCH; c++)
-                ptx::tma_load_3d(sQ + c * C::BM * C::CW, &tm_q, q_full, c * C::CW, q0, slice);
-            ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.nq_tiles + qt) * C::QSF_BYTES,
-                           C::QSF_BYTES, q_full);
-            int k_issued = 0, v_issued = 0;
-            for (int j = 0; j < nk; j++) {
-                const int ks = j % C::KST;
-                if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
-                ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::KSF_BYTES);
+    if (warp < 4) {
+        ptx::setmaxnreg_dec<kCtlRegs>();
+        if (warp == 0) {
+            // -------------------------------------------------------- producer
+            if (lane == 0) {
+                ptx::mbar_arrive_expect_tx(q_full, C::Q_BYTES + C::QSF_BYTES);
 #pragma unroll
                 for (int c = 0; c < C::NCH; c++)
-                    ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW, j * BN,
-                                     slice);
-                ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
-                               args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::KSF_BYTES, C::KSF_BYTES,
-                               &k_full[ks]);
-                k_issued = j + 1;
-                if (!kScores) {
+                    ptx::tma_load_3d(sQ + c * C::BM * C::CW, &tm_q, q_full, c * C::CW, q0, slice);
+                ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.nq_tiles + qt) * C::QSF_BYTES,
+                               C::QSF_BYTES, q_full);
+                int k_issued = 0, v_issued = 0;
+                for (int j = 0; j < nk; j++) {
+                    const int ks = j % C::KST;
+                    if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::KSF_BYTES);
+#pragma unroll
+                    for (int c = 0; c < C::NCH; c++)
+                        ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW,
+                                         j * BN, slice);
+                    ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
+                                   args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::KSF_BYTES, C::KSF_BYTES,
+                                   &k_full[ks]);
+                    k_issued = j + 1;
+                    if (!kScores) {
+                        const int vs = j % C::VST;
+                        if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty))
+                            break;
+                        ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+#pragma unroll
+                        for (int c = 0; c < C::VCH; c++)
+                            ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
+                                             c * (C::VCW / 2), j * BN, slice);
+                        v_issued = j + 1;
+                    }
+                }
+                // Every load this thread issued must land before the CTA exits.
+                const unsigned long long drain_ns = 2ull * args.timeout_ns;
+                drain_phase(q_full, 0, drain_ns);
+                for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
+                    drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
+                for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
+                    drain_phase(&v_full[i % C::VST], (i / C::VST) & 1, drain_ns);
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            // -------------------------------------------------------- MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::CW);
+                constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
+                // Descriptors are built once; per MMA only the 16-byte-unit start
+                // address in the low bits moves.
+                const uint64_t qdesc0 = ptx::make_sdesc(ptx::smem_u32(sQ), 16, 8 * C::CW, qk_layout);
+                const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::CW, qk_layout);
+                const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
+                const uint64_t sfdesc0 = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
+                constexpr uint32_t idesc_pv = ptx::idesc_f16(128, D, true);
+                bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
+                if (ok) {
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int at = 0; at < C::SFA_ATOMS; at++)
+                        ptx::tc_cp_32x128b_warpx4(
+                            tmem + C::SFA_COL + 4 * at,
+                            ptx::make_sdesc(ptx::smem_u32(sQsf + 512 * at), 0, 128, ptx::kSwizzleNone));
+                }
+                auto issue_s = [&](int j) -> bool {
+                    const int ks = j % C::KST;
+                    if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) return false;
+                    ptx::tc_fence_after();
+                    const uint32_t sfb_base = tmem + C::SFB_COL + ks * C::SFB_COLS;
+#pragma unroll
+                    for (int at = 0; at < C::SFB_ATOMS; at++)
+                        ptx::tc_cp_32x128b_warpx4(sfb_base + 4 * at,
+                                                  sfdesc0 + static_cast<uint64_t>((ks * C::KSF_BYTES + 512 * at) >> 4));
+                    const uint32_t s_tmem = tmem + C::S_COL + (j & 1) * BN;
+                    const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
+#pragma unroll
+                    for (int kk = 0; kk < C::KSTEPS; kk++) {
+                        const int off = kk * 32, ch = off / C::CW, in = off % C::CW;
+                        const uint32_t sf_id = 2u * (kk & 1);
+                        ptx::mma_mxf4(s_tmem, qdesc0 + static_cast<uint64_t>((ch * C::BM * C::CW + in) >> 4),
+                                      kdesc + static_cast<uint64_t>((ch * BN * C::CW + in) >> 4),
+                                      ptx::idesc_mxf4(128, BN, sf_id, sf_id),
+                                      (tmem + C::SFA_COL + 4 * (kk >> 1)) | (sf_id << 30),
+                                      (sfb_base + (BN == 128 ? 4 : 2) * (kk >> 1)) | (sf_id << 30), kk > 0 ? 1u : 0u);
+                    }
+                    ptx::tc_commit(&s_full[j & 1]);
+                    ptx::tc_commit(&k_empty[ks]);
+                    return true;
+                };
+                if (ok) ok = issue_s(0);
+                if (ok && nk > 1) ok = issue_s(1);
+                for (int j = 0; ok && j < nk; j++) {
+                    // S_{j+2} reuses S_j's buffer as soon as the softmax has read S_j.
+                    if (j + 2 < nk) {
+                        if (!wait_phase(&s_free[j & 1], (j >> 1) & 1, wctx, kSiteSFree)) break;
+                        ptx::tc_fence_after();
+                        if (!issue_s(j + 2)) break;
+                    }
+                    if (kScores) continue;
+                    if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
                     const int vs = j % C::VST;
-                    if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty)) break;
-                    ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+                    if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
+                    ptx::tc_fence_after();
+                    const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
 #pragma unroll
-                    for (int c = 0; c < C::VCH; c++)
-                        ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
-                                         c * (C::VCW / 2), j * BN, slice);
-                    v_issued = j + 1;
+                    for (int kk = 0; kk < BN / 16; kk++)
+                        ptx::mma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
+                                        vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
+                                        (j > 0 || kk > 0) ? 1u : 0u);
+                    ptx::tc_commit(&v_empty[vs]);
+                    ptx::tc_commit(pv_done);
                 }
+                // Drain every tcgen05 op this thread issued before TMEM is freed.
+                ptx::tc_commit(drain_bar);
+                drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
             }
-            // Every load this thread issued must land before the CTA exits.
-            const unsigned long long drain_ns = 2ull * args.timeout_ns;
-            drain_phase(q_full, 0, drain_ns);
-            for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
-                drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
-            for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
-                drain_phase(&v_full[i % C::VST], (i / C::VST) & 1, drain_ns);
+            __syncwarp();
         }
-        __syncwarp();
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::CW);
-            constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
-            const uint32_t sQ_a = ptx::smem_u32(sQ), sK_a = ptx::smem_u32(sK), sV_a = ptx::smem_u32(sV);
-            bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
-            if (ok) {
-                ptx::tc_fence_after();
-#pragma unroll
-                for (int at = 0; at < C::SFA_ATOMS; at++)
-                    ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL + 4 * at,
-                                              ptx::make_sdesc(ptx::smem_u32(sQsf + 512 * at), 0, 128, ptx::kSwizzleNone));
-            }
-            auto issue_s = [&](int j) -> bool {
-                const int ks = j % C::KST;
-                if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) return false;
-                ptx::tc_fence_after();
-                const uint32_t sfb_base = tmem + C::SFB_COL + ks * C::SFB_COLS;
-#pragma unroll
-                for (int at = 0; at < C::SFB_ATOMS; at++)
-                    ptx::tc_cp_32x128b_warpx4(
-                        sfb_base + 4 * at,
-                        ptx::make_sdesc(ptx::smem_u32(sKsf + ks * C::KSF_BYTES + 512 * at), 0, 128, ptx::kSwizzleNone));
-                const uint32_t s_tmem = tmem + C::S_COL + (j & 1) * BN;
-#pragma unroll
-                for (int kk = 0; kk < C::KSTEPS; kk++) {
-                    const int off = kk * 32, ch = off / C::CW, in = off % C::CW;
-                    const uint64_t adesc = ptx::make_sdesc(sQ_a + ch * C::BM * C::CW + in, 16, 8 * C::CW, qk_layout);
-                    const uint64_t bdesc =
-                        ptx::make_sdesc(sK_a + ks * C::K_STRIDE + ch * BN * C::CW + in, 16, 8 * C::CW, qk_layout);
-                    const uint32_t sf_id = 2u * (kk & 1);
-                    const uint32_t sfa = (tmem + C::SFA_COL + 4 * (kk >> 1)) | (sf_id << 30);
-                    const uint32_t sfb = (sfb_base + (BN == 128 ? 4 : 2) * (kk >> 1)) | (sf_id << 30);
-                    ptx::mma_mxf4(s_tmem, adesc, bdesc, ptx::idesc_mxf4(128, BN, sf_id, sf_id), sfa, sfb,
-                                  kk > 0 ? 1u : 0u);
-                }
-                ptx::tc_commit(&s_full[j & 1]);
-                ptx::tc_commit(&k_empty[ks]);
-                return true;
-            };
-            if (ok) ok = issue_s(0);
-            for (int j = 0; ok && j < nk; j++) {
-                if (j + 1 < nk && !issue_s(j + 1)) break;
-                if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
-                if (kScores) continue;
-                const int vs = j % C::VST;
-                if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
-                ptx::tc_fence_after();
-                const uint32_t p_tmem = tmem + C::S_COL + (j & 1) * BN;
-#pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t bdesc =
-                        ptx::make_sdesc(sV_a + vs * C::V_STRIDE + kk * 16 * C::VCW, BN * C::VCW, 8 * C::VCW, v_layout);
-                    ptx::mma_f16_ts(tmem + C::O_COL, p_tmem + kk * 8, bdesc, ptx::idesc_f16(128, D, true),
-                                    (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                ptx::tc_commit(&v_empty[vs]);
-                ptx::tc_commit(pv_done);
-            }
-            // Drain every tcgen05 op this thread issued before TMEM is freed.
-            ptx::tc_commit(drain_bar);
-            drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
-        }
-        __syncwarp();
     } else {
+        ptx::setmaxnreg_inc<kSmRegs>();
         // ------------------------------------------------------------ softmax warpgroups
         constexpr int HC = BN / 2;                 // S columns per warpgroup
         constexpr int NT = HC / 32;                // 32-column chunks per warpgroup
         constexpr int HD = D / 2;                  // O columns per warpgroup
         constexpr int OCH = HD % 32 == 0 ? 32 : 16;  // O column chunk
-        const int half = (warp - 2) / 4;           // which half of the columns
+        const int half = (warp - 4) / 4;           // which half of the columns
         const int wq = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = wq * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
@@ -349,15 +385,24 @@ __global__ void __maxnreg__(184)
         const float c = args.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
+        auto load_s = [&](int j, uint32_t (&buf)[NT][32]) {
+            const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC;
+#pragma unroll
+            for (int t = 0; t < NT; t++) ptx::tmem_ld32(s_tm + 32 * t, buf[t]);
+        };
+        // After the loads of S_j have completed: let the MMA reuse S_j's buffer.
+        auto release_s = [&](int j) {
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&s_free[j & 1]);
+        };
         if (kScores) {
             for (int j = 0; j < nk; j++) {
                 if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
                 ptx::tc_fence_after();
                 uint32_t sr[NT][32];
-#pragma unroll
-                for (int t = 0; t < NT; t++)
-                    ptx::tmem_ld32(tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC + 32 * t, sr[t]);
+                load_s(j, sr);
                 ptx::tc_wait_ld();
+                release_s(j);
                 const int valid = args.seq_k - j * BN - half * HC;
                 const int grow = q0 + row;
                 if (grow < args.seq_q) {
@@ -370,25 +415,13 @@ __global__ void __maxnreg__(184)
                         for (int i = 0; i < 32; i++)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
                 }
-                ptx::tc_fence_before();
-                ptx::mbar_arrive(&p_full[j & 1]);
             }
         } else {
-            // Software-pipelined over K tiles: while the exponentials of S_j
-            // run, the TMEM load of S_{j+1} is in flight; its partial row max
-            // is then published to the partner warp (the other half of the
-            // columns, same rows) through an mbarrier, and collected only after
-            // this warp has finished with P_j, so neither warp idles at the
-            // exchange.  Exchange barriers and slots alternate with tile parity.
             uint32_t sA[NT][32], sB[NT][32];
             float alpha = 1.f;
             bool rescale = false;
-            auto load_s = [&](int j, uint32_t (&buf)[NT][32]) {
-                const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC;
-#pragma unroll
-                for (int t = 0; t < NT; t++) ptx::tmem_ld32(s_tm + 32 * t, buf[t]);
-            };
-            // Mask missing keys, reduce this half's row max, publish it.
+            // Mask missing keys, reduce this half's row max, publish it to the
+            // partner warp (slot and barrier alternate with tile parity).
             auto publish_max = [&](int j, uint32_t (&buf)[NT][32]) -> float {
                 const int valid = args.seq_k - j * BN - half * HC;
                 if (valid < HC) {
@@ -407,7 +440,6 @@ __global__ void __maxnreg__(184)
                             ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(buf[t][i]), __uint_as_float(buf[t][i + 1]));
                 const float pm = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
                 red[((j & 1) * 2 + half) * 128 + row] = pm;
-                ptx::tc_fence_before();
                 ptx::mbar_arrive(&xchg[(wq * 2 + half) * 2 + (j & 1)]);
                 return pm;
             };
@@ -415,7 +447,6 @@ __global__ void __maxnreg__(184)
             auto collect_max = [&](int j, float pm) -> bool {
                 if (!wait_phase(&xchg[(wq * 2 + (1 - half)) * 2 + (j & 1)], (j >> 1) & 1, wctx, kSiteXchg))
                     return false;
-                ptx::tc_fence_after();
                 const float mx = fmaxf(pm, red[((j & 1) * 2 + (1 - half)) * 128 + row]);
                 const float m_new = fmaxf(m, mx * c);
                 alpha = 1.f;
@@ -429,8 +460,9 @@ __global__ void __maxnreg__(184)
                 }
                 return true;
             };
-            // One pipelined step: exponentials of S_j (in cur) while S_{j+1}
-            // (into nxt) is loading.
+            // One pipelined step: S_j (in cur) becomes P_j while S_{j+1} loads
+            // into nxt; S_{j+1}'s partial max is published halfway through the
+            // exponentials and collected after P_j has been handed to the MMA.
             auto step = [&](int j, uint32_t (&cur)[NT][32], uint32_t (&nxt)[NT][32]) -> bool {
                 const bool more = j + 1 < nk;
                 if (more) {
@@ -438,12 +470,12 @@ __global__ void __maxnreg__(184)
                     ptx::tc_fence_after();
                     load_s(j + 1, nxt);
                 }
-                const uint32_t p_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * (HC / 2);
                 float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                 const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+                uint32_t pk[NT][16];
+                float pm = 0.f;
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
-                    uint32_t pk[16];
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         const float2 x =
@@ -454,45 +486,47 @@ __global__ void __maxnreg__(184)
                                              ? ptx::exp2_poly3(x)
                                              : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
                         sum2[(i >> 1) & 1] = ptx::fadd2(sum2[(i >> 1) & 1], p);
-                        pk[i / 2] = ptx::pack_half2(p.x, p.y);
+                        pk[t][i / 2] = ptx::pack_half2(p.x, p.y);
                     }
-                    ptx::tmem_st16(p_tm + 16 * t, pk);  // P_j (FP16 pairs) over S_j's first columns
+                    if (more && t == (NT - 1) / 2) {
+                        ptx::tc_wait_ld();
+                        release_s(j + 1);
+                        pm = publish_max(j + 1, nxt);
+                    }
                 }
                 l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
-                float pm = 0.f;
-                if (more) {
-                    ptx::tc_wait_ld();
-                    pm = publish_max(j + 1, nxt);
-                }
-                ptx::tc_wait_st();
                 if (j > 0) {
-                    // O += P_{j-1} V_{j-1} must have landed before O is rescaled (and
-                    // waiting every phase keeps this barrier's parity unambiguous).
+                    // PV_{j-1} must be done: it reads the P columns this step
+                    // overwrites, and O is rescaled below (waiting every phase
+                    // also keeps this barrier's parity unambiguous).
                     if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) return false;
                     ptx::tc_fence_after();
-                    if (__any_sync(0xffffffffu, rescale)) {
+                }
+                const uint32_t p_tm = tmem + lane_off + C::P_COL + half * (HC / 2);
+#pragma unroll
+                for (int t = 0; t < NT; t++) ptx::tmem_st16(p_tm + 16 * t, pk[t]);
+                if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-                        for (int t = 0; t < HD / OCH; t++) {
-                            const uint32_t o_tm = tmem + lane_off + C::O_COL + half * HD + OCH * t;
-                            if constexpr (OCH == 32) {
-                                uint32_t o[32];
-                                ptx::tmem_ld32(o_tm, o);
-                                ptx::tc_wait_ld();
+                    for (int t = 0; t < HD / OCH; t++) {
+                        const uint32_t o_tm = tmem + lane_off + C::O_COL + half * HD + OCH * t;
+                        if constexpr (OCH == 32) {
+                            uint32_t o[32];
+                            ptx::tmem_ld32(o_tm, o);
+                            ptx::tc_wait_ld();
 #pragma unroll
-                                for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                                ptx::tmem_st32(o_tm, o);
-                            } else {
-                                uint32_t o[16];
-                                ptx::tmem_ld16(o_tm, o);
-                                ptx::tc_wait_ld();
+                            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                            ptx::tmem_st32(o_tm, o);
+                        } else {
+                            uint32_t o[16];
+                            ptx::tmem_ld16(o_tm, o);
+                            ptx::tc_wait_ld();
 #pragma unroll
-                                for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                                ptx::tmem_st16(o_tm, o);
-                            }
+                            for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                            ptx::tmem_st16(o_tm, o);
                         }
-                        ptx::tc_wait_st();
                     }
                 }
+                ptx::tc_wait_st();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&p_full[j & 1]);
                 if (more && !collect_max(j + 1, pm)) return false;
@@ -505,6 +539,7 @@ __global__ void __maxnreg__(184)
                 ptx::tc_fence_after();
                 load_s(0, sA);
                 ptx::tc_wait_ld();
+                release_s(0);
                 const float pm = publish_max(0, sA);
                 ok = collect_max(0, pm);
             }
@@ -546,11 +581,9 @@ __global__ void __maxnreg__(184)
                             for (int i = 0; i < OCH; i += 8) {
                                 uint32_t w[4];
 #pragma unroll
-                                for (int k = 0; k < 4; k++) {
-                                    __half2 h = __floats2half2_rn(__uint_as_float(o[i + 2 * k]) * inv_l,
-                                                                  __uint_as_float(o[i + 2 * k + 1]) * inv_l);
-                                    w[k] = *reinterpret_cast<uint32_t*>(&h);
-                                }
+                                for (int k = 0; k < 4; k++)
+                                    w[k] = ptx::pack_half2(__uint_as_float(o[i + 2 * k]) * inv_l,
+                                                           __uint_as_float(o[i + 2 * k + 1]) * inv_l);
                                 *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + OCH * t + i) =
                                     make_uint4(w[0], w[1], w[2], w[3]);
                             }

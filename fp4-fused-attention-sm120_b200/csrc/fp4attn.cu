@@ -201,10 +201,22 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
 {
     using C = fp4attn::FwdCfg<D, BN>;
     auto kern = fp4attn::fp4_attention_fwd_kernel<D, BN, OutT, kScores, kPoly8>;
+    // The kernel re-splits its launch registers with setmaxnreg; refuse to
+    // launch unless the pool it was given covers the split.
+    static int launch_regs = -1;
+    if (launch_regs < 0) {
+        cudaFuncAttributes attr;
+        FP4_CUDA(cudaFuncGetAttributes(&attr, kern));
+        launch_regs = attr.numRegs;
+    }
+    if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::kCtlRegs + 256 * fp4attn::kSmRegs ||
+        launch_regs > fp4attn::kLaunchRegs)
+        return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
+                    launch_regs, fp4attn::kLaunchRegs);
     FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
     dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
-    kern<<<grid, 320, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }

@@ -188,6 +188,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         : "memory");
 }
 
+// Warpgroup-wide register reallocation (all 4 warps of the warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Named barrier over `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)
 {
