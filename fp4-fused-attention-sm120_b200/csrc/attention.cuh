@@ -417,40 +417,41 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
             }
         } else {
-            uint32_t sA[NT][32], sB[NT][32];
-            float alpha = 1.f;
-            bool rescale = false;
-            // Mask missing keys, reduce this half's row max, publish it to the
-            // partner warp (slot and barrier alternate with tile parity).
-            auto publish_max = [&](int j, uint32_t (&buf)[NT][32]) -> float {
-                const int valid = args.seq_k - j * BN - half * HC;
-                if (valid < HC) {
+            // Each warp loads the whole S_j row (all BN columns) to form the
+            // row max itself -- the partner warp computes the same max from the
+            // same values, so the halves never wait on each other -- and then
+            // exponentiates only its own half of the columns.
+            constexpr int NF = BN / 32;            // 32-column chunks of a full S row
+            for (int j = 0; j < nk; j++) {
+                if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t sr[NF][32];
+                {
+                    const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN;
 #pragma unroll
-                    for (int t = 0; t < NT; t++)
+                    for (int t = 0; t < NF; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
+                }
+                ptx::tc_wait_ld();
+                release_s(j);
+                const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+                if (valid < BN) {
+#pragma unroll
+                    for (int t = 0; t < NF; t++)
 #pragma unroll
                         for (int i = 0; i < 32; i++)
-                            if (32 * t + i >= valid) buf[t][i] = __float_as_uint(-INFINITY);
+                            if (32 * t + i >= valid) sr[t][i] = __float_as_uint(-INFINITY);
                 }
                 float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int t = 0; t < NT; t++)
+                for (int t = 0; t < NF; t++)
 #pragma unroll
                     for (int i = 0; i < 32; i += 2)
                         mx4[(i >> 1) & 3] =
-                            ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(buf[t][i]), __uint_as_float(buf[t][i + 1]));
-                const float pm = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
-                red[((j & 1) * 2 + half) * 128 + row] = pm;
-                ptx::mbar_arrive(&xchg[(wq * 2 + half) * 2 + (j & 1)]);
-                return pm;
-            };
-            // Collect the partner's partial max and update the running max.
-            auto collect_max = [&](int j, float pm) -> bool {
-                if (!wait_phase(&xchg[(wq * 2 + (1 - half)) * 2 + (j & 1)], (j >> 1) & 1, wctx, kSiteXchg))
-                    return false;
-                const float mx = fmaxf(pm, red[((j & 1) * 2 + (1 - half)) * 128 + row]);
+                            ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[t][i]), __uint_as_float(sr[t][i + 1]));
+                const float mx = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
                 const float m_new = fmaxf(m, mx * c);
-                alpha = 1.f;
-                rescale = false;
+                float alpha = 1.f;
+                bool rescale = false;
                 if (j == 0) {
                     m = m_new;
                 } else if (m_new > m + 8.0f) {
@@ -458,48 +459,37 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     m = m_new;
                     rescale = true;
                 }
-                return true;
-            };
-            // One pipelined step: S_j (in cur) becomes P_j while S_{j+1} loads
-            // into nxt; S_{j+1}'s partial max is published halfway through the
-            // exponentials and collected after P_j has been handed to the MMA.
-            auto step = [&](int j, uint32_t (&cur)[NT][32], uint32_t (&nxt)[NT][32]) -> bool {
-                const bool more = j + 1 < nk;
-                if (more) {
-                    if (!wait_phase(&s_full[(j + 1) & 1], ((j + 1) >> 1) & 1, wctx, kSiteSFull)) return false;
-                    ptx::tc_fence_after();
-                    load_s(j + 1, nxt);
-                }
                 float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                 const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
                 uint32_t pk[NT][16];
-                float pm = 0.f;
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
+                // Exponentials of one 32-column chunk (indices stay compile-time
+                // so the row stays in registers).
+                auto exps_chunk = [&](const uint32_t (&src)[32], uint32_t (&dst)[16]) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        const float2 x =
-                            ptx::ffma2(make_float2(__uint_as_float(cur[t][i]), __uint_as_float(cur[t][i + 1])), c2, nm2);
+                        const float2 x = ptx::ffma2(make_float2(__uint_as_float(src[i]), __uint_as_float(src[i + 1])), c2, nm2);
                         // kPoly8 of every 8 column pairs take 2^x on the FMA pipe,
                         // the rest on MUFU, so both pipes share the exponentials.
                         const float2 p = ((i >> 1) & 7) < kPoly8
                                              ? ptx::exp2_poly3(x)
                                              : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
                         sum2[(i >> 1) & 1] = ptx::fadd2(sum2[(i >> 1) & 1], p);
-                        pk[t][i / 2] = ptx::pack_half2(p.x, p.y);
+                        dst[i / 2] = ptx::pack_half2(p.x, p.y);
                     }
-                    if (more && t == (NT - 1) / 2) {
-                        ptx::tc_wait_ld();
-                        release_s(j + 1);
-                        pm = publish_max(j + 1, nxt);
-                    }
+                };
+                if (half == 0) {
+#pragma unroll
+                    for (int t = 0; t < NT; t++) exps_chunk(sr[t], pk[t]);
+                } else {
+#pragma unroll
+                    for (int t = 0; t < NT; t++) exps_chunk(sr[NT + t], pk[t]);
                 }
                 l = l * alpha + ((sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y));
                 if (j > 0) {
                     // PV_{j-1} must be done: it reads the P columns this step
                     // overwrites, and O is rescaled below (waiting every phase
                     // also keeps this barrier's parity unambiguous).
-                    if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) return false;
+                    if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
                     ptx::tc_fence_after();
                 }
                 const uint32_t p_tm = tmem + lane_off + C::P_COL + half * (HC / 2);
@@ -529,23 +519,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 ptx::tc_wait_st();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&p_full[j & 1]);
-                if (more && !collect_max(j + 1, pm)) return false;
-                return true;
-            };
-            // prologue: S_0 and its row max
-            if (!wait_phase(&s_full[0], 0, wctx, kSiteSFull)) {
-                ok = false;
-            } else {
-                ptx::tc_fence_after();
-                load_s(0, sA);
-                ptx::tc_wait_ld();
-                release_s(0);
-                const float pm = publish_max(0, sA);
-                ok = collect_max(0, pm);
-            }
-            for (int j = 0; ok && j < nk; j += 2) {
-                if (!step(j, sA, sB)) { ok = false; break; }
-                if (j + 1 < nk && !step(j + 1, sB, sA)) { ok = false; break; }
             }
         }
         if (!kScores && ok) {
