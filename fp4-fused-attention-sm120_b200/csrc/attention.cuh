@@ -8,20 +8,21 @@
 //
 //   warp 0      TMA producer: Q tile once, then K tiles (codes + scale tiles)
 //               and V tiles through KST/VST-stage mbarrier rings.
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T with
-//               tcgen05.mma kind::mxf4 block_scale (scales in TMEM, copied with
-//               tcgen05.cp), and O += P_j V_j with tcgen05.mma kind::f16 whose
-//               A operand (P) is read from TMEM.  S is double-buffered and P
-//               has its own columns, so S_{j+2} is issued as soon as the
-//               softmax has loaded S_j -- the tensor cores run ahead of the
-//               softmax instead of waiting behind P.V.
-//   warps 2-3   idle (they complete the control warpgroup for setmaxnreg)
+//   warp 1      S issuer (one thread): S_j = Q K_j^T with tcgen05.mma
+//               kind::mxf4 block_scale (scales in TMEM, copied with
+//               tcgen05.cp).  S is double-buffered: S_{j+2} is issued when the
+//               softmax has finished step j, a whole step before it is needed.
+//   warp 2      P.V issuer (one thread): O += P_j V_j with tcgen05.mma
+//               kind::f16 whose A operand (P) is read from its own TMEM
+//               columns; on its own warp so it is issued as soon as P_j is
+//               ready (tcgen05 issue shares each sub-partition's queue with the
+//               softmax's MUFU traffic, so one thread issuing both is slow).
+//   warp 3      idle (completes the control warpgroup for setmaxnreg)
 //   warps 4-11  two softmax warpgroups; thread = query row = TMEM lane, and
 //               each warpgroup owns half of the S_j columns (and half of O's).
-//               Software-pipelined over K tiles: the TMEM load of S_{j+1} and
-//               its partial row max (exchanged with the partner warp through
-//               shared memory and an mbarrier) overlap the exponentials of
-//               S_j.  Online max/sum in FP32 (log2 domain), P_j stored as FP16
+//               Each warp loads the whole S_j row and forms the row max itself
+//               (its partner computes the same value), so the two halves never
+//               wait on each other.  Online max/sum in FP32 (log2 domain), P_j stored as FP16
 //               with tcgen05.st, lazy O rescale (only when the row max grows
 //               by more than 2^8), final O / l for its half of the columns.
 //
@@ -84,12 +85,10 @@ struct FwdCfg {
     static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
     static constexpr int OFF_V = align1k(OFF_KSF + KST * KSF_BYTES);
     static constexpr int V_STRIDE = align1k(V_BYTES);
-    static constexpr int OFF_RED = OFF_V + VST * V_STRIDE;   // [2 parity][2 halves][128 rows] f32 row maxima
-    static constexpr int OFF_REDL = OFF_RED + 2 * 2 * 128 * 4; // [2 halves][128 rows] f32 row sums
+    static constexpr int OFF_REDL = OFF_V + VST * V_STRIDE;    // [2 halves][128 rows] f32 row sums
     static constexpr int OFF_BAR = OFF_REDL + 2 * 128 * 4;
-    // q_full, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done, drain,
-    // and the row-max exchange barriers xchg[4 quarters][2 halves][2 parities]
-    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 2 + 1 + 1 + 16;
+    // q_full, K ring, V ring, s_full[2], p_full[2], pv_done, drain
+    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
 };
 
@@ -113,8 +112,6 @@ enum WaitSite : int {
     kSitePFull,
     kSitePvDone,
     kSiteDrain,
-    kSiteXchg,
-    kSiteSFree,
 };
 
 struct WaitCtx {
@@ -199,11 +196,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint64_t* v_full = k_empty + C::KST;
     uint64_t* v_empty = v_full + C::VST;
     uint64_t* s_full = v_empty + C::VST;  // S_j computed (tcgen05.commit)
-    uint64_t* s_free = s_full + 2;        // S_j loaded by all 256 softmax threads
-    uint64_t* p_full = s_free + 2;        // P_j stored and O rescaled (256 threads)
+    uint64_t* p_full = s_full + 2;        // step j done: S_j read, P_j stored, O rescaled (256 threads)
     uint64_t* pv_done = p_full + 2;       // O += P_j V_j complete (tcgen05.commit)
     uint64_t* drain_bar = pv_done + 1;
-    uint64_t* xchg = drain_bar + 1;
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
@@ -225,12 +220,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         for (int i = 0; i < 2; i++) {
             ptx::mbar_init(&s_full[i], 1);
-            ptx::mbar_init(&s_free[i], 256);
             ptx::mbar_init(&p_full[i], 256);
         }
         ptx::mbar_init(pv_done, 1);
-        ptx::mbar_init(drain_bar, 1);
-        for (int i = 0; i < 16; i++) ptx::mbar_init(&xchg[i], 32);
+        ptx::mbar_init(drain_bar, 2);  // one commit from each MMA issuer
         abort_sh = 0;
         ptx::fence_mbar_init();
     }
@@ -295,17 +288,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             __syncwarp();
         } else if (warp == 1) {
-            // -------------------------------------------------------- MMA issuer
+            // -------------------------------------------------------- S = Q K^T issuer
             if (lane == 0) {
                 constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::CW);
-                constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
                 // Descriptors are built once; per MMA only the 16-byte-unit start
                 // address in the low bits moves.
                 const uint64_t qdesc0 = ptx::make_sdesc(ptx::smem_u32(sQ), 16, 8 * C::CW, qk_layout);
                 const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::CW, qk_layout);
-                const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
                 const uint64_t sfdesc0 = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
-                constexpr uint32_t idesc_pv = ptx::idesc_f16(128, D, true);
                 bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
                 if (ok) {
                     ptx::tc_fence_after();
@@ -342,28 +332,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 };
                 if (ok) ok = issue_s(0);
                 if (ok && nk > 1) ok = issue_s(1);
-                for (int j = 0; ok && j < nk; j++) {
-                    // S_{j+2} reuses S_j's buffer as soon as the softmax has read S_j.
-                    if (j + 2 < nk) {
-                        if (!wait_phase(&s_free[j & 1], (j >> 1) & 1, wctx, kSiteSFree)) break;
-                        ptx::tc_fence_after();
-                        if (!issue_s(j + 2)) break;
-                    }
-                    if (kScores) continue;
+                // S_{j+2} reuses S_j's buffer once the softmax is done with step j
+                // (p_full[j]); it is needed only a whole step later.
+                for (int j = 0; ok && j + 2 < nk; j++) {
                     if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
-                    const int vs = j % C::VST;
-                    if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
                     ptx::tc_fence_after();
-                    const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
-#pragma unroll
-                    for (int kk = 0; kk < BN / 16; kk++)
-                        ptx::mma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
-                                        vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
-                                        (j > 0 || kk > 0) ? 1u : 0u);
-                    ptx::tc_commit(&v_empty[vs]);
-                    ptx::tc_commit(pv_done);
+                    if (!issue_s(j + 2)) break;
                 }
                 // Drain every tcgen05 op this thread issued before TMEM is freed.
+                ptx::tc_commit(drain_bar);
+                drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+            }
+            __syncwarp();
+        } else if (warp == 2) {
+            // -------------------------------------------------------- O += P V issuer
+            // On its own warp (and SM sub-partition), so P.V is issued the moment
+            // P_j is ready instead of queueing behind the S issue.
+            if (lane == 0) {
+                if (!kScores) {
+                    constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
+                    const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
+                    constexpr uint32_t idesc_pv = ptx::idesc_f16(128, D, true);
+                    for (int j = 0; j < nk; j++) {
+                        if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
+                        const int vs = j % C::VST;
+                        if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
+                        ptx::tc_fence_after();
+                        const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
+#pragma unroll
+                        for (int kk = 0; kk < BN / 16; kk++)
+                            ptx::mma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
+                                            vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
+                                            (j > 0 || kk > 0) ? 1u : 0u);
+                        ptx::tc_commit(&v_empty[vs]);
+                        ptx::tc_commit(pv_done);
+                    }
+                }
                 ptx::tc_commit(drain_bar);
                 drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
             }
@@ -380,7 +384,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int wq = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = wq * 32 + lane;            // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-        float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
         float* red_l = reinterpret_cast<float*>(smem + C::OFF_REDL);
         const float c = args.scale_log2;
         float m = -INFINITY, l = 0.f;
@@ -390,11 +393,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int t = 0; t < NT; t++) ptx::tmem_ld32(s_tm + 32 * t, buf[t]);
         };
-        // After the loads of S_j have completed: let the MMA reuse S_j's buffer.
-        auto release_s = [&](int j) {
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&s_free[j & 1]);
-        };
         if (kScores) {
             for (int j = 0; j < nk; j++) {
                 if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
@@ -402,7 +400,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 uint32_t sr[NT][32];
                 load_s(j, sr);
                 ptx::tc_wait_ld();
-                release_s(j);
                 const int valid = args.seq_k - j * BN - half * HC;
                 const int grow = q0 + row;
                 if (grow < args.seq_q) {
@@ -415,6 +412,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         for (int i = 0; i < 32; i++)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
                 }
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&p_full[j & 1]);  // done with S_j: its buffer may be reused
             }
         } else {
             // Each warp loads the whole S_j row (all BN columns) to form the
@@ -432,7 +431,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     for (int t = 0; t < NF; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
                 }
                 ptx::tc_wait_ld();
-                release_s(j);
                 const int valid = args.seq_k - j * BN;  // keys of this tile that exist
                 if (valid < BN) {
 #pragma unroll

@@ -180,7 +180,7 @@ int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slice
     a.ntiles = (seq + tile_rows - 1) / tile_rows;
     a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
     a.ocp_mode = ocp;
-    const int per_slice = a.ntiles * tile_rows * (a.padded_dim / 32) * 4;
+    const int per_slice = a.ntiles * tile_rows * (a.padded_dim / 32);
     const int gx = static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
     dim3 grid(gx, static_cast<unsigned>(slices));
     const InT* xp = static_cast<const InT*>(x);
@@ -400,7 +400,7 @@ int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8
     if (rc) return rc;
     if (rows == 0) return FP4ATTN_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int64_t work = rows * (head_dim / 32) * 4;
+    const int64_t work = rows * (head_dim / 32);
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
     if (dtype == FP4ATTN_F16)
         fp4attn::quantize_rowmajor_kernel<__half>

@@ -329,6 +329,14 @@ __device__ __forceinline__ float fmax3(float a, float b, float c)
     return d;
 }
 
+// max(a, |b|, |c|) in one instruction (a is already non-negative).
+__device__ __forceinline__ float fmax3_abs(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(fabsf(b)), "f"(fabsf(c)));
+    return d;
+}
+
 // Two floats to packed FP16 (round to nearest even), `lo` in the low half.
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
 {

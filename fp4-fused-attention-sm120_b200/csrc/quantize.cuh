@@ -2,11 +2,10 @@
 // reference's encode_fp4_e2m1 / compute_scale_ue8m0 (common.h:21-48) and its
 // quantisation loop (common.h:115-123, :160-168).
 //
-// Four lanes per 32-element block, eight elements per lane: the lanes reduce
-// max|x| with two shuffles, form the scale byte, and each writes 4 bytes of
-// packed codes (element 2i in the low nibble); lane 0 of the group writes the
-// scale byte.  The kernel is HBM-bound: 2 (or 4) bytes in and 0.53 bytes out
-// per element.
+// One lane per 32-element block: it reads the block with 16-byte loads, forms
+// the scale byte once, and writes 16 bytes of packed codes (element 2i in the
+// low nibble) plus the scale byte.  The kernel is HBM-bound: 2 (or 4) bytes in
+// and 0.53 bytes out per element.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -90,81 +89,95 @@ __device__ __forceinline__ void load8<float>(const float* src, float (&v)[8])
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// One lane's share of a 32-element block: the block maximum is reduced over
-// the 4 lanes of the group (all 32 lanes of the warp must call this), then the
-// reference scale byte is formed and this lane's 8 elements are encoded
-// (the common.h:118-122 loop: x / exp2f(scale - 127), encoded) into 4 bytes.
+// One lane per 32-element block: the whole block (64 B of FP16 or 128 B of
+// FP32) is read with 16-byte loads and reduced to max|x| with 3-input max
+// instructions; the reference scale byte is formed and the block is encoded
+// (the common.h:118-122 loop: x / exp2f(scale - 127), encoded) into 16 bytes.
 //
 // Encoding uses the hardware E2M1 conversion, which rounds to nearest with
 // ties to even and saturates at 6; the reference rounds ties up (away from
 // zero).  The two differ only at exact ties (|q| = 0.25, 1.25, 2.5, 5), at
 // -0.0 (the reference gives code 0) and at NaN (code 0).
-//  * kFromHalf (values came from FP16, so q has at most 11 significant bits):
-//    q * (1 + 2^-12) + 0 moves every exact tie above its threshold and no
-//    other value across one (a non-tie is at least 2^-11 relative away from
-//    any threshold), and turns -0.0 into +0.0; only a NaN in the block (seen
-//    through the block sum) takes the exact path.
-//  * FP32 input: a lane whose values include a possible tie (21 low mantissa
-//    bits zero), -0.0 or NaN redoes its 8 elements with the exact encoder.
-template <bool kFromHalf>
-__device__ __forceinline__ uint32_t quantize8(const float (&v)[8], int ocp_mode, uint32_t& packed)
+//  * FP16 input (q then has at most 11 significant bits): q * (1 + 2^-12) + 0
+//    moves every exact tie above its threshold and no other value across one
+//    (a non-tie is at least 2^-11 relative away from any threshold), and
+//    turns -0.0 into +0.0; only a NaN in the block (seen through the block
+//    sum) takes the exact encoder.
+//  * FP32 input: a block with a possible tie (21 low mantissa bits zero),
+//    -0.0 or NaN is redone with the exact encoder.
+template <typename InT>
+__device__ __forceinline__ uint32_t quantize32(const InT* __restrict__ src, int ocp_mode, uint4& packed)
 {
-    float amax = 0.f;
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float a = fabsf(v[i]);
-        amax = a > amax ? a : amax;  // NaN never wins, as in common.h:44
-    }
+    for (int k = 0; k < 4; k++) {
+        float t[8];
+        load8<InT>(src + 8 * k, t);
 #pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-        const float other = __shfl_xor_sync(0xffffffffu, amax, o);
-        amax = other > amax ? other : amax;
+        for (int i = 0; i < 8; i++) v[8 * k + i] = t[i];
     }
+    float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        m0 = ptx::fmax3_abs(m0, v[i], v[i + 1]);
+        m1 = ptx::fmax3_abs(m1, v[i + 2], v[i + 3]);
+        m2 = ptx::fmax3_abs(m2, v[i + 4], v[i + 5]);
+        m3 = ptx::fmax3_abs(m3, v[i + 6], v[i + 7]);
+    }
+    const float amax = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));  // NaN never wins, as in common.h:44
     const uint32_t sb = scale_byte(amax, ocp_mode);
     const int s = static_cast<int>(sb) - 127;
-    uint32_t w = 0u;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (s != 128) {  // s == 128: the reference divides by exp2f(128) = inf, every code is 0
-        const float inv = exact_pow2_neg(s);  // x * 2^-s rounds exactly like x / 2^s
-        float q[8];
-        bool exact = false;
-        if constexpr (kFromHalf) {
-            const float2 inv2 = make_float2(inv, inv);
+        const float inv = exact_pow2_neg(s);
+        const float2 inv2 = make_float2(inv, inv);
+        if constexpr (sizeof(InT) == 2) {
             const float2 nudge = make_float2(1.0f + 0x1p-12f, 1.0f + 0x1p-12f), zero = make_float2(0.f, 0.f);
             float2 sum = zero;
-            float qq[8];
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const float2 t = ptx::fmul2(make_float2(v[i], v[i + 1]), inv2);
-                qq[i] = t.x;
-                qq[i + 1] = t.y;
-                const float2 u = ptx::ffma2(t, nudge, zero);
-                q[i] = u.x;
-                q[i + 1] = u.y;
-                sum = ptx::fadd2(sum, make_float2(v[i], v[i + 1]));
+            for (int k = 0; k < 4; k++) {
+                float q[8];
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    const float2 u = ptx::ffma2(ptx::fmul2(make_float2(v[8 * k + i], v[8 * k + i + 1]), inv2), nudge, zero);
+                    q[i] = u.x;
+                    q[i + 1] = u.y;
+                    sum = ptx::fadd2(sum, make_float2(v[8 * k + i], v[8 * k + i + 1]));
+                }
+                w[k] = ptx::cvt_e2m1x8(q);
             }
-            w = ptx::cvt_e2m1x8(q);
-            if (isnan(sum.x + sum.y)) {
-                w = 0u;
+            if (isnan(sum.x + sum.y)) {  // a NaN in the block: exact encoder
 #pragma unroll
-                for (int i = 0; i < 8; i++) w |= encode_e2m1(qq[i]) << (4 * i);
+                for (int k = 0; k < 4; k++) {
+                    w[k] = 0u;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) w[k] |= encode_e2m1(v[8 * k + i] * inv) << (4 * i);
+                }
             }
         } else {
+            bool exact = false;
 #pragma unroll
-            for (int i = 0; i < 8; i++) q[i] = v[i] * inv;
-            w = ptx::cvt_e2m1x8(q);
+            for (int k = 0; k < 4; k++) {
+                float q[8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const uint32_t b = __float_as_uint(q[i]);
-                exact |= ((b << 11) == 0u && b != 0u) || ((b & 0x7FFFFFFFu) > 0x7F800000u);
+                for (int i = 0; i < 8; i++) {
+                    q[i] = v[8 * k + i] * inv;
+                    const uint32_t b = __float_as_uint(q[i]);
+                    exact |= ((b << 11) == 0u && b != 0u) || ((b & 0x7FFFFFFFu) > 0x7F800000u);
+                }
+                w[k] = ptx::cvt_e2m1x8(q);
             }
             if (exact) {
-                w = 0u;
 #pragma unroll
-                for (int i = 0; i < 8; i++) w |= encode_e2m1(q[i]) << (4 * i);
+                for (int k = 0; k < 4; k++) {
+                    w[k] = 0u;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) w[k] |= encode_e2m1(v[8 * k + i] * inv) << (4 * i);
+                }
             }
         }
     }
-    packed = w;
+    packed = make_uint4(w[0], w[1], w[2], w[3]);
     return sb;
 }
 
@@ -207,30 +220,25 @@ __global__ void __launch_bounds__(256) quantize_tiles_kernel(const InT* __restri
                                                              uint8_t* __restrict__ sf, QuantTileArgs a)
 {
     const int seq_pad = a.ntiles * a.tile_rows;
-    const int total = seq_pad * kNB * 4;  // lanes per slice; a multiple of 32
+    const int total = seq_pad * kNB;  // blocks of 32 in this slice (padded rows included)
     const int64_t slice = blockIdx.y;
     const InT* xs = x + slice * a.seq * a.head_dim;
     uint8_t* cs = codes + slice * a.seq * (kNB * 16);
     uint8_t* fs = sf + slice * a.ntiles * a.sf_tile_bytes;
-    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
-        const int sub = idx & 3;
-        const int blk = idx >> 2;
+    for (int blk = blockIdx.x * blockDim.x + threadIdx.x; blk < total; blk += gridDim.x * blockDim.x) {
         const int b = blk % kNB;
         const int r = blk / kNB;
-        const bool real = r < a.seq;
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const bool has_data = real && b * 32 < a.head_dim;
-        if (has_data) load8<InT>(xs + static_cast<int64_t>(r) * a.head_dim + b * 32 + sub * 8, v);
-        uint32_t packed;
-        uint32_t sb = quantize8<sizeof(InT) == 2>(v, a.ocp_mode, packed);
-        if (!has_data) sb = 127u;
-        if (sb == 255u) sb = 254u;
-        if (real) *reinterpret_cast<uint32_t*>(cs + static_cast<int64_t>(r) * (kNB * 16) + b * 16 + sub * 4) = packed;
-        if (sub == 0) {
-            const int tile = r >> a.tile_shift, rr = r & (a.tile_rows - 1);
-            fs[static_cast<int64_t>(tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] =
-                static_cast<uint8_t>(sb);
+        uint32_t sb = 127u;
+        if (r < a.seq) {
+            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+            if (b * 32 < a.head_dim) {
+                sb = quantize32<InT>(xs + static_cast<int64_t>(r) * a.head_dim + b * 32, a.ocp_mode, packed);
+                if (sb == 255u) sb = 254u;
+            }
+            *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (kNB * 16) + b * 16) = packed;
         }
+        const int tile = r >> a.tile_shift, rr = r & (a.tile_rows - 1);
+        fs[static_cast<int64_t>(tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] = static_cast<uint8_t>(sb);
     }
 }
 
@@ -241,21 +249,13 @@ __global__ void __launch_bounds__(256) quantize_rowmajor_kernel(const InT* __res
                                                                 uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
                                                                 int ocp_mode)
 {
-    const int64_t total = rows * (head_dim / 32) * 4;
-    const int lane = threadIdx.x & 31;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t base = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) & ~int64_t(31); base < total;
-         base += stride) {
-        const int64_t idx = base + lane;
-        const bool active = idx < total;
-        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (active) load8<InT>(x + idx * 8, v);
-        uint32_t packed;
-        const uint32_t sb = quantize8<sizeof(InT) == 2>(v, ocp_mode, packed);
-        if (active) {
-            *reinterpret_cast<uint32_t*>(codes + idx * 4) = packed;
-            if ((idx & 3) == 0) sf[idx >> 2] = static_cast<uint8_t>(sb);
-        }
+    const int64_t total = rows * (head_dim / 32);
+    for (int64_t blk = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; blk < total;
+         blk += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        uint4 packed;
+        const uint32_t sb = quantize32<InT>(x + blk * 32, ocp_mode, packed);
+        *reinterpret_cast<uint4*>(codes + blk * 16) = packed;
+        sf[blk] = static_cast<uint8_t>(sb);
     }
 }
 
