@@ -102,3 +102,20 @@ def test_quantize_rejects_bad_arguments(fa):
 def test_python_wrapper_errors_carry_detail(fa):
     err = fa.Fp4AttnError(fa.EINVAL, "fp4attn_forward", "null tensor pointer")
     assert "invalid argument" in str(err) and "null tensor pointer" in str(err)
+
+
+def test_cpp_launcher_header_compiles_and_links(tmp_path, fa):
+    """The reference-order C++ launcher (include/fp4_fused_attention.h)
+    compiles against the CUDA headers and links against libfp4attn.so."""
+    src = tmp_path / "use.cpp"
+    src.write_text(
+        '#include "fp4_fused_attention.h"\n'
+        "int run(const float* q, const float* k, float* o, const float* v) {\n"
+        "  return fused_fp4_attention_launch<128>(q, k, o, v, 64, 128, 32);\n}\n"
+        "int run16(const __half* q, const __half* k, __half* o, const __half* v) {\n"
+        "  return fused_fp4_attention_launch<64>(q, k, o, v, 4096, 4096, 32, 2, nullptr);\n}\n"
+        "int main() { return 0; }\n")
+    libdir = str(fa.lib_path().parent)
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include",
+                    str(src), "-L", libdir, "-lfp4attn", "-L", "/usr/local/cuda/lib64", "-lcudart",
+                    f"-Wl,-rpath,{libdir}", "-o", str(tmp_path / "use")], check=True)
