@@ -382,6 +382,12 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
 
 }  // namespace
 
+namespace fp4attn {
+// Lets other translation units of the library report a detail through
+// fp4attn_last_error().
+void set_error_detail(const char* msg) { g_last_error = msg; }
+}  // namespace fp4attn
+
 extern "C" {
 
 int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8_t* codes, uint8_t* scales,

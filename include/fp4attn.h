@@ -116,6 +116,21 @@ int fp4attn_prepare(const void* Q, const void* K, const void* V, int in_dtype, i
 int fp4attn_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q, int seq_k,
                    int head_dim, float softmax_scale, const void* workspace, size_t workspace_bytes, void* stream);
 
+/* fp4attn_forward for callers that cannot allocate device memory (code running
+ * during CUDA graph capture, runtimes that own all device memory, loops that
+ * must not block on an allocation): the same computation, with the workspace
+ * taken from a 64 MiB scratch array the library holds on each device from the
+ * first call (or from context creation under CUDA_MODULE_LOADING=EAGER) until
+ * the process exits.  Problems whose fp4attn_workspace_size exceeds 64 MiB are
+ * rejected with FP4ATTN_EWORKSPACE.  The first call on a device looks up the
+ * scratch's device address; make it before any stream capture.  All calls on a
+ * device share the scratch: calls that may overlap on the GPU must be
+ * serialised by the caller.  No counterpart in the reference (its kernel keeps
+ * everything in shared memory and needs no workspace). */
+int fp4attn_forward_noalloc(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                            int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                            int scale_mode, void* stream);
+
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
  * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
  * power-of-two scales are exact, S is checkable bit for bit.
