@@ -95,9 +95,10 @@ struct FwdCfg {
 struct FwdArgs {
     int seq_q, seq_k;
     int nq_tiles, nk_tiles;
+    int q_sf_tiles;            // 128-row scale tiles per slice in q_sf (>= nq_tiles)
     float scale_log2;          // softmax_scale * log2(e)
     void* out;                 // [slices, seq_q, D] (attention) or [slices, seq_q, seq_k] FP32 (scores)
-    const uint8_t* q_sf;       // [slices][nq_tiles][QSF_BYTES]
+    const uint8_t* q_sf;       // [slices][q_sf_tiles][QSF_BYTES]
     const uint8_t* k_sf;       // [slices][nk_tiles][KSF_BYTES]
     unsigned long long timeout_ns;
 };
@@ -112,6 +113,7 @@ enum WaitSite : int {
     kSitePFull,
     kSitePvDone,
     kSiteDrain,
+    kSiteSFree,
 };
 
 struct WaitCtx {
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
                 for (int c = 0; c < C::NCH; c++)
                     ptx::tma_load_3d(sQ + c * C::BM * C::CW, &tm_q, q_full, c * C::CW, q0, slice);
-                ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.nq_tiles + qt) * C::QSF_BYTES,
+                ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + qt) * C::QSF_BYTES,
                                C::QSF_BYTES, q_full);
                 int k_issued = 0, v_issued = 0;
                 for (int j = 0; j < nk; j++) {

@@ -1,0 +1,467 @@
+// attention_pair.cuh -- FP4 fused attention forward, two query tiles per CTA,
+// for head_dim <= 128 on sm_100a.
+//
+// Same computation as fp4_attention_fwd_kernel (attention.cuh) -- the
+// reference kernel fused_fp4_attention (common.h:68-328) with Q, K in
+// E2M1 + UE8M0 and V, P in FP16 -- with a different division of the work.
+// Each CTA owns 256 query rows as two independent 128-row tiles T0, T1 and
+// walks the keys in 64-row tiles:
+//
+//   warp 0      TMA producer: both Q tiles once, then K (codes + scale tile)
+//               and V tiles through KST/VST-stage mbarrier rings.
+//   warp 1      S issuer: S_t = Q_t K_j^T (tcgen05.mma kind::mxf4 block_scale,
+//               M128 N64) for t = 0, 1; S_t for step j+1 is issued as soon
+//               as softmax warpgroup t has copied S_t of step j to registers.
+//   warp 2      P.V issuer: O_t += P_t [V_j | 1] (tcgen05.mma kind::f16, P read
+//               from TMEM) as soon as softmax warpgroup t has stored P_t.  Each
+//               V stage carries, after V's own swizzled chunks, one constant
+//               chunk whose first 16 columns are 1.0, and the MMA runs 16
+//               columns wider than V: O_t's extra columns accumulate the row
+//               sum l = sum_j rowsum(P_t) on the tensor core (from the same
+//               FP16 P that multiplies V), rescaled together with O.
+//   warp 3      idle (completes the control warpgroup for setmaxnreg)
+//   warps 4-7   softmax of tile T0; warps 8-11 softmax of tile T1.  Thread =
+//               query row = TMEM lane; each thread owns its whole 64-column S
+//               row, so the row max, the exponentials, the row sum, the lazy O
+//               rescale and the final O / l need no exchange between warps.
+//               Warps 4+k and 8+k share SM sub-partition k and its MUFU unit;
+//               a pair of named barriers makes them take turns at the
+//               exponentials (T0, T1, T0, ...), so that one warp's MUFU-bound
+//               exponentials overlap the other's TMEM loads, row max and waits
+//               instead of both fighting for MUFU at once.
+//
+// TMEM columns (512 allocated): S_0 [0,64), S_1 [64,128), O_0, O_1 (NPV each:
+// V's padded width + 16 columns holding l), P_0, P_1 (32 each: 64 FP16
+// pairs), the two Q scale column groups, then KST groups of K scale columns.
+//
+// Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
+// FP4ATTN_ETIMEOUT, all roles leave their loops, in-flight copies and MMAs are
+// drained (bounded), TMEM is freed and the CTA returns.  Nothing traps.
+#pragma once
+
+#include "attention.cuh"
+
+namespace fp4attn {
+
+template <int D>
+struct PairCfg {
+    static constexpr int BM = 128;                          // rows per query tile (MMA M)
+    static constexpr int BN = 64;                           // keys per step
+    static constexpr int DP = (D + 63) / 64 * 64;           // head_dim padded to the MMA K step
+    static constexpr int QK_ROW = DP / 2;                   // bytes per packed code row
+    static constexpr int CW = QK_ROW;                       // swizzle chunk = whole row (32 or 64 B)
+    static constexpr int KSTEPS = DP / 64;                  // mxf4 MMAs per S tile
+    static constexpr int VCW = D == 32 ? 64 : 128;          // swizzle chunk of a V row (bytes)
+    static constexpr int VCH = (2 * D + VCW - 1) / VCW;     // V chunks (TMA boxes) per tile
+    static constexpr int L_COL = VCH * VCW / 2;             // O column holding the row sum l
+    static constexpr int NPV = L_COL + 16;                  // P.V MMA width: V chunks + the ones block
+    static constexpr int KST = 4;
+    static constexpr int VST = 4;
+    static_assert(D % 32 == 0 && D <= 128, "the paired kernel covers head_dim <= 128");
+    // TMEM
+    static constexpr int S_COL = 0;                         // + t * BN
+    static constexpr int O_COL = 2 * BN;                    // + t * NPV
+    static constexpr int P_COL = O_COL + 2 * NPV;           // + t * BN / 2
+    static constexpr int SFA_COL = P_COL + BN;              // + t * 4
+    static constexpr int SFB_COL = SFA_COL + 8;             // + stage * 4
+    static constexpr int TMEM_USED = SFB_COL + 4 * KST;
+    static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
+    // shared memory (offsets from a 1024-aligned base)
+    static constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+    static constexpr int Q_BYTES = BM * QK_ROW;             // one query tile
+    static constexpr int K_BYTES = BN * QK_ROW;
+    static constexpr int SF_BYTES = 512;                    // one scale atom (Q: 128 rows x 4, K: 64 rows x 8)
+    static constexpr int V_BYTES = VCH * BN * VCW;          // loaded by TMA; the ones chunk follows
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_QSF = align1k(OFF_Q + 2 * Q_BYTES);
+    static constexpr int OFF_K = align1k(OFF_QSF + 2 * SF_BYTES);
+    static constexpr int K_STRIDE = align1k(K_BYTES);
+    static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
+    static constexpr int OFF_V = align1k(OFF_KSF + KST * SF_BYTES);
+    static constexpr int V_STRIDE = align1k(V_BYTES + BN * VCW);
+    static constexpr int OFF_BAR = OFF_V + VST * V_STRIDE;
+    // q_full, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain
+    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 8 + 1;
+    static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
+};
+
+struct PairArgs {
+    int seq_q, seq_k;
+    int nk_tiles;
+    int q_sf_tiles;            // 128-row scale tiles per slice in q_sf (even)
+    float scale_log2;          // softmax_scale * log2(e)
+    void* out;                 // [slices, seq_q, D]
+    const uint8_t* q_sf;       // [slices][q_sf_tiles][512]
+    const uint8_t* k_sf;       // [slices][nk_tiles][512]
+    unsigned long long timeout_ns;
+};
+
+template <int D, typename OutT, int kPoly8, bool kTurns>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                              const __grid_constant__ CUtensorMap tm_v, const PairArgs args)
+{
+    using C = PairCfg<D>;
+    constexpr int BN = C::BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem + C::OFF_Q;
+    uint8_t* sQsf = smem + C::OFF_QSF;
+    uint8_t* sK = smem + C::OFF_K;
+    uint8_t* sKsf = smem + C::OFF_KSF;
+    uint8_t* sV = smem + C::OFF_V;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = k_full + C::KST;
+    uint64_t* v_full = k_empty + C::KST;
+    uint64_t* v_empty = v_full + C::VST;
+    uint64_t* s_full = v_empty + C::VST;  // [t] S_t computed (tcgen05.commit)
+    uint64_t* s_free = s_full + 2;        // [t] S_t copied to registers (128 threads)
+    uint64_t* p_full = s_free + 2;        // [t] P_t stored, O_t rescaled (128 threads)
+    uint64_t* pv_done = p_full + 2;       // [t] O_t += P_t V complete (tcgen05.commit)
+    uint64_t* drain_bar = pv_done + 2;
+
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int pair = blockIdx.x, slice = blockIdx.y;
+    const int q0 = pair * 2 * C::BM;
+    const int nk = args.nk_tiles;
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(q_full, 1);
+        for (int i = 0; i < C::KST; i++) {
+            ptx::mbar_init(&k_full[i], 1);
+            ptx::mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < C::VST; i++) {
+            ptx::mbar_init(&v_full[i], 1);
+            ptx::mbar_init(&v_empty[i], 1);
+        }
+        for (int t = 0; t < 2; t++) {
+            ptx::mbar_init(&s_full[t], 1);
+            ptx::mbar_init(&s_free[t], 128);
+            ptx::mbar_init(&p_full[t], 128);
+            ptx::mbar_init(&pv_done[t], 1);
+        }
+        ptx::mbar_init(drain_bar, 2);  // one commit from each MMA issuer
+        abort_sh = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&tm_q);
+        ptx::prefetch_tmap(&tm_k);
+        ptx::prefetch_tmap(&tm_v);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(&tmem_base_sh, 512);
+        ptx::tmem_relinquish();
+    }
+    {
+        // The ones chunk of every V stage: logical [BN rows][VCW bytes] FP16,
+        // 1.0 in columns 0..15, stored with the stage's swizzle (the 16-byte
+        // unit index XORed with address bits 7 and up).
+        constexpr uint32_t kMask = C::VCW == 128 ? 7u : C::VCW == 64 ? 3u : 1u;
+        constexpr int kUnits = BN * C::VCW / 16;
+        for (int u = threadIdx.x; u < C::VST * kUnits; u += blockDim.x) {
+            const int stage = u / kUnits, o = (u % kUnits) * 16;
+            const int col16 = (o % C::VCW) / 16;  // 16-byte unit within the row: 8 FP16 columns
+            const uint32_t phys = static_cast<uint32_t>(o) ^ (((static_cast<uint32_t>(o) >> 7) & kMask) << 4);
+            const uint32_t one2 = 0x3C003C00u;    // two FP16 1.0
+            const uint4 val = col16 < 2 ? make_uint4(one2, one2, one2, one2) : make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(sV + stage * C::V_STRIDE + C::V_BYTES + phys) = val;
+        }
+        ptx::fence_proxy_async_smem();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const WaitCtx wctx{&abort_sh, args.timeout_ns};
+
+    if (warp < 4) {
+        ptx::setmaxnreg_dec<kCtlRegs>();
+        if (warp == 0) {
+            // -------------------------------------------------------- producer
+            if (lane == 0) {
+                ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
+#pragma unroll
+                for (int t = 0; t < 2; t++) {
+                    ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, q0 + t * C::BM, slice);
+                    ptx::bulk_load(sQsf + t * C::SF_BYTES,
+                                   args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + 2 * pair + t) * C::SF_BYTES,
+                                   C::SF_BYTES, q_full);
+                }
+                int k_issued = 0, v_issued = 0;
+                for (int j = 0; j < nk; j++) {
+                    const int ks = j % C::KST;
+                    if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::SF_BYTES);
+                    ptx::tma_load_3d(sK + ks * C::K_STRIDE, &tm_k, &k_full[ks], 0, j * BN, slice);
+                    ptx::bulk_load(sKsf + ks * C::SF_BYTES,
+                                   args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::SF_BYTES, C::SF_BYTES,
+                                   &k_full[ks]);
+                    k_issued = j + 1;
+                    const int vs = j % C::VST;
+                    if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+#pragma unroll
+                    for (int c = 0; c < C::VCH; c++)
+                        ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
+                                         c * (C::VCW / 2), j * BN, slice);
+                    v_issued = j + 1;
+                }
+                // Every load this thread issued must land before the CTA exits.
+                const unsigned long long drain_ns = 2ull * args.timeout_ns;
+                drain_phase(q_full, 0, drain_ns);
+                for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
+                    drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
+                for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
+                    drain_phase(&v_full[i % C::VST], (i / C::VST) & 1, drain_ns);
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            // -------------------------------------------------------- S_t = Q_t K^T issuer
+            if (lane == 0) {
+                constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::CW);
+                const uint64_t qdesc0 = ptx::make_sdesc(ptx::smem_u32(sQ), 16, 8 * C::CW, qk_layout);
+                const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::CW, qk_layout);
+                const uint64_t sfdesc0 = ptx::make_sdesc(ptx::smem_u32(sQsf), 0, 128, ptx::kSwizzleNone);
+                const uint64_t ksfdesc0 = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
+                bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
+                if (ok) {
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int t = 0; t < 2; t++)
+                        ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL + 4 * t,
+                                                  sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
+                }
+                for (int j = 0; ok && j < nk; j++) {
+                    const int ks = j % C::KST;
+                    if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) break;
+                    ptx::tc_fence_after();
+                    const uint32_t sfb = tmem + C::SFB_COL + 4 * ks;
+                    ptx::tc_cp_32x128b_warpx4(sfb, ksfdesc0 + static_cast<uint64_t>((ks * C::SF_BYTES) >> 4));
+                    const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
+#pragma unroll
+                    for (int t = 0; t < 2; t++) {
+                        // S_t's columns are free once warpgroup t holds step j-1 in registers.
+                        if (j > 0) {
+                            if (!wait_phase(&s_free[t], (j - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
+                            ptx::tc_fence_after();
+                        }
+#pragma unroll
+                        for (int kk = 0; kk < C::KSTEPS; kk++) {
+                            const uint32_t sf_id = 2u * (kk & 1);
+                            ptx::mma_mxf4(tmem + C::S_COL + t * BN,
+                                          qdesc0 + static_cast<uint64_t>((t * C::Q_BYTES + kk * 32) >> 4),
+                                          kdesc + static_cast<uint64_t>((kk * 32) >> 4),
+                                          ptx::idesc_mxf4(128, BN, sf_id, sf_id),
+                                          (tmem + C::SFA_COL + 4 * t) | (sf_id << 30), sfb | (sf_id << 30),
+                                          kk > 0 ? 1u : 0u);
+                        }
+                        ptx::tc_commit(&s_full[t]);
+                    }
+                    if (!ok) break;
+                    ptx::tc_commit(&k_empty[ks]);
+                }
+                // Drain every tcgen05 op this thread issued before TMEM is freed.
+                ptx::tc_commit(drain_bar);
+                drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+            }
+            __syncwarp();
+        } else if (warp == 2) {
+            // -------------------------------------------------------- O_t += P_t V issuer
+            if (lane == 0) {
+                constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
+                const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
+                constexpr uint32_t idesc_pv = ptx::idesc_f16(128, C::NPV, true);
+                bool ok = true;
+                for (int j = 0; ok && j < nk; j++) {
+                    const int vs = j % C::VST;
+                    if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
+                    const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
+#pragma unroll
+                    for (int t = 0; t < 2; t++) {
+                        if (!wait_phase(&p_full[t], j & 1, wctx, kSitePFull)) { ok = false; break; }
+                        ptx::tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < BN / 16; kk++)
+                            ptx::mma_f16_ts(tmem + C::O_COL + t * C::NPV, tmem + C::P_COL + t * (BN / 2) + kk * 8,
+                                            vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
+                                            (j > 0 || kk > 0) ? 1u : 0u);
+                        ptx::tc_commit(&pv_done[t]);
+                    }
+                    if (!ok) break;
+                    ptx::tc_commit(&v_empty[vs]);
+                }
+                ptx::tc_commit(drain_bar);
+                drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+            }
+            __syncwarp();
+        }
+    } else {
+        ptx::setmaxnreg_inc<kSmRegs>();
+        // ------------------------------------------------------------ softmax warpgroups
+        constexpr int NT = BN / 32;                // 32-column chunks of an S row
+        const int t = (warp - 4) / 4;              // query tile of this warpgroup
+        const int wq = warp & 3;                   // TMEM lane quarter this warp may access
+        const int row = wq * 32 + lane;            // query row within the tile
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t s_tm = tmem + lane_off + C::S_COL + t * BN;
+        const uint32_t o_tm = tmem + lane_off + C::O_COL + t * C::NPV;
+        const uint32_t p_tm = tmem + lane_off + C::P_COL + t * (BN / 2);
+        const float c = args.scale_log2;
+        float m = -INFINITY;
+        bool ok = true;
+        // Turn-taking at the exponentials: T0 waits on bar_mine = 1 + wq and
+        // signals 5 + wq, T1 the other way round.  Every bar.sync is matched by
+        // one bar.arrive of the partner; a warp that leaves the loop early
+        // arrives once more so the partner cannot block (the partner reaches a
+        // bounded wait, sees the abort flag and leaves, before its next sync).
+        // Waits are decided per warp (__all_sync) so barrier use stays uniform.
+        const uint32_t bar_mine = t == 0 ? 1 + wq : 5 + wq;
+        const uint32_t bar_other = t == 0 ? 5 + wq : 1 + wq;
+        if (kTurns && t == 1) ptx::named_bar_arrive(bar_other, 64);  // T0 goes first
+        for (int j = 0; j < nk; j++) {
+            if (!__all_sync(0xffffffffu, wait_phase(&s_full[t], j & 1, wctx, kSiteSFull))) { ok = false; break; }
+            ptx::tc_fence_after();
+            uint32_t sr[NT][32];
+#pragma unroll
+            for (int k = 0; k < NT; k++) ptx::tmem_ld32(s_tm + 32 * k, sr[k]);
+            ptx::tc_wait_ld();
+            // S_t is in registers: the issuer may compute the next step into it.
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&s_free[t]);
+            const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+            if (valid < BN) {
+#pragma unroll
+                for (int k = 0; k < NT; k++)
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
+            }
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int k = 0; k < NT; k++)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2)
+                    mx4[(i >> 1) & 3] =
+                        ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
+            const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (j == 0) {
+                m = m_new;
+            } else if (m_new > m + 8.0f) {
+                // Lazy rescale: O and l keep the old reference max until the
+                // row max has grown by more than 2^8.
+                alpha = ptx::ex2_approx(m - m_new);
+                m = m_new;
+                rescale = true;
+            }
+            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+            uint32_t pk[NT][16];
+            if (kTurns) ptx::named_bar_sync(bar_mine, 64);
+#pragma unroll
+            for (int k = 0; k < NT; k++)
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 x =
+                        ptx::ffma2(make_float2(__uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1])), c2, nm2);
+                    // kPoly8 of every 8 column pairs take 2^x on the FMA pipe,
+                    // the rest on MUFU, so both pipes share the exponentials.
+                    const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
+                                                             : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                    pk[k][i / 2] = ptx::pack_half2(p.x, p.y);
+                }
+            if (kTurns) ptx::named_bar_arrive(bar_other, 64);
+            if (j > 0) {
+                // PV_{j-1} must be done: it reads the P columns this step
+                // overwrites, and O is rescaled below.
+                if (!__all_sync(0xffffffffu, wait_phase(&pv_done[t], (j - 1) & 1, wctx, kSitePvDone))) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+            }
+#pragma unroll
+            for (int k = 0; k < NT; k++) ptx::tmem_st16(p_tm + 16 * k, pk[k]);
+            if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+                // O and its row-sum columns move to the new reference max.
+#pragma unroll 1
+                for (int k = 0; k < C::L_COL / 32; k++) {
+                    uint32_t o[32];
+                    ptx::tmem_ld32(o_tm + 32 * k, o);
+                    ptx::tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    ptx::tmem_st32(o_tm + 32 * k, o);
+                }
+                uint32_t o[16];
+                ptx::tmem_ld16(o_tm + C::L_COL, o);
+                ptx::tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                ptx::tmem_st16(o_tm + C::L_COL, o);
+            }
+            ptx::tc_wait_st();
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(&p_full[t]);
+        }
+        if (!kTurns) {
+        } else if (!ok) {
+            ptx::named_bar_arrive(bar_other, 64);
+        } else if (t == 0) {
+            ptx::named_bar_sync(bar_mine, 64);  // T1's last arrive: leave both barriers balanced
+        }
+        if (ok && __all_sync(0xffffffffu, wait_phase(&pv_done[t], (nk - 1) & 1, wctx, kSitePvDone))) {
+            ptx::tc_fence_after();
+            uint32_t lsum[16];
+            ptx::tmem_ld16(o_tm + C::L_COL, lsum);
+            ptx::tc_wait_ld();
+            const float inv_l = 1.0f / __uint_as_float(lsum[0]);
+            const int grow = q0 + t * C::BM + row;
+            OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D;
+#pragma unroll 1
+            for (int k = 0; k < D / 32; k++) {
+                uint32_t o[32];
+                ptx::tmem_ld32(o_tm + 32 * k, o);
+                ptx::tc_wait_ld();
+                if (grow < args.seq_q) {
+                    if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float4 v = make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
+                                                   __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+                            *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + 32 * k + i) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 8) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int q = 0; q < 4; q++)
+                                w[q] = ptx::pack_half2(__uint_as_float(o[i + 2 * q]) * inv_l,
+                                                       __uint_as_float(o[i + 2 * q + 1]) * inv_l);
+                            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + 32 * k + i) =
+                                make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace fp4attn

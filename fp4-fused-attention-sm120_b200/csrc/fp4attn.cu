@@ -15,7 +15,7 @@
 #include <string>
 
 #include "../../include/fp4attn.h"
-#include "attention.cuh"
+#include "attention_pair.cuh"
 #include "quantize.cuh"
 
 namespace {
@@ -49,7 +49,11 @@ bool supported_dim(int d)
     return false;
 }
 
-int block_n_for(int d) { return d == 256 ? 64 : 128; }
+// Keys per attention step: 64 (the two-query-tile kernel for head_dim <= 128,
+// and head_dim 256), except head_dim 160 (one query tile, 128 keys).
+int block_n_for(int d) { return d == 160 ? 128 : 64; }
+// The two-query-tile kernel covers head_dim <= 128.
+bool paired(int d) { return d <= 128; }
 int padded_dim(int d) { return (d + 63) / 64 * 64; }
 int sfa_atoms(int d) { return (padded_dim(d) + 127) / 128; }
 int sf_tile_bytes(int d, int tile_rows)
@@ -63,10 +67,18 @@ struct Workspace {
     size_t q_codes, k_codes, q_sf, k_sf, v16, total;
 };
 
+// 128-row Q scale tiles per slice: rounded up to whole pairs for the
+// two-query-tile kernel (the extra tile holds padding scales).
+int q_sf_tiles(int sq, int d)
+{
+    const int nq = (sq + 127) / 128;
+    return paired(d) ? (nq + 1) / 2 * 2 : nq;
+}
+
 Workspace plan_workspace(int64_t slices, int sq, int sk, int d, int in_dtype)
 {
     const int dp = padded_dim(d), bn = block_n_for(d);
-    const int64_t nq = (sq + 127) / 128, nk = (sk + bn - 1) / bn;
+    const int64_t nq = q_sf_tiles(sq, d), nk = (sk + bn - 1) / bn;
     Workspace w{};
     size_t off = 0;
     w.q_codes = off;
@@ -168,7 +180,7 @@ int grid_for(int64_t work, int per_block = 256)
 
 template <typename InT>
 int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slices, int seq, int d, int tile_rows,
-                       int ocp, cudaStream_t st)
+                       int ntiles, int ocp, cudaStream_t st)
 {
     fp4attn::QuantTileArgs a;
     a.slices = slices;
@@ -177,7 +189,7 @@ int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slice
     a.padded_dim = padded_dim(d);
     a.tile_rows = tile_rows;
     a.tile_shift = tile_rows == 128 ? 7 : 6;
-    a.ntiles = (seq + tile_rows - 1) / tile_rows;
+    a.ntiles = ntiles;
     a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
     a.ocp_mode = ocp;
     const int per_slice = a.ntiles * tile_rows * (a.padded_dim / 32);
@@ -232,29 +244,91 @@ int poly8_setting()
     return v;
 }
 
+// Whether the two query tiles' softmax warps take turns at the exponentials
+// (FP4ATTN_TURNS=1 selects it for the FP16-output D=128 kernel, for tuning).
+int turns_setting()
+{
+    static int v = [] {
+        const char* s = getenv("FP4ATTN_TURNS");
+        return s ? atoi(s) : -1;
+    }();
+    return v;
+}
+
 template <int D, int BN, typename OutT, bool kScores>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                int64_t slices, cudaStream_t st)
 {
-    if constexpr (D == 128 && !kScores && sizeof(OutT) == 2) {
+    return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
+}
+
+template <int D, typename OutT, int kPoly8, bool kTurns>
+int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
+                     int64_t slices, cudaStream_t st)
+{
+    using C = fp4attn::PairCfg<D>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kTurns>;
+    static int launch_regs = -1;
+    if (launch_regs < 0) {
+        cudaFuncAttributes attr;
+        FP4_CUDA(cudaFuncGetAttributes(&attr, kern));
+        launch_regs = attr.numRegs;
+    }
+    if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::kCtlRegs + 256 * fp4attn::kSmRegs ||
+        launch_regs > fp4attn::kLaunchRegs)
+        return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
+                    launch_regs, fp4attn::kLaunchRegs);
+    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
+    fp4attn::PairArgs a;
+    a.seq_q = fa.seq_q;
+    a.seq_k = fa.seq_k;
+    a.nk_tiles = fa.nk_tiles;
+    a.q_sf_tiles = fa.q_sf_tiles;
+    a.scale_log2 = fa.scale_log2;
+    a.out = fa.out;
+    a.q_sf = fa.q_sf;
+    a.k_sf = fa.k_sf;
+    a.timeout_ns = fa.timeout_ns;
+    dim3 grid(fa.q_sf_tiles / 2, static_cast<unsigned>(slices));
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    FP4_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+template <int D, typename OutT>
+int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
+                int64_t slices, cudaStream_t st)
+{
+    if constexpr (D == 128 && sizeof(OutT) == 2) {
+        const bool turns = turns_setting() == 1;
         switch (poly8_setting()) {
-            case 0: return launch_fwd_poly<D, BN, OutT, kScores, 0>(tq, tk, tv, a, slices, st);
-            case 2: return launch_fwd_poly<D, BN, OutT, kScores, 2>(tq, tk, tv, a, slices, st);
-            case 4: return launch_fwd_poly<D, BN, OutT, kScores, 4>(tq, tk, tv, a, slices, st);
-            default: break;
+            case 2: return turns ? launch_pair_poly<D, OutT, 2, true>(tq, tk, tv, a, slices, st)
+                                 : launch_pair_poly<D, OutT, 2, false>(tq, tk, tv, a, slices, st);
+            case 4: return turns ? launch_pair_poly<D, OutT, 4, true>(tq, tk, tv, a, slices, st)
+                                 : launch_pair_poly<D, OutT, 4, false>(tq, tk, tv, a, slices, st);
+            default:
+                if (turns) return launch_pair_poly<D, OutT, 3, true>(tq, tk, tv, a, slices, st);
+                break;
         }
     }
-    return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
+    return launch_pair_poly<D, OutT, 3, false>(tq, tk, tv, a, slices, st);
 }
 
 template <int D, bool kScores>
 int dispatch_out(int out_dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                  const fp4attn::FwdArgs& a, int64_t slices, cudaStream_t st)
 {
-    constexpr int BN = D == 256 ? 64 : 128;
-    if (kScores) return launch_fwd<D, BN, float, true>(tq, tk, tv, a, slices, st);
-    if (out_dtype == FP4ATTN_F32) return launch_fwd<D, BN, float, false>(tq, tk, tv, a, slices, st);
-    return launch_fwd<D, BN, __half, false>(tq, tk, tv, a, slices, st);
+    constexpr int BN = D == 160 ? 128 : 64;
+    if constexpr (kScores) {
+        return launch_fwd<D, BN, float, true>(tq, tk, tv, a, slices, st);
+    } else if constexpr (D <= 128) {
+        if (out_dtype == FP4ATTN_F32) return launch_pair<D, float>(tq, tk, tv, a, slices, st);
+        return launch_pair<D, __half>(tq, tk, tv, a, slices, st);
+    } else {
+        if (out_dtype == FP4ATTN_F32) return launch_fwd<D, BN, float, false>(tq, tk, tv, a, slices, st);
+        return launch_fwd<D, BN, __half, false>(tq, tk, tv, a, slices, st);
+    }
 }
 
 template <bool kScores>
@@ -318,13 +392,14 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const int bn = block_n_for(d);
+    const int nq_sf = q_sf_tiles(sq, d), nk_sf = (sk + bn - 1) / bn;
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
     if (in_dtype == FP4ATTN_F16) {
-        if ((rc = launch_quant_tiles<__half>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<__half>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<__half>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, nq_sf, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<__half>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, nk_sf, ocp, st))) return rc;
     } else {
-        if ((rc = launch_quant_tiles<float>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<float>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<float>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, nq_sf, ocp, st))) return rc;
+        if ((rc = launch_quant_tiles<float>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, nk_sf, ocp, st))) return rc;
         if (need_v) {
             const int64_t n4 = p.slices * static_cast<int64_t>(sk) * d / 4;
             fp4attn::f32_to_f16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4*>(V),
@@ -369,6 +444,7 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     a.seq_q = sq;
     a.seq_k = sk;
     a.nq_tiles = (sq + 127) / 128;
+    a.q_sf_tiles = q_sf_tiles(sq, d);
     a.nk_tiles = (sk + bn - 1) / bn;
     const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(d));
     a.scale_log2 = scale * 1.4426950408889634f;

@@ -206,6 +206,19 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tcgen05.mma operand reads); follow with a CTA barrier.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Arrives on named barrier `id` without waiting (the other side bar.syncs).
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads)
+{
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---------------------------------------------------------------- UMMA
 // Shared-memory matrix descriptor (sm_100 format): start, leading and stride
 // byte offsets in 16-byte units, version 1 at bits 46-47, layout at 61-63.

@@ -59,8 +59,12 @@ def test_supported_head_dims(fa):
 
 def test_workspace_size_host_only(fa):
     ws = fa.workspace_size(2, 32, 4096, 4096, 128)
-    # Q and K codes (64 B per row) + scale tiles (512 B per 128 rows)
-    assert ws == 2 * 64 * 4096 * 64 + 2 * 64 * 32 * 512
+    # Q and K codes (64 B per row) + scale tiles (512 B per 128 Q rows, per
+    # 64 K rows)
+    assert ws == 2 * 64 * 4096 * 64 + 64 * (32 + 64) * 512
+    # head_dim <= 128: Q scale tiles come in pairs (one 128-row tile here,
+    # padded to two)
+    assert fa.workspace_size(1, 1, 100, 64, 128) == 100 * 64 + 64 * 64 + 2 * 512 + 512
     assert fa.workspace_size(1, 1, 1, 1, 100) == 0
     assert fa.workspace_size(0, 1, 1, 1, 128) == 0
     assert fa.workspace_size(1, 1, 64, 128, 128, fa.F32) > fa.workspace_size(1, 1, 64, 128, 128, fa.F16)
