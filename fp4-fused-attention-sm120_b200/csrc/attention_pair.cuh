@@ -24,11 +24,11 @@
 //               query row = TMEM lane; each thread owns its whole 64-column S
 //               row, so the row max, the exponentials, the row sum, the lazy O
 //               rescale and the final O / l need no exchange between warps.
-//               Warps 4+k and 8+k share SM sub-partition k and its MUFU unit;
-//               a pair of named barriers makes them take turns at the
-//               exponentials (T0, T1, T0, ...), so that one warp's MUFU-bound
-//               exponentials overlap the other's TMEM loads, row max and waits
-//               instead of both fighting for MUFU at once.
+//               The exponentials of a step are computed against the running
+//               reference max while the step's row max is formed alongside
+//               (kSpec); only when a row max jumps past the lazy-rescale
+//               threshold is the step redone max-first, so the max is off the
+//               critical path.
 //
 // TMEM columns (512 allocated): S_0 [0,64), S_1 [64,128), O_0, O_1 (NPV each:
 // V's padded width + 16 columns holding l), P_0, P_1 (32 each: 64 FP16
@@ -38,6 +38,8 @@
 // FP4ATTN_ETIMEOUT, all roles leave their loops, in-flight copies and MMAs are
 // drained (bounded), TMEM is freed and the CTA returns.  Nothing traps.
 #pragma once
+
+#include <type_traits>
 
 #include "attention.cuh"
 
@@ -97,7 +99,7 @@ struct PairArgs {
     unsigned long long timeout_ns;
 };
 
-template <int D, typename OutT, int kPoly8, bool kTurns>
+template <int D, typename OutT, int kPoly8, bool kSpec>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const PairArgs args)
@@ -317,15 +319,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float c = args.scale_log2;
         float m = -INFINITY;
         bool ok = true;
-        // Turn-taking at the exponentials: T0 waits on bar_mine = 1 + wq and
-        // signals 5 + wq, T1 the other way round.  Every bar.sync is matched by
-        // one bar.arrive of the partner; a warp that leaves the loop early
-        // arrives once more so the partner cannot block (the partner reaches a
-        // bounded wait, sees the abort flag and leaves, before its next sync).
-        // Waits are decided per warp (__all_sync) so barrier use stays uniform.
-        const uint32_t bar_mine = t == 0 ? 1 + wq : 5 + wq;
-        const uint32_t bar_other = t == 0 ? 5 + wq : 1 + wq;
-        if (kTurns && t == 1) ptx::named_bar_arrive(bar_other, 64);  // T0 goes first
         for (int j = 0; j < nk; j++) {
             if (!__all_sync(0xffffffffu, wait_phase(&s_full[t], j & 1, wctx, kSiteSFull))) { ok = false; break; }
             ptx::tc_fence_after();
@@ -337,48 +330,66 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             ptx::tc_fence_before();
             ptx::mbar_arrive(&s_free[t]);
             const int valid = args.seq_k - j * BN;  // keys of this tile that exist
-            if (valid < BN) {
+            uint32_t pk[NT][16];
+            // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column
+            // pairs take 2^x on the FMA pipe, the rest on MUFU.  With a true
+            // tag it also returns the row max of S, whose (independent) ALU
+            // work then interleaves with the exponentials.
+            auto exps = [&](float mref, auto with_max) -> float {
+                const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
                 for (int k = 0; k < NT; k++)
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
-            }
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int k = 0; k < NT; k++)
-#pragma unroll
-                for (int i = 0; i < 32; i += 2)
-                    mx4[(i >> 1) & 3] =
-                        ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
-            const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float s0 = __uint_as_float(sr[k][i]), s1 = __uint_as_float(sr[k][i + 1]);
+                        if constexpr (decltype(with_max)::value) mx4[(i >> 1) & 3] = ptx::fmax3(mx4[(i >> 1) & 3], s0, s1);
+                        const float2 x = ptx::ffma2(make_float2(s0, s1), c2, nm2);
+                        const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
+                                                                 : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                        pk[k][i / 2] = ptx::pack_half2(p.x, p.y);
+                    }
+                return ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+            };
             float alpha = 1.f;
             bool rescale = false;
-            if (j == 0) {
-                m = m_new;
-            } else if (m_new > m + 8.0f) {
-                // Lazy rescale: O and l keep the old reference max until the
-                // row max has grown by more than 2^8.
-                alpha = ptx::ex2_approx(m - m_new);
-                m = m_new;
-                rescale = true;
+            bool exact = true;
+            if (kSpec && j > 0 && valid >= BN) {
+                // Speculative pass against the current reference max m: it
+                // stands unless some row's max grew by more than 2^8 (the lazy
+                // rescale threshold), which after the first step is rare.
+                const float mx = exps(m, std::true_type{});
+                exact = __any_sync(0xffffffffu, mx * c > m + 8.0f);
             }
-            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
-            uint32_t pk[NT][16];
-            if (kTurns) ptx::named_bar_sync(bar_mine, 64);
+            if (exact) {
+                // Row max first, then the exponentials: the first step, the
+                // ragged last step, and steps where some row's max jumped.
+                if (valid < BN) {
 #pragma unroll
-            for (int k = 0; k < NT; k++)
+                    for (int k = 0; k < NT; k++)
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float2 x =
-                        ptx::ffma2(make_float2(__uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1])), c2, nm2);
-                    // kPoly8 of every 8 column pairs take 2^x on the FMA pipe,
-                    // the rest on MUFU, so both pipes share the exponentials.
-                    const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
-                                                             : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
-                    pk[k][i / 2] = ptx::pack_half2(p.x, p.y);
+                        for (int i = 0; i < 32; i++)
+                            if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
                 }
-            if (kTurns) ptx::named_bar_arrive(bar_other, 64);
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int k = 0; k < NT; k++)
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2)
+                        mx4[(i >> 1) & 3] =
+                            ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
+                const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
+                if (j == 0) {
+                    m = m_new;
+                } else if (m_new > m + 8.0f) {
+                    // Lazy rescale: O and l keep the old reference max until
+                    // the row max has grown by more than 2^8.
+                    alpha = ptx::ex2_approx(m - m_new);
+                    m = m_new;
+                    rescale = true;
+                }
+                (void)exps(m, std::false_type{});
+            }
             if (j > 0) {
                 // PV_{j-1} must be done: it reads the P columns this step
                 // overwrites, and O is rescaled below.
@@ -411,12 +422,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             ptx::tc_wait_st();
             ptx::tc_fence_before();
             ptx::mbar_arrive(&p_full[t]);
-        }
-        if (!kTurns) {
-        } else if (!ok) {
-            ptx::named_bar_arrive(bar_other, 64);
-        } else if (t == 0) {
-            ptx::named_bar_sync(bar_mine, 64);  // T1's last arrive: leave both barriers balanced
         }
         if (ok && __all_sync(0xffffffffu, wait_phase(&pv_done[t], (nk - 1) & 1, wctx, kSitePvDone))) {
             ptx::tc_fence_after();

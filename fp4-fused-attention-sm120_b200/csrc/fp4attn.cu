@@ -244,12 +244,13 @@ int poly8_setting()
     return v;
 }
 
-// Whether the two query tiles' softmax warps take turns at the exponentials
-// (FP4ATTN_TURNS=1 selects it for the FP16-output D=128 kernel, for tuning).
-int turns_setting()
+// Whether the paired kernel exponentiates against the running max while it
+// forms the row max (FP4ATTN_SPEC=0 turns it off for the FP16-output D=128
+// kernel, for comparison).
+int spec_setting()
 {
     static int v = [] {
-        const char* s = getenv("FP4ATTN_TURNS");
+        const char* s = getenv("FP4ATTN_SPEC");
         return s ? atoi(s) : -1;
     }();
     return v;
@@ -262,12 +263,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
 }
 
-template <int D, typename OutT, int kPoly8, bool kTurns>
+template <int D, typename OutT, int kPoly8, bool kSpec>
 int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
                      int64_t slices, cudaStream_t st)
 {
     using C = fp4attn::PairCfg<D>;
-    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kTurns>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec>;
     static int launch_regs = -1;
     if (launch_regs < 0) {
         cudaFuncAttributes attr;
@@ -301,18 +302,18 @@ int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
                 int64_t slices, cudaStream_t st)
 {
     if constexpr (D == 128 && sizeof(OutT) == 2) {
-        const bool turns = turns_setting() == 1;
+        const bool spec = spec_setting() != 0;
         switch (poly8_setting()) {
-            case 2: return turns ? launch_pair_poly<D, OutT, 2, true>(tq, tk, tv, a, slices, st)
-                                 : launch_pair_poly<D, OutT, 2, false>(tq, tk, tv, a, slices, st);
-            case 4: return turns ? launch_pair_poly<D, OutT, 4, true>(tq, tk, tv, a, slices, st)
-                                 : launch_pair_poly<D, OutT, 4, false>(tq, tk, tv, a, slices, st);
+            case 2: return spec ? launch_pair_poly<D, OutT, 2, true>(tq, tk, tv, a, slices, st)
+                                : launch_pair_poly<D, OutT, 2, false>(tq, tk, tv, a, slices, st);
+            case 4: return spec ? launch_pair_poly<D, OutT, 4, true>(tq, tk, tv, a, slices, st)
+                                : launch_pair_poly<D, OutT, 4, false>(tq, tk, tv, a, slices, st);
             default:
-                if (turns) return launch_pair_poly<D, OutT, 3, true>(tq, tk, tv, a, slices, st);
+                if (!spec) return launch_pair_poly<D, OutT, 3, false>(tq, tk, tv, a, slices, st);
                 break;
         }
     }
-    return launch_pair_poly<D, OutT, 3, false>(tq, tk, tv, a, slices, st);
+    return launch_pair_poly<D, OutT, 3, true>(tq, tk, tv, a, slices, st);
 }
 
 template <int D, bool kScores>
