@@ -81,7 +81,11 @@ struct PairCfg {
     static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
     static constexpr int OFF_V = align1k(OFF_KSF + KST * SF_BYTES);
     static constexpr int V_STRIDE = align1k(V_BYTES + BN * VCW);
-    static constexpr int OFF_BAR = OFF_V + VST * V_STRIDE;
+    // Output staging: per softmax warp two buffers of 32 rows x 32 columns
+    // (sized for FP32), written swizzled and sent out by TMA stores.
+    static constexpr int OST_BYTES = 32 * 32 * 4;
+    static constexpr int OFF_OST = OFF_V + VST * V_STRIDE;
+    static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
     // q_full, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain
     static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 8 + 1;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
@@ -102,7 +106,8 @@ struct PairArgs {
 template <int D, typename OutT, int kPoly8, bool kSpec>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                              const __grid_constant__ CUtensorMap tm_v, const PairArgs args)
+                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                              const PairArgs args)
 {
     using C = PairCfg<D>;
     constexpr int BN = C::BN;
@@ -157,6 +162,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ptx::prefetch_tmap(&tm_q);
         ptx::prefetch_tmap(&tm_k);
         ptx::prefetch_tmap(&tm_v);
+        ptx::prefetch_tmap(&tm_o);
     }
     if (warp == 1) {
         ptx::tmem_alloc(&tmem_base_sh, 512);
@@ -429,35 +435,51 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             ptx::tmem_ld16(o_tm + C::L_COL, lsum);
             ptx::tc_wait_ld();
             const float inv_l = 1.0f / __uint_as_float(lsum[0]);
-            const int grow = q0 + t * C::BM + row;
-            OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D;
+            // O / l in 32-column chunks: each warp writes its 32 rows x 32
+            // columns to a staging buffer (swizzled like the TMA box, so the
+            // 16-byte writes of a warp hit distinct banks) and lane 0 stores
+            // the box with TMA; rows past seq_q are clipped by the tensor map.
+            constexpr int OB = 32 * static_cast<int>(sizeof(OutT));  // bytes per staged row
+            uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
+            const int grow0 = q0 + t * C::BM + wq * 32;
 #pragma unroll 1
             for (int k = 0; k < D / 32; k++) {
                 uint32_t o[32];
                 ptx::tmem_ld32(o_tm + 32 * k, o);
                 ptx::tc_wait_ld();
-                if (grow < args.seq_q) {
-                    if constexpr (sizeof(OutT) == 4) {
+                uint8_t* buf = ost + (k & 1) * C::OST_BYTES;
+                if (k >= 2) {
+                    // The store that last read this buffer must be done with it.
+                    if (lane == 0) ptx::bulk_wait_group_read<1>();
+                    __syncwarp();
+                }
+                uint32_t w[OB / 4];
+                if constexpr (sizeof(OutT) == 4) {
 #pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float4 v = make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
-                                                   __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
-                            *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + 32 * k + i) = v;
-                        }
-                    } else {
+                    for (int i = 0; i < 32; i++) w[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
+                } else {
 #pragma unroll
-                        for (int i = 0; i < 32; i += 8) {
-                            uint32_t w[4];
+                    for (int i = 0; i < 16; i++)
+                        w[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+                }
+                // 16-byte unit u of row `lane` sits at unit u ^ (address bits 7+):
+                // SWIZZLE_128B for 128-byte rows, SWIZZLE_64B for 64-byte rows.
 #pragma unroll
-                            for (int q = 0; q < 4; q++)
-                                w[q] = ptx::pack_half2(__uint_as_float(o[i + 2 * q]) * inv_l,
-                                                       __uint_as_float(o[i + 2 * q + 1]) * inv_l);
-                            *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + 32 * k + i) =
-                                make_uint4(w[0], w[1], w[2], w[3]);
-                        }
-                    }
+                for (int u = 0; u < OB / 16; u++) {
+                    const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
+                    *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
+                        make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::tma_store_3d(&tm_o, buf, 32 * k, grow0, slice);
+                    ptx::bulk_commit_group();
                 }
             }
+            // Shared memory must outlive the stores that read it.
+            if (lane == 0) ptx::bulk_wait_group<0>();
+            __syncwarp();
         }
     }
 

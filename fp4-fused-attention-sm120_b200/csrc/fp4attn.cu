@@ -291,8 +291,16 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     a.q_sf = fa.q_sf;
     a.k_sf = fa.k_sf;
     a.timeout_ns = fa.timeout_ns;
+    // Output written by TMA stores in 32-row x 32-column boxes (64-byte rows
+    // for FP16, 128-byte rows for FP32, swizzled to match the staging).
+    CUtensorMap to;
+    constexpr bool f32 = sizeof(OutT) == 4;
+    int rc = make_map_3d(&to, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         static_cast<int>(sizeof(OutT)), fa.out, D, fa.seq_q, slices, 32, 32,
+                         f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
     dim3 grid(fa.q_sf_tiles / 2, static_cast<unsigned>(slices));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }
