@@ -114,6 +114,7 @@ enum WaitSite : int {
     kSitePvDone,
     kSiteDrain,
     kSiteSFree,
+    kSiteQEmpty,
 };
 
 struct WaitCtx {

@@ -4,11 +4,17 @@
 // Same computation as fp4_attention_fwd_kernel (attention.cuh) -- the
 // reference kernel fused_fp4_attention (common.h:68-328) with Q, K in
 // E2M1 + UE8M0 and V, P in FP16 -- with a different division of the work.
-// Each CTA owns 256 query rows as two independent 128-row tiles T0, T1 and
-// walks the keys in 64-row tiles:
+// A work item is 256 query rows of one (batch, head) slice, as two
+// independent 128-row tiles T0, T1, whose keys are walked in 64-row tiles.
+// The kernel is persistent: one CTA per SM takes items blockIdx.x,
+// blockIdx.x + gridDim.x, ... (consecutive items share a slice's K/V in L2),
+// and every barrier phase and ring index runs on across items, so the next
+// item's Q, K, V and first S are fetched and computed while the current
+// item's last step and epilogue run.  Roles:
 //
-//   warp 0      TMA producer: both Q tiles once, then K (codes + scale tile)
-//               and V tiles through KST/VST-stage mbarrier rings.
+//   warp 0      TMA producer: per item both Q tiles (once the previous item's
+//               S MMAs are done with them), then K (codes + scale tile) and V
+//               tiles through KST/VST-stage mbarrier rings.
 //   warp 1      S issuer: S_t = Q_t K_j^T (tcgen05.mma kind::mxf4 block_scale,
 //               M128 N64) for t = 0, 1; S_t for step j+1 is issued as soon
 //               as softmax warpgroup t has copied S_t of step j to registers.
@@ -86,8 +92,8 @@ struct PairCfg {
     static constexpr int OST_BYTES = 32 * 32 * 4;
     static constexpr int OFF_OST = OFF_V + VST * V_STRIDE;
     static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
-    // q_full, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain
-    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 8 + 1;
+    // q_full, q_empty, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain
+    static constexpr int NUM_BARS = 2 + 2 * KST + 2 * VST + 8 + 1;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -95,6 +101,8 @@ struct PairCfg {
 struct PairArgs {
     int seq_q, seq_k;
     int nk_tiles;
+    int n_pairs;               // query tile pairs per slice (q_sf_tiles / 2)
+    int n_items;               // work items = n_pairs * slices
     int q_sf_tiles;            // 128-row scale tiles per slice in q_sf (even)
     float scale_log2;          // softmax_scale * log2(e)
     void* out;                 // [slices, seq_q, D]
@@ -120,7 +128,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint8_t* sV = smem + C::OFF_V;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
+    uint64_t* q_empty = bars + 1;         // this item's S MMAs are done with Q (tcgen05.commit)
+    uint64_t* k_full = bars + 2;
     uint64_t* k_empty = k_full + C::KST;
     uint64_t* v_full = k_empty + C::KST;
     uint64_t* v_empty = v_full + C::VST;
@@ -134,12 +143,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __shared__ int abort_sh;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int pair = blockIdx.x, slice = blockIdx.y;
-    const int q0 = pair * 2 * C::BM;
     const int nk = args.nk_tiles;
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
+        ptx::mbar_init(q_empty, 1);
         for (int i = 0; i < C::KST; i++) {
             ptx::mbar_init(&k_full[i], 1);
             ptx::mbar_init(&k_empty[i], 1);
@@ -194,37 +202,53 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ptx::setmaxnreg_dec<kCtlRegs>();
         if (warp == 0) {
             // -------------------------------------------------------- producer
+            // Items in order; the K/V ring index kv runs on across items, and
+            // the next item's Q (and its first K/V tiles) load while the
+            // current item's last steps run.
             if (lane == 0) {
-                ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
+                int it = 0, kv = 0, k_issued = 0, v_issued = 0;
+                bool ok = true;
+                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x, it++) {
+                    const int slice = w / args.n_pairs, pair = w % args.n_pairs;
+                    if (it > 0 && !wait_phase(q_empty, (it - 1) & 1, wctx, kSiteQEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
 #pragma unroll
-                for (int t = 0; t < 2; t++) {
-                    ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, q0 + t * C::BM, slice);
-                    ptx::bulk_load(sQsf + t * C::SF_BYTES,
-                                   args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + 2 * pair + t) * C::SF_BYTES,
-                                   C::SF_BYTES, q_full);
-                }
-                int k_issued = 0, v_issued = 0;
-                for (int j = 0; j < nk; j++) {
-                    const int ks = j % C::KST;
-                    if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
-                    ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::SF_BYTES);
-                    ptx::tma_load_3d(sK + ks * C::K_STRIDE, &tm_k, &k_full[ks], 0, j * BN, slice);
-                    ptx::bulk_load(sKsf + ks * C::SF_BYTES,
-                                   args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::SF_BYTES, C::SF_BYTES,
-                                   &k_full[ks]);
-                    k_issued = j + 1;
-                    const int vs = j % C::VST;
-                    if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty)) break;
-                    ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+                    for (int t = 0; t < 2; t++) {
+                        ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, pair * 2 * C::BM + t * C::BM, slice);
+                        ptx::bulk_load(sQsf + t * C::SF_BYTES,
+                                       args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + 2 * pair + t) *
+                                                       C::SF_BYTES,
+                                       C::SF_BYTES, q_full);
+                    }
+                    for (int j = 0; j < nk; j++, kv++) {
+                        const int ks = kv % C::KST;
+                        if (kv >= C::KST && !wait_phase(&k_empty[ks], ((kv / C::KST) - 1) & 1, wctx, kSiteKEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::SF_BYTES);
+                        ptx::tma_load_3d(sK + ks * C::K_STRIDE, &tm_k, &k_full[ks], 0, j * BN, slice);
+                        ptx::bulk_load(sKsf + ks * C::SF_BYTES,
+                                       args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::SF_BYTES, C::SF_BYTES,
+                                       &k_full[ks]);
+                        k_issued = kv + 1;
+                        const int vs = kv % C::VST;
+                        if (kv >= C::VST && !wait_phase(&v_empty[vs], ((kv / C::VST) - 1) & 1, wctx, kSiteVEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
 #pragma unroll
-                    for (int c = 0; c < C::VCH; c++)
-                        ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
-                                         c * (C::VCW / 2), j * BN, slice);
-                    v_issued = j + 1;
+                        for (int c = 0; c < C::VCH; c++)
+                            ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
+                                             c * (C::VCW / 2), j * BN, slice);
+                        v_issued = kv + 1;
+                    }
                 }
-                // Every load this thread issued must land before the CTA exits.
+                // Every load this thread issued must land before the CTA exits
+                // (Q loads are at most one phase ahead of their consumer).
                 const unsigned long long drain_ns = 2ull * args.timeout_ns;
-                drain_phase(q_full, 0, drain_ns);
+                if (it > 0) drain_phase(q_full, (it - 1) & 1, drain_ns);
                 for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
                     drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
                 for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
@@ -239,42 +263,48 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::CW, qk_layout);
                 const uint64_t sfdesc0 = ptx::make_sdesc(ptx::smem_u32(sQsf), 0, 128, ptx::kSwizzleNone);
                 const uint64_t ksfdesc0 = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
-                bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
-                if (ok) {
+                // g: global step (s_free phase), kv: K ring index, it: item.
+                int g = 0, kv = 0, it = 0;
+                bool ok = true;
+                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x, it++) {
+                    if (!wait_phase(q_full, it & 1, wctx, kSiteQFull)) break;
                     ptx::tc_fence_after();
+                    // The previous item's S MMAs are complete: the producer
+                    // loaded this Q only after their q_empty commit arrived.
+                    const uint32_t sfa = tmem + C::SFA_COL;
 #pragma unroll
                     for (int t = 0; t < 2; t++)
-                        ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL + 4 * t,
-                                                  sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
-                }
-                for (int j = 0; ok && j < nk; j++) {
-                    const int ks = j % C::KST;
-                    if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) break;
-                    ptx::tc_fence_after();
-                    const uint32_t sfb = tmem + C::SFB_COL + 4 * ks;
-                    ptx::tc_cp_32x128b_warpx4(sfb, ksfdesc0 + static_cast<uint64_t>((ks * C::SF_BYTES) >> 4));
-                    const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
+                        ptx::tc_cp_32x128b_warpx4(sfa + 4 * t, sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
+                    for (int j = 0; ok && j < nk; j++, kv++, g++) {
+                        const int ks = kv % C::KST;
+                        if (!wait_phase(&k_full[ks], (kv / C::KST) & 1, wctx, kSiteKFull)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t sfb = tmem + C::SFB_COL + 4 * ks;
+                        ptx::tc_cp_32x128b_warpx4(sfb, ksfdesc0 + static_cast<uint64_t>((ks * C::SF_BYTES) >> 4));
+                        const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
 #pragma unroll
-                    for (int t = 0; t < 2; t++) {
-                        // S_t's columns are free once warpgroup t holds step j-1 in registers.
-                        if (j > 0) {
-                            if (!wait_phase(&s_free[t], (j - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
-                            ptx::tc_fence_after();
-                        }
+                        for (int t = 0; t < 2; t++) {
+                            // S_t's columns are free once warpgroup t holds the previous step in registers.
+                            if (g > 0) {
+                                if (!wait_phase(&s_free[t], (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
+                                ptx::tc_fence_after();
+                            }
 #pragma unroll
-                        for (int kk = 0; kk < C::KSTEPS; kk++) {
-                            const uint32_t sf_id = 2u * (kk & 1);
-                            ptx::mma_mxf4(tmem + C::S_COL + t * BN,
-                                          qdesc0 + static_cast<uint64_t>((t * C::Q_BYTES + kk * 32) >> 4),
-                                          kdesc + static_cast<uint64_t>((kk * 32) >> 4),
-                                          ptx::idesc_mxf4(128, BN, sf_id, sf_id),
-                                          (tmem + C::SFA_COL + 4 * t) | (sf_id << 30), sfb | (sf_id << 30),
-                                          kk > 0 ? 1u : 0u);
+                            for (int kk = 0; kk < C::KSTEPS; kk++) {
+                                const uint32_t sf_id = 2u * (kk & 1);
+                                ptx::mma_mxf4(tmem + C::S_COL + t * BN,
+                                              qdesc0 + static_cast<uint64_t>((t * C::Q_BYTES + kk * 32) >> 4),
+                                              kdesc + static_cast<uint64_t>((kk * 32) >> 4),
+                                              ptx::idesc_mxf4(128, BN, sf_id, sf_id), (sfa + 4 * t) | (sf_id << 30),
+                                              sfb | (sf_id << 30), kk > 0 ? 1u : 0u);
+                            }
+                            ptx::tc_commit(&s_full[t]);
                         }
-                        ptx::tc_commit(&s_full[t]);
+                        if (!ok) break;
+                        ptx::tc_commit(&k_empty[ks]);
                     }
                     if (!ok) break;
-                    ptx::tc_commit(&k_empty[ks]);
+                    ptx::tc_commit(q_empty);  // the producer may load the next item's Q
                 }
                 // Drain every tcgen05 op this thread issued before TMEM is freed.
                 ptx::tc_commit(drain_bar);
@@ -287,24 +317,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
                 const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
                 constexpr uint32_t idesc_pv = ptx::idesc_f16(128, C::NPV, true);
+                int g = 0;  // global step: p_full phase and V ring index
                 bool ok = true;
-                for (int j = 0; ok && j < nk; j++) {
-                    const int vs = j % C::VST;
-                    if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
-                    const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
+                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x) {
+                    for (int j = 0; ok && j < nk; j++, g++) {
+                        const int vs = g % C::VST;
+                        if (!wait_phase(&v_full[vs], (g / C::VST) & 1, wctx, kSiteVFull)) { ok = false; break; }
+                        const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
 #pragma unroll
-                    for (int t = 0; t < 2; t++) {
-                        if (!wait_phase(&p_full[t], j & 1, wctx, kSitePFull)) { ok = false; break; }
-                        ptx::tc_fence_after();
+                        for (int t = 0; t < 2; t++) {
+                            if (!wait_phase(&p_full[t], g & 1, wctx, kSitePFull)) { ok = false; break; }
+                            ptx::tc_fence_after();
+                            // The first step of an item starts O_t afresh.
 #pragma unroll
-                        for (int kk = 0; kk < BN / 16; kk++)
-                            ptx::mma_f16_ts(tmem + C::O_COL + t * C::NPV, tmem + C::P_COL + t * (BN / 2) + kk * 8,
-                                            vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
-                                            (j > 0 || kk > 0) ? 1u : 0u);
-                        ptx::tc_commit(&pv_done[t]);
+                            for (int kk = 0; kk < BN / 16; kk++)
+                                ptx::mma_f16_ts(tmem + C::O_COL + t * C::NPV, tmem + C::P_COL + t * (BN / 2) + kk * 8,
+                                                vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
+                                                (j > 0 || kk > 0) ? 1u : 0u);
+                            ptx::tc_commit(&pv_done[t]);
+                        }
+                        if (!ok) break;
+                        ptx::tc_commit(&v_empty[vs]);
                     }
-                    if (!ok) break;
-                    ptx::tc_commit(&v_empty[vs]);
                 }
                 ptx::tc_commit(drain_bar);
                 drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
@@ -323,164 +357,176 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t o_tm = tmem + lane_off + C::O_COL + t * C::NPV;
         const uint32_t p_tm = tmem + lane_off + C::P_COL + t * (BN / 2);
         const float c = args.scale_log2;
-        float m = -INFINITY;
+        uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
+        int g = 0;  // global step: phase of s_full / s_free / p_full / pv_done
         bool ok = true;
-        for (int j = 0; j < nk; j++) {
-            if (!__all_sync(0xffffffffu, wait_phase(&s_full[t], j & 1, wctx, kSiteSFull))) { ok = false; break; }
-            ptx::tc_fence_after();
-            uint32_t sr[NT][32];
+        for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x) {
+            const int slice = w / args.n_pairs, pair = w % args.n_pairs;
+            float m = -INFINITY;
+            for (int j = 0; j < nk; j++, g++) {
+                if (!__all_sync(0xffffffffu, wait_phase(&s_full[t], g & 1, wctx, kSiteSFull))) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t sr[NT][32];
 #pragma unroll
-            for (int k = 0; k < NT; k++) ptx::tmem_ld32(s_tm + 32 * k, sr[k]);
-            ptx::tc_wait_ld();
-            // S_t is in registers: the issuer may compute the next step into it.
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&s_free[t]);
-            const int valid = args.seq_k - j * BN;  // keys of this tile that exist
-            uint32_t pk[NT][16];
-            // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column
-            // pairs take 2^x on the FMA pipe, the rest on MUFU.  With a true
-            // tag it also returns the row max of S, whose (independent) ALU
-            // work then interleaves with the exponentials.
-            auto exps = [&](float mref, auto with_max) -> float {
-                const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
-                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                for (int k = 0; k < NT; k++)
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float s0 = __uint_as_float(sr[k][i]), s1 = __uint_as_float(sr[k][i + 1]);
-                        if constexpr (decltype(with_max)::value) mx4[(i >> 1) & 3] = ptx::fmax3(mx4[(i >> 1) & 3], s0, s1);
-                        const float2 x = ptx::ffma2(make_float2(s0, s1), c2, nm2);
-                        const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
-                                                                 : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
-                        pk[k][i / 2] = ptx::pack_half2(p.x, p.y);
-                    }
-                return ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
-            };
-            float alpha = 1.f;
-            bool rescale = false;
-            bool exact = true;
-            if (kSpec && j > 0 && valid >= BN) {
-                // Speculative pass against the current reference max m: it
-                // stands unless some row's max grew by more than 2^8 (the lazy
-                // rescale threshold), which after the first step is rare.
-                const float mx = exps(m, std::true_type{});
-                exact = __any_sync(0xffffffffu, mx * c > m + 8.0f);
-            }
-            if (exact) {
-                // Row max first, then the exponentials: the first step, the
-                // ragged last step, and steps where some row's max jumped.
-                if (valid < BN) {
+                for (int k = 0; k < NT; k++) ptx::tmem_ld32(s_tm + 32 * k, sr[k]);
+                ptx::tc_wait_ld();
+                // S_t is in registers: the issuer may compute the next step into it.
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&s_free[t]);
+                const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+                uint32_t pk[NT][16];
+                // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column
+                // pairs take 2^x on the FMA pipe, the rest on MUFU.  With a true
+                // tag it also returns the row max of S, whose (independent) ALU
+                // work then interleaves with the exponentials.
+                auto exps = [&](float mref, auto with_max) -> float {
+                    const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
+                    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
                     for (int k = 0; k < NT; k++)
 #pragma unroll
-                        for (int i = 0; i < 32; i++)
-                            if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
+                        for (int i = 0; i < 32; i += 2) {
+                            const float s0 = __uint_as_float(sr[k][i]), s1 = __uint_as_float(sr[k][i + 1]);
+                            if constexpr (decltype(with_max)::value) mx4[(i >> 1) & 3] = ptx::fmax3(mx4[(i >> 1) & 3], s0, s1);
+                            const float2 x = ptx::ffma2(make_float2(s0, s1), c2, nm2);
+                            const float2 p = ((i >> 1) & 7) < kPoly8 ? ptx::exp2_poly3(x)
+                                                                     : make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                            pk[k][i / 2] = ptx::pack_half2(p.x, p.y);
+                        }
+                    return ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+                };
+                float alpha = 1.f;
+                bool rescale = false;
+                bool exact = true;
+                if (kSpec && j > 0 && valid >= BN) {
+                    // Speculative pass against the current reference max m: it
+                    // stands unless some row's max grew by more than 2^8 (the lazy
+                    // rescale threshold), which after the first step is rare.
+                    const float mx = exps(m, std::true_type{});
+                    exact = __any_sync(0xffffffffu, mx * c > m + 8.0f);
                 }
-                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (exact) {
+                    // Row max first, then the exponentials: the first step, the
+                    // ragged last step, and steps where some row's max jumped.
+                    if (valid < BN) {
 #pragma unroll
-                for (int k = 0; k < NT; k++)
+                        for (int k = 0; k < NT; k++)
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2)
-                        mx4[(i >> 1) & 3] =
-                            ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
-                const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
-                if (j == 0) {
-                    m = m_new;
-                } else if (m_new > m + 8.0f) {
-                    // Lazy rescale: O and l keep the old reference max until
-                    // the row max has grown by more than 2^8.
-                    alpha = ptx::ex2_approx(m - m_new);
-                    m = m_new;
-                    rescale = true;
+                            for (int i = 0; i < 32; i++)
+                                if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
+                    }
+                    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                    for (int k = 0; k < NT; k++)
+#pragma unroll
+                        for (int i = 0; i < 32; i += 2)
+                            mx4[(i >> 1) & 3] =
+                                ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
+                    const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
+                    if (j == 0) {
+                        m = m_new;
+                    } else if (m_new > m + 8.0f) {
+                        // Lazy rescale: O and l keep the old reference max until
+                        // the row max has grown by more than 2^8.
+                        alpha = ptx::ex2_approx(m - m_new);
+                        m = m_new;
+                        rescale = true;
+                    }
+                    (void)exps(m, std::false_type{});
                 }
-                (void)exps(m, std::false_type{});
-            }
-            if (j > 0) {
-                // PV_{j-1} must be done: it reads the P columns this step
-                // overwrites, and O is rescaled below.
-                if (!__all_sync(0xffffffffu, wait_phase(&pv_done[t], (j - 1) & 1, wctx, kSitePvDone))) {
-                    ok = false;
-                    break;
+                if (j > 0) {
+                    // PV_{j-1} must be done: it reads the P columns this step
+                    // overwrites, and O is rescaled below.
+                    if (!__all_sync(0xffffffffu, wait_phase(&pv_done[t], (g - 1) & 1, wctx, kSitePvDone))) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
                 }
-                ptx::tc_fence_after();
-            }
 #pragma unroll
-            for (int k = 0; k < NT; k++) ptx::tmem_st16(p_tm + 16 * k, pk[k]);
-            if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-                // O and its row-sum columns move to the new reference max.
+                for (int k = 0; k < NT; k++) ptx::tmem_st16(p_tm + 16 * k, pk[k]);
+                if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+                    // O and its row-sum columns move to the new reference max.
 #pragma unroll 1
-                for (int k = 0; k < C::L_COL / 32; k++) {
+                    for (int k = 0; k < C::L_COL / 32; k++) {
+                        uint32_t o[32];
+                        ptx::tmem_ld32(o_tm + 32 * k, o);
+                        ptx::tc_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        ptx::tmem_st32(o_tm + 32 * k, o);
+                    }
+                    uint32_t o[16];
+                    ptx::tmem_ld16(o_tm + C::L_COL, o);
+                    ptx::tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    ptx::tmem_st16(o_tm + C::L_COL, o);
+                }
+                ptx::tc_wait_st();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&p_full[t]);
+            }
+            // The last step's P.V must be complete before O is read.
+            if (!ok || !__all_sync(0xffffffffu, wait_phase(&pv_done[t], (g - 1) & 1, wctx, kSitePvDone))) {
+                ok = false;
+                break;
+            }
+            {
+                ptx::tc_fence_after();
+                uint32_t lsum[16];
+                ptx::tmem_ld16(o_tm + C::L_COL, lsum);
+                ptx::tc_wait_ld();
+                const float inv_l = 1.0f / __uint_as_float(lsum[0]);
+                // O / l in 32-column chunks: each warp writes its 32 rows x 32
+                // columns to a staging buffer (swizzled like the TMA box, so the
+                // 16-byte writes of a warp hit distinct banks) and lane 0 stores
+                // the box with TMA; rows past seq_q are clipped by the tensor map.
+                constexpr int OB = 32 * static_cast<int>(sizeof(OutT));  // bytes per staged row
+                const int grow0 = pair * 2 * C::BM + t * C::BM + wq * 32;
+#pragma unroll 1
+                for (int k = 0; k < D / 32; k++) {
                     uint32_t o[32];
                     ptx::tmem_ld32(o_tm + 32 * k, o);
                     ptx::tc_wait_ld();
+                    uint8_t* buf = ost + (k & 1) * C::OST_BYTES;
+                    if (k >= 2) {
+                        // The store that last read this buffer must be done with it.
+                        if (lane == 0) ptx::bulk_wait_group_read<1>();
+                        __syncwarp();
+                    }
+                    uint32_t ov[OB / 4];
+                    if constexpr (sizeof(OutT) == 4) {
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    ptx::tmem_st32(o_tm + 32 * k, o);
-                }
-                uint32_t o[16];
-                ptx::tmem_ld16(o_tm + C::L_COL, o);
-                ptx::tc_wait_ld();
+                        for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
+                    } else {
 #pragma unroll
-                for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                ptx::tmem_st16(o_tm + C::L_COL, o);
-            }
-            ptx::tc_wait_st();
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(&p_full[t]);
-        }
-        if (ok && __all_sync(0xffffffffu, wait_phase(&pv_done[t], (nk - 1) & 1, wctx, kSitePvDone))) {
-            ptx::tc_fence_after();
-            uint32_t lsum[16];
-            ptx::tmem_ld16(o_tm + C::L_COL, lsum);
-            ptx::tc_wait_ld();
-            const float inv_l = 1.0f / __uint_as_float(lsum[0]);
-            // O / l in 32-column chunks: each warp writes its 32 rows x 32
-            // columns to a staging buffer (swizzled like the TMA box, so the
-            // 16-byte writes of a warp hit distinct banks) and lane 0 stores
-            // the box with TMA; rows past seq_q are clipped by the tensor map.
-            constexpr int OB = 32 * static_cast<int>(sizeof(OutT));  // bytes per staged row
-            uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
-            const int grow0 = q0 + t * C::BM + wq * 32;
-#pragma unroll 1
-            for (int k = 0; k < D / 32; k++) {
-                uint32_t o[32];
-                ptx::tmem_ld32(o_tm + 32 * k, o);
-                ptx::tc_wait_ld();
-                uint8_t* buf = ost + (k & 1) * C::OST_BYTES;
-                if (k >= 2) {
-                    // The store that last read this buffer must be done with it.
-                    if (lane == 0) ptx::bulk_wait_group_read<1>();
+                        for (int i = 0; i < 16; i++)
+                            ov[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+                    }
+                    // 16-byte unit u of row `lane` sits at unit u ^ (address bits 7+):
+                    // SWIZZLE_128B for 128-byte rows, SWIZZLE_64B for 64-byte rows.
+#pragma unroll
+                    for (int u = 0; u < OB / 16; u++) {
+                        const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
+                        *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
+                            make_uint4(ov[4 * u], ov[4 * u + 1], ov[4 * u + 2], ov[4 * u + 3]);
+                    }
+                    ptx::fence_proxy_async_smem();
                     __syncwarp();
+                    if (lane == 0) {
+                        ptx::tma_store_3d(&tm_o, buf, 32 * k, grow0, slice);
+                        ptx::bulk_commit_group();
+                    }
                 }
-                uint32_t w[OB / 4];
-                if constexpr (sizeof(OutT) == 4) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) w[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        w[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
-                }
-                // 16-byte unit u of row `lane` sits at unit u ^ (address bits 7+):
-                // SWIZZLE_128B for 128-byte rows, SWIZZLE_64B for 64-byte rows.
-#pragma unroll
-                for (int u = 0; u < OB / 16; u++) {
-                    const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
-                    *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
-                        make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-                }
-                ptx::fence_proxy_async_smem();
+                // The next item's epilogue reuses the staging buffers.
+                if (lane == 0) ptx::bulk_wait_group_read<0>();
                 __syncwarp();
-                if (lane == 0) {
-                    ptx::tma_store_3d(&tm_o, buf, 32 * k, grow0, slice);
-                    ptx::bulk_commit_group();
-                }
             }
-            // Shared memory must outlive the stores that read it.
-            if (lane == 0) ptx::bulk_wait_group<0>();
-            __syncwarp();
         }
+        // Shared memory must outlive the stores that read it.
+        if (lane == 0) ptx::bulk_wait_group<0>();
+        __syncwarp();
     }
 
     ptx::tc_fence_before();

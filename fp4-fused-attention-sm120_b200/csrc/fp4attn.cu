@@ -299,7 +299,15 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
                          static_cast<int>(sizeof(OutT)), fa.out, D, fa.seq_q, slices, 32, 32,
                          f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
-    dim3 grid(fa.q_sf_tiles / 2, static_cast<unsigned>(slices));
+    // Persistent: one CTA per SM walks the (slice, query-tile pair) items.
+    a.n_pairs = fa.q_sf_tiles / 2;
+    const int64_t items = static_cast<int64_t>(a.n_pairs) * slices;
+    if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
+    a.n_items = static_cast<int>(items);
+    int dev = 0, sms = 0;
+    FP4_CUDA(cudaGetDevice(&dev));
+    FP4_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, std::max(sms, 1)));
     kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
