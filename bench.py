@@ -119,9 +119,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def profile_traffic(workload):
-    """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / f"fp4_attention_fwd_{workload}.md"
+def profile_traffic(workload, kernel):
+    """DRAM bytes per attention launch from the committed ncu summary of this
+    kernel on this workload, if any."""
+    p = ROOT / "profiles" / f"{kernel.replace('_kernel', '')}_{workload}.md"
     if p.exists():
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
         if m:
@@ -341,7 +342,8 @@ def main():
         w_shard = wl.Workload(base.name, 1, n, base.seq_q, base.seq_k, base.head_dim)
         peak = mixed_roofline(w_shard, bf16)
         achieved = flops_rank / (kern_ms * 1e-3) / 1e12
-        traffic = profile_traffic(args.workload)
+        kernel = "fp4_attention_pair_kernel" if base.head_dim <= 128 else "fp4_attention_fwd_kernel"
+        traffic = profile_traffic(args.workload, kernel)
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             ref = CpuReference(base)
@@ -361,7 +363,7 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_basis": f"mixed: QK^T at 4x and PV at 1x the {peak_src} bf16 dense "
                                        f"{bf16:g} TFLOP/s",
-                         "kernel": "fp4_attention_fwd_kernel", "kernel_ms": kern_ms},
+                         "kernel": kernel, "kernel_ms": kern_ms},
             "frac_of_mixed_roofline_step": value / world / peak,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms},
