@@ -28,6 +28,8 @@ OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, EWORKSPACE = range(6)
 F32, F16 = 0, 1
 SCALE_REFERENCE, SCALE_OCP = 0, 1
 LAYOUT_ROWMAJOR = 0
+MASK_NONE = 0    # every query sees every key (the reference's only mode)
+MASK_CAUSAL = 1  # query i sees keys j <= i + seq_k - seq_q (bottom-right aligned)
 
 _HERE = pathlib.Path(__file__).resolve().parent
 _LIB = None
@@ -67,6 +69,10 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_prepare.restype = i32
     L.fp4attn_attend.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, vp, sz, vp]
     L.fp4attn_attend.restype = i32
+    L.fp4attn_forward_masked.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, i32, vp, sz, vp]
+    L.fp4attn_forward_masked.restype = i32
+    L.fp4attn_attend_masked.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, vp, sz, vp]
+    L.fp4attn_attend_masked.restype = i32
     L.fp4attn_debug_scores.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]
     L.fp4attn_debug_scores.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
@@ -168,17 +174,21 @@ def _check_qkv(Q, K, V):
     return B, H, Sq, K.shape[2], D
 
 
-def fused_fp4_attention_into(Q, K, V, out, workspace, softmax_scale=None, scale_mode="reference", stream=None):
+def fused_fp4_attention_into(Q, K, V, out, workspace, softmax_scale=None, scale_mode="reference", stream=None,
+                             causal=False):
     """Launch into caller-provided `out` and `workspace` (uint8 CUDA tensor of
-    at least workspace_size(...) bytes); no allocation, async on `stream`."""
+    at least workspace_size(...) bytes); no allocation, async on `stream`.
+    causal=True applies the bottom-right causal mask (fp4attn_forward_masked)."""
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
     if out.shape != Q.shape or not out.is_contiguous():
         raise ValueError("out must be contiguous with Q's shape")
-    rc = lib().fp4attn_forward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), _dtype_code(Q),
-                               _dtype_code(out), B, H, Sq, Sk, D, float(softmax_scale or 0.0),
-                               _scale_mode(scale_mode), workspace.data_ptr(), workspace.numel(),
-                               _stream_ptr(stream))
-    _check(rc, "fp4attn_forward")
+    args = (Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), _dtype_code(Q), _dtype_code(out), B, H, Sq, Sk,
+            D, float(softmax_scale or 0.0), _scale_mode(scale_mode))
+    tail = (workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+    if causal:
+        _check(lib().fp4attn_forward_masked(*args, MASK_CAUSAL, *tail), "fp4attn_forward_masked")
+    else:
+        _check(lib().fp4attn_forward(*args, *tail), "fp4attn_forward")
     return out
 
 
@@ -190,12 +200,17 @@ def prepare(Q, K, V, workspace, scale_mode="reference", stream=None):
     _check(rc, "fp4attn_prepare")
 
 
-def attend(V, out, workspace, in_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale=None, stream=None):
-    """The attention kernel on a prepared workspace (fp4attn_attend)."""
-    rc = lib().fp4attn_attend(V.data_ptr(), out.data_ptr(), in_dtype, _dtype_code(out), batch, heads, seq_q, seq_k,
-                              head_dim, float(softmax_scale or 0.0), workspace.data_ptr(), workspace.numel(),
-                              _stream_ptr(stream))
-    _check(rc, "fp4attn_attend")
+def attend(V, out, workspace, in_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale=None, stream=None,
+           causal=False):
+    """The attention kernel on a prepared workspace (fp4attn_attend, or
+    fp4attn_attend_masked with the causal mask)."""
+    head = (V.data_ptr(), out.data_ptr(), in_dtype, _dtype_code(out), batch, heads, seq_q, seq_k, head_dim,
+            float(softmax_scale or 0.0))
+    tail = (workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
+    if causal:
+        _check(lib().fp4attn_attend_masked(*head, MASK_CAUSAL, *tail), "fp4attn_attend_masked")
+    else:
+        _check(lib().fp4attn_attend(*head, *tail), "fp4attn_attend")
     return out
 
 
@@ -211,15 +226,17 @@ def shard_range(n_slices: int, world: int, rank: int) -> tuple[int, int]:
     return lo, lo + base + (1 if rank < extra else 0)
 
 
-def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode="reference", stream=None):
+def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode="reference", stream=None,
+                        causal=False):
     """softmax(Q K^T * scale) V with FP4 (E2M1 + UE8M0/32) Q and K: the
     reference kernel fused_fp4_attention<HEAD_DIM> (common.h:68-328) for
-    [batch, heads, seq, head_dim] tensors of any seq_q / seq_k."""
+    [batch, heads, seq, head_dim] tensors of any seq_q / seq_k.  causal=True
+    adds the bottom-right causal mask (not in the reference)."""
     torch = _torch()
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
     out = torch.empty((B, H, Sq, D), dtype=out_dtype or Q.dtype, device=Q.device)
     ws = torch.empty(workspace_size(B, H, Sq, Sk, D, _dtype_code(Q)), dtype=torch.uint8, device=Q.device)
-    return fused_fp4_attention_into(Q, K, V, out, ws, softmax_scale, scale_mode, stream)
+    return fused_fp4_attention_into(Q, K, V, out, ws, softmax_scale, scale_mode, stream, causal)
 
 
 def debug_scores(Q, K, scale_mode="reference", stream=None):

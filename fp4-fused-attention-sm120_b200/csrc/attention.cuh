@@ -101,6 +101,8 @@ struct FwdArgs {
     const uint8_t* q_sf;       // [slices][q_sf_tiles][QSF_BYTES]
     const uint8_t* k_sf;       // [slices][nk_tiles][KSF_BYTES]
     unsigned long long timeout_ns;
+    int causal;                // 1: query i sees keys j <= i + causal_off only (attention, not scores)
+    int causal_off;            // seq_k - seq_q (bottom-right alignment)
 };
 
 enum WaitSite : int {
@@ -207,9 +209,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __shared__ int abort_sh;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int qt = blockIdx.x, slice = blockIdx.y;
+    // With the causal mask a tile needs keys only up to its last row: the
+    // heaviest tiles (last rows) are launched first, and the key loop stops
+    // at the tile's last visible key.
+    const bool causal = !kScores && args.causal;
+    const int qt = causal ? args.nq_tiles - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
+    const int slice = blockIdx.y;
     const int q0 = qt * C::BM;
-    const int nk = args.nk_tiles;
+    int nk = args.nk_tiles;
+    if (causal) {
+        const int hi = min(q0 + C::BM - 1, args.seq_q - 1) + args.causal_off;
+        nk = hi < 0 ? 1 : min(nk, hi / BN + 1);
+    }
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
@@ -266,7 +277,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW,
                                          j * BN, slice);
                     ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
-                                   args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::KSF_BYTES, C::KSF_BYTES,
+                                   args.k_sf + (static_cast<size_t>(slice) * args.nk_tiles + j) * C::KSF_BYTES, C::KSF_BYTES,
                                    &k_full[ks]);
                     k_issued = j + 1;
                     if (!kScores) {
@@ -424,6 +435,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             // same values, so the halves never wait on each other -- and then
             // exponentiates only its own half of the columns.
             constexpr int NF = BN / 32;            // 32-column chunks of a full S row
+            // Keys this row sees: [0, row_lim) (the causal mask, or all keys).
+            const int row_lim = causal ? min(q0 + row + args.causal_off + 1, args.seq_k) : args.seq_k;
             for (int j = 0; j < nk; j++) {
                 if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
                 ptx::tc_fence_after();
@@ -434,7 +447,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     for (int t = 0; t < NF; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
                 }
                 ptx::tc_wait_ld();
-                const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+                const int valid = row_lim - j * BN;  // keys of this step this row sees
                 if (valid < BN) {
 #pragma unroll
                     for (int t = 0; t < NF; t++)
@@ -461,7 +474,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     rescale = true;
                 }
                 float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-                const float2 c2 = make_float2(c, c), nm2 = make_float2(-m, -m);
+                // A row that has seen no key yet keeps m = -inf; its P is 0.
+                const float m_ref = m == -INFINITY ? 0.f : m;
+                const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_ref, -m_ref);
                 uint32_t pk[NT][16];
                 // Exponentials of one 32-column chunk (indices stay compile-time
                 // so the row stays in registers).
@@ -528,7 +543,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const float l_tot = l + red_l[(1 - half) * 128 + row];
             if (wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone)) {
                 ptx::tc_fence_after();
-                const float inv_l = 1.0f / l_tot;
+                const float inv_l = l_tot > 0.f ? 1.0f / l_tot : 0.f;  // a row that saw no key outputs 0
                 const int grow = q0 + row;
                 OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D +
                             half * HD;

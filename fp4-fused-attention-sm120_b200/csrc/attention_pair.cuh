@@ -109,7 +109,43 @@ struct PairArgs {
     const uint8_t* q_sf;       // [slices][q_sf_tiles][512]
     const uint8_t* k_sf;       // [slices][nk_tiles][512]
     unsigned long long timeout_ns;
+    int causal;                // 1: query i sees keys j <= i + causal_off only
+    int causal_off;            // seq_k - seq_q (bottom-right alignment)
 };
+
+// Work item r of this CTA's static schedule: (slice, query-tile pair) and its
+// number of 64-key steps.  Without a mask items go in slice order (a slice's
+// K/V stay in L2 while its pairs run).  With the causal mask an item needs
+// keys only up to its last query row, so items go heaviest first (pair-major,
+// last pairs first) and are dealt to the CTAs in a snake order (forward on
+// even rounds, backward on odd ones), which evens out each CTA's total.
+struct PairItem {
+    int slice, pair, nk;
+    bool valid;
+};
+
+__device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
+{
+    const int G = gridDim.x, b = blockIdx.x;
+    PairItem it;
+    if (a.causal) {
+        const int w = r * G + ((r & 1) ? G - 1 - b : b);
+        const int slices = a.n_items / a.n_pairs;
+        it.valid = w < a.n_items;
+        it.slice = w % slices;
+        it.pair = a.n_pairs - 1 - w / slices;
+        const int last_row = min(it.pair * 256 + 255, a.seq_q - 1);
+        const int hi = last_row + a.causal_off;  // last key any row of the item sees
+        it.nk = hi < 0 ? 1 : min(a.nk_tiles, hi / 64 + 1);
+    } else {
+        const int w = r * G + b;
+        it.valid = w < a.n_items;
+        it.slice = w / a.n_pairs;
+        it.pair = w % a.n_pairs;
+        it.nk = a.nk_tiles;
+    }
+    return it;
+}
 
 template <int D, typename OutT, int kPoly8, bool kSpec>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -143,7 +179,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     __shared__ int abort_sh;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int nk = args.nk_tiles;
 
     if (threadIdx.x == 0) {
         ptx::mbar_init(q_full, 1);
@@ -208,8 +243,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (lane == 0) {
                 int it = 0, kv = 0, k_issued = 0, v_issued = 0;
                 bool ok = true;
-                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x, it++) {
-                    const int slice = w / args.n_pairs, pair = w % args.n_pairs;
+                for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                    const PairItem item = pair_item(args, r);
+                    if (!item.valid) continue;
+                    const int slice = item.slice, pair = item.pair, nk = item.nk;
                     if (it > 0 && !wait_phase(q_empty, (it - 1) & 1, wctx, kSiteQEmpty)) break;
                     ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
 #pragma unroll
@@ -229,7 +266,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::SF_BYTES);
                         ptx::tma_load_3d(sK + ks * C::K_STRIDE, &tm_k, &k_full[ks], 0, j * BN, slice);
                         ptx::bulk_load(sKsf + ks * C::SF_BYTES,
-                                       args.k_sf + (static_cast<size_t>(slice) * nk + j) * C::SF_BYTES, C::SF_BYTES,
+                                       args.k_sf + (static_cast<size_t>(slice) * args.nk_tiles + j) * C::SF_BYTES, C::SF_BYTES,
                                        &k_full[ks]);
                         k_issued = kv + 1;
                         const int vs = kv % C::VST;
@@ -244,6 +281,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                                              c * (C::VCW / 2), j * BN, slice);
                         v_issued = kv + 1;
                     }
+                    it++;
                 }
                 // Every load this thread issued must land before the CTA exits
                 // (Q loads are at most one phase ahead of their consumer).
@@ -266,7 +304,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // g: global step (s_free phase), kv: K ring index, it: item.
                 int g = 0, kv = 0, it = 0;
                 bool ok = true;
-                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x, it++) {
+                for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                    const PairItem item = pair_item(args, r);
+                    if (!item.valid) continue;
+                    const int nk = item.nk;
                     if (!wait_phase(q_full, it & 1, wctx, kSiteQFull)) break;
                     ptx::tc_fence_after();
                     // The previous item's S MMAs are complete: the producer
@@ -305,6 +346,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     }
                     if (!ok) break;
                     ptx::tc_commit(q_empty);  // the producer may load the next item's Q
+                    it++;
                 }
                 // Drain every tcgen05 op this thread issued before TMEM is freed.
                 ptx::tc_commit(drain_bar);
@@ -319,7 +361,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 constexpr uint32_t idesc_pv = ptx::idesc_f16(128, C::NPV, true);
                 int g = 0;  // global step: p_full phase and V ring index
                 bool ok = true;
-                for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x) {
+                for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                    const PairItem item = pair_item(args, r);
+                    if (!item.valid) continue;
+                    const int nk = item.nk;
                     for (int j = 0; ok && j < nk; j++, g++) {
                         const int vs = g % C::VST;
                         if (!wait_phase(&v_full[vs], (g / C::VST) & 1, wctx, kSiteVFull)) { ok = false; break; }
@@ -360,8 +405,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
         int g = 0;  // global step: phase of s_full / s_free / p_full / pv_done
         bool ok = true;
-        for (int w = blockIdx.x; ok && w < args.n_items; w += gridDim.x) {
-            const int slice = w / args.n_pairs, pair = w % args.n_pairs;
+        for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+            const PairItem item = pair_item(args, r);
+            if (!item.valid) continue;
+            const int slice = item.slice, pair = item.pair, nk = item.nk;
+            // Keys this row sees: [0, row_lim) (the causal mask, or all keys).
+            const int qi = pair * 2 * C::BM + t * C::BM + row;
+            const int row_lim = args.causal ? min(qi + args.causal_off + 1, args.seq_k) : args.seq_k;
             float m = -INFINITY;
             for (int j = 0; j < nk; j++, g++) {
                 if (!__all_sync(0xffffffffu, wait_phase(&s_full[t], g & 1, wctx, kSiteSFull))) { ok = false; break; }
@@ -373,7 +423,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // S_t is in registers: the issuer may compute the next step into it.
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&s_free[t]);
-                const int valid = args.seq_k - j * BN;  // keys of this tile that exist
+                const int valid = row_lim - j * BN;  // keys of this step this row sees
                 uint32_t pk[NT][16];
                 // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column
                 // pairs take 2^x on the FMA pipe, the rest on MUFU.  With a true
@@ -398,16 +448,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 float alpha = 1.f;
                 bool rescale = false;
                 bool exact = true;
-                if (kSpec && j > 0 && valid >= BN) {
+                const bool spec_ok =
+                    args.causal ? __all_sync(0xffffffffu, valid >= BN && m != -INFINITY) : valid >= BN;
+                if (kSpec && j > 0 && spec_ok) {
                     // Speculative pass against the current reference max m: it
                     // stands unless some row's max grew by more than 2^8 (the lazy
                     // rescale threshold), which after the first step is rare.
                     const float mx = exps(m, std::true_type{});
                     exact = __any_sync(0xffffffffu, mx * c > m + 8.0f);
                 }
-                if (exact) {
+                if (exact && __all_sync(0xffffffffu, valid <= 0)) {
+                    // No row of this warp sees a key of this step: P = 0.
+#pragma unroll
+                    for (int k = 0; k < NT; k++)
+#pragma unroll
+                        for (int i = 0; i < 16; i++) pk[k][i] = 0u;
+                } else if (exact) {
                     // Row max first, then the exponentials: the first step, the
-                    // ragged last step, and steps where some row's max jumped.
+                    // ragged or masked steps, and steps where some row's max jumped.
                     if (valid < BN) {
 #pragma unroll
                         for (int k = 0; k < NT; k++)
@@ -432,7 +490,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         m = m_new;
                         rescale = true;
                     }
-                    (void)exps(m, std::false_type{});
+                    // A row that has seen no key yet keeps m = -inf; its P is 0.
+                    (void)exps(m == -INFINITY ? 0.f : m, std::false_type{});
                 }
                 if (j > 0) {
                     // PV_{j-1} must be done: it reads the P columns this step
@@ -477,7 +536,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 uint32_t lsum[16];
                 ptx::tmem_ld16(o_tm + C::L_COL, lsum);
                 ptx::tc_wait_ld();
-                const float inv_l = 1.0f / __uint_as_float(lsum[0]);
+                const float lv = __uint_as_float(lsum[0]);
+                const float inv_l = lv > 0.f ? 1.0f / lv : 0.f;  // a row that saw no key outputs 0
                 // O / l in 32-column chunks: each warp writes its 32 rows x 32
                 // columns to a staging buffer (swizzled like the TMA box, so the
                 // 16-byte writes of a warp hit distinct banks) and lane 0 stores

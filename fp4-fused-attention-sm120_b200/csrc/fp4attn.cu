@@ -291,6 +291,8 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     a.q_sf = fa.q_sf;
     a.k_sf = fa.k_sf;
     a.timeout_ns = fa.timeout_ns;
+    a.causal = fa.causal;
+    a.causal_off = fa.causal_off;
     // Output written by TMA stores in 32-row x 32-column boxes (64-byte rows
     // for FP16, 128-byte rows for FP32, swizzled to match the staging).
     CUtensorMap to;
@@ -428,8 +430,11 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
 }
 
 int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int sq, int sk, int d,
-              float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores)
+              float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores,
+              int mask_mode = FP4ATTN_MASK_NONE)
 {
+    if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
+        return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
     const void* dummy = workspace;
     int rc = check_problem(dummy, dummy, V, Out, in_dtype, out_dtype, batch, heads, sq, sk, d, FP4ATTN_SCALE_REFERENCE,
                            !scores);
@@ -469,6 +474,8 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     a.q_sf = ws + p.w.q_sf;
     a.k_sf = ws + p.w.k_sf;
     a.timeout_ns = wait_timeout_ns();
+    a.causal = mask_mode == FP4ATTN_MASK_CAUSAL ? 1 : 0;
+    a.causal_off = sk - sq;
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
     return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, p.slices, st);
 }
@@ -546,6 +553,31 @@ int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int 
         return rc;
     return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
                      workspace_bytes, stream, false);
+}
+
+int fp4attn_attend_masked(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                          int seq_k, int head_dim, float softmax_scale, int mask_mode, const void* workspace,
+                          size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false, mask_mode);
+}
+
+int fp4attn_forward_masked(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                           int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                           int scale_mode, int mask_mode, void* workspace, size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
+        return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
+    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, true);
+    if (rc) return rc;
+    if ((rc = do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
+                         workspace_bytes, stream, true)))
+        return rc;
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false, mask_mode);
 }
 
 int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, int batch, int heads, int seq_q,

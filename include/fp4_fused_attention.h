@@ -33,15 +33,16 @@ constexpr int dtype_code()
 
 template <int HEAD_DIM, typename InT, typename OutT>
 inline int launch(const InT* Q, const InT* K, OutT* Out, const InT* V, int seq_q, int seq_k, int heads, int batch,
-                  cudaStream_t stream)
+                  cudaStream_t stream, bool causal)
 {
     const int in = dtype_code<InT>(), out = dtype_code<OutT>();
     const size_t ws_bytes = fp4attn_workspace_size(batch, heads, seq_q, seq_k, HEAD_DIM, in);
     if (ws_bytes == 0) return FP4ATTN_EINVAL;
     void* ws = nullptr;
     if (cudaMallocAsync(&ws, ws_bytes, stream) != cudaSuccess) return FP4ATTN_ECUDA;
-    const int rc = fp4attn_forward(Q, K, V, Out, in, out, batch, heads, seq_q, seq_k, HEAD_DIM, 0.0f,
-                                   FP4ATTN_SCALE_REFERENCE, ws, ws_bytes, stream);
+    const int rc = fp4attn_forward_masked(Q, K, V, Out, in, out, batch, heads, seq_q, seq_k, HEAD_DIM, 0.0f,
+                                          FP4ATTN_SCALE_REFERENCE, causal ? FP4ATTN_MASK_CAUSAL : FP4ATTN_MASK_NONE,
+                                          ws, ws_bytes, stream);
     const cudaError_t fe = cudaFreeAsync(ws, stream);
     if (rc != FP4ATTN_OK) return rc;
     return fe == cudaSuccess ? FP4ATTN_OK : FP4ATTN_ECUDA;
@@ -50,26 +51,30 @@ inline int launch(const InT* Q, const InT* K, OutT* Out, const InT* V, int seq_q
 }  // namespace fp4attn_detail
 
 /* The reference's argument order: Q, K, Out, V, seq_q, seq_k, heads; then the
- * batch the reference infers from its grid, and a stream. */
+ * batch the reference infers from its grid, a stream, and (an extension) the
+ * bottom-right causal mask. */
 template <int HEAD_DIM>
 inline int fused_fp4_attention_launch(const float* Q, const float* K, float* Out, const float* V, int seq_q,
-                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0)
+                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0,
+                                      bool causal = false)
 {
-    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream);
+    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream, causal);
 }
 
 template <int HEAD_DIM>
 inline int fused_fp4_attention_launch(const __half* Q, const __half* K, float* Out, const __half* V, int seq_q,
-                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0)
+                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0,
+                                      bool causal = false)
 {
-    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream);
+    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream, causal);
 }
 
 template <int HEAD_DIM>
 inline int fused_fp4_attention_launch(const __half* Q, const __half* K, __half* Out, const __half* V, int seq_q,
-                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0)
+                                      int seq_k, int heads, int batch = 1, cudaStream_t stream = 0,
+                                      bool causal = false)
 {
-    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream);
+    return fp4attn_detail::launch<HEAD_DIM>(Q, K, Out, V, seq_q, seq_k, heads, batch, stream, causal);
 }
 
 #endif /* FP4_FUSED_ATTENTION_H */

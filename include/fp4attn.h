@@ -60,6 +60,15 @@ typedef enum {
     FP4ATTN_SCALE_OCP = 1
 } fp4attn_scale_mode;
 
+/* ---- attention masks ------------------------------------------------------ */
+typedef enum {
+    FP4ATTN_MASK_NONE = 0,   /* every query sees every key (the reference's only mode) */
+    /* Causal, bottom-right aligned: query i sees keys j <= i + seq_k - seq_q, so
+     * with seq_q == seq_k row i sees keys 0..i.  A query that sees no key
+     * (only possible when seq_q > seq_k) gets a zero output row. */
+    FP4ATTN_MASK_CAUSAL = 1
+} fp4attn_mask;
+
 /* ---- layouts of quantised output ---------------------------------------- */
 typedef enum {
     /* codes: rows x head_dim/2 bytes, two E2M1 codes per byte, element 2i in
@@ -115,6 +124,19 @@ int fp4attn_prepare(const void* Q, const void* K, const void* V, int in_dtype, i
  * Replaces: the main loop of the reference kernel (common.h:140-327). */
 int fp4attn_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q, int seq_k,
                    int head_dim, float softmax_scale, const void* workspace, size_t workspace_bytes, void* stream);
+
+/* fp4attn_forward and fp4attn_attend with a mask (fp4attn_mask).  With
+ * FP4ATTN_MASK_NONE they are those calls; with FP4ATTN_MASK_CAUSAL each query
+ * tile also stops reading keys after the last one it can see, so a causal
+ * problem costs about half the unmasked one.  The workspace is the same.
+ * No counterpart in the reference, which has no mask (common.h:228-265
+ * softmaxes every key of every tile). */
+int fp4attn_forward_masked(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                           int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                           int scale_mode, int mask_mode, void* workspace, size_t workspace_bytes, void* stream);
+int fp4attn_attend_masked(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                          int seq_k, int head_dim, float softmax_scale, int mask_mode, const void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* fp4attn_forward for callers that cannot allocate device memory (code running
  * during CUDA graph capture, runtimes that own all device memory, loops that

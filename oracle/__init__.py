@@ -39,6 +39,10 @@ def oracle_lib() -> ctypes.CDLL:
         L.oracle_fp4_attention.argtypes = [_f32, _f32, _f32, _f32] + [c.c_int] * 4 + [c.c_float, c.c_int, c.c_int]
         L.oracle_fp4_attention_rows.argtypes = [_f32, _f32, _f32, _f32, c.c_int, _i32, _i32, c.c_int, c.c_int,
                                                 c.c_int, c.c_float, c.c_int]
+        L.oracle_attention_causal.argtypes = [_f32, _f32, _f32, _f32, c.c_int, c.c_int, c.c_int, c.c_float,
+                                              c.c_int, c.c_int]
+        L.oracle_fp4_attention_causal.argtypes = ([_f32, _f32, _f32, _f32] + [c.c_int] * 4 +
+                                                  [c.c_float, c.c_int, c.c_int])
         L.oracle_fp4_scores.argtypes = [_f32, _f32, _f32, c.c_int, c.c_int, c.c_int, c.c_int]
         L.oracle_cosine.argtypes = [_f32, _f32, c.c_int64]
         L.oracle_cosine.restype = c.c_double
@@ -106,14 +110,26 @@ def attention(Q, K, V, scale: float = 0.0):
     return out
 
 
-def fp4_attention(Q, K, V, scale: float = 0.0, scale_mode: int = 0, threads: int = 8):
-    """The FP4 path for [slices, seq, head_dim] (or [B, H, seq, head_dim]) inputs."""
+def fp4_attention(Q, K, V, scale: float = 0.0, scale_mode: int = 0, threads: int = 8, causal: bool = False):
+    """The FP4 path for [slices, seq, head_dim] (or [B, H, seq, head_dim]) inputs.
+    causal=True applies the bottom-right causal mask (our extension; the
+    reference has none): query i sees keys j <= i + seq_k - seq_q."""
     Q, K, V = _c(Q), _c(K), _c(V)
     d = Q.shape[-1]
     sq, sk = Q.shape[-2], K.shape[-2]
     slices = Q.size // (sq * d)
     out = np.zeros(Q.shape, np.float32)
-    oracle_lib().oracle_fp4_attention(Q, K, V, out, slices, sq, sk, d, scale, scale_mode, threads)
+    fn = oracle_lib().oracle_fp4_attention_causal if causal else oracle_lib().oracle_fp4_attention
+    fn(Q, K, V, out, slices, sq, sk, d, scale, scale_mode, threads)
+    return out
+
+
+def attention_causal(Q, K, V, scale: float = 0.0, first_row: int = 0, seq_q_total=None):
+    """Unquantised FP32 causal attention of one slice (query rows first_row...)."""
+    Q, K, V = _c(Q), _c(K), _c(V)
+    out = np.zeros(Q.shape, np.float32)
+    total = Q.shape[0] if seq_q_total is None else seq_q_total
+    oracle_lib().oracle_attention_causal(Q, K, V, out, Q.shape[0], K.shape[0], Q.shape[1], scale, first_row, total)
     return out
 
 

@@ -133,6 +133,40 @@ void oracle_attention(const float* Q, const float* K, const float* V, float* Out
     free(Kt); free(row); free(acc);
 }
 
+/* The causal extension (our own; the reference has no mask): the row loop of
+ * oracle_attention restricted to the visible keys [0, lim). */
+void oracle_attention_causal(const float* Q, const float* K, const float* V, float* Out,
+                             int sq, int sk, int d, float scale, int first_row, int sq_total)
+{
+    float* row = (float*)malloc(sizeof(float) * (size_t)(sk > 0 ? sk : 1));
+    float* acc = (float*)malloc(sizeof(float) * (size_t)d);
+    if (!(scale > 0.f)) scale = 1.0f / sqrtf((float)d);
+    for (int i = 0; i < sq; i++) {
+        long lim = (long)first_row + i + sk - sq_total + 1;
+        if (lim > sk) lim = sk;
+        for (int j = 0; j < d; j++) acc[j] = 0.f;
+        if (lim > 0) {
+            for (long j = 0; j < lim; j++) {
+                float a = 0.f;
+                for (int k = 0; k < d; k++) a += Q[(size_t)i * d + k] * K[(size_t)j * d + k];
+                row[j] = a * scale;
+            }
+            float m = row[0];
+            for (long j = 1; j < lim; j++) m = fmaxf(m, row[j]);
+            float sum = 0.f;
+            for (long j = 0; j < lim; j++) { row[j] = expf(row[j] - m); sum += row[j]; }
+            for (long j = 0; j < lim; j++) row[j] /= sum;
+            for (long k = 0; k < lim; k++) {
+                float p = row[k];
+                const float* v = V + (size_t)k * d;
+                for (int j = 0; j < d; j++) acc[j] += p * v[j];
+            }
+        }
+        for (int j = 0; j < d; j++) Out[(size_t)i * d + j] = acc[j];
+    }
+    free(row); free(acc);
+}
+
 static void quant_dequant(const float* x, int64_t rows, int d, int mode, float* out)
 {
     uint8_t* codes = (uint8_t*)malloc((size_t)rows * d);
@@ -145,6 +179,7 @@ static void quant_dequant(const float* x, int64_t rows, int d, int mode, float* 
 typedef struct {
     const float *Q, *K, *V; float* Out;
     int s0, s1, sq, sk, d, mode; float scale;
+    int causal;
 } slice_job;
 
 static void* run_slices(void* arg)
@@ -156,15 +191,18 @@ static void* run_slices(void* arg)
     for (int s = j->s0; s < j->s1; s++) {
         quant_dequant(j->Q + s * qn, j->sq, j->d, j->mode, qd);
         quant_dequant(j->K + s * kn, j->sk, j->d, j->mode, kd);
-        oracle_attention(qd, kd, j->V + s * kn, j->Out + s * qn, j->sq, j->sk, j->d, j->scale);
+        if (j->causal)
+            oracle_attention_causal(qd, kd, j->V + s * kn, j->Out + s * qn, j->sq, j->sk, j->d, j->scale, 0, j->sq);
+        else
+            oracle_attention(qd, kd, j->V + s * kn, j->Out + s * qn, j->sq, j->sk, j->d, j->scale);
     }
     free(qd); free(kd);
     return NULL;
 }
 
-void oracle_fp4_attention(const float* Q, const float* K, const float* V, float* Out,
-                          int slices, int sq, int sk, int d, float scale, int mode,
-                          int threads)
+static void fp4_attention_slices(const float* Q, const float* K, const float* V, float* Out,
+                                 int slices, int sq, int sk, int d, float scale, int mode,
+                                 int threads, int causal)
 {
     if (threads < 1) threads = 1;
     if (threads > slices) threads = slices;
@@ -172,12 +210,26 @@ void oracle_fp4_attention(const float* Q, const float* K, const float* V, float*
     slice_job* jobs = (slice_job*)malloc(sizeof(slice_job) * threads);
     for (int t = 0; t < threads; t++) {
         slice_job jb = {Q, K, V, Out, slices * t / threads, slices * (t + 1) / threads,
-                        sq, sk, d, mode, scale};
+                        sq, sk, d, mode, scale, causal};
         jobs[t] = jb;
         pthread_create(&tid[t], NULL, run_slices, &jobs[t]);
     }
     for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
     free(tid); free(jobs);
+}
+
+void oracle_fp4_attention(const float* Q, const float* K, const float* V, float* Out,
+                          int slices, int sq, int sk, int d, float scale, int mode,
+                          int threads)
+{
+    fp4_attention_slices(Q, K, V, Out, slices, sq, sk, d, scale, mode, threads, 0);
+}
+
+void oracle_fp4_attention_causal(const float* Q, const float* K, const float* V, float* Out,
+                                 int slices, int sq, int sk, int d, float scale, int mode,
+                                 int threads)
+{
+    fp4_attention_slices(Q, K, V, Out, slices, sq, sk, d, scale, mode, threads, 1);
 }
 
 void oracle_fp4_attention_rows(const float* Q, const float* K, const float* V,

@@ -50,6 +50,20 @@ void oracle_quantize(const float* x, int64_t rows, int head_dim,
 void oracle_dequantize(const uint8_t* codes, const uint8_t* scales, int64_t rows,
                        int head_dim, float* out);
 
+/* Causal variant of oracle_attention -- not part of the reference, which has
+ * no mask: query row i of this call is row first_row + i of a sequence of
+ * seq_q_total queries and sees keys j <= first_row + i + seq_k - seq_q_total
+ * (bottom-right alignment); a row that sees no key gets a zero output.  The
+ * arithmetic of every visible element is that of oracle_attention. */
+void oracle_attention_causal(const float* Q, const float* K, const float* V, float* Out,
+                             int seq_q, int seq_k, int head_dim, float scale,
+                             int first_row, int seq_q_total);
+
+/* oracle_fp4_attention with the causal mask of oracle_attention_causal. */
+void oracle_fp4_attention_causal(const float* Q, const float* K, const float* V, float* Out,
+                                 int slices, int seq_q, int seq_k, int head_dim,
+                                 float scale, int scale_mode, int threads);
+
 /* cpu_attention (tests/test_attention.cu:33-54) for one (batch, head) slice,
  * FP32 throughout: S = Q K^T, S *= scale, row softmax with expf, Out = P V.
  * scale <= 0 selects 1/sqrt(head_dim) as the reference does (:46). */

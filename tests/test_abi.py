@@ -123,3 +123,11 @@ def test_cpp_launcher_header_compiles_and_links(tmp_path, fa):
     subprocess.run(["g++", "-std=c++17", "-Wall", "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include",
                     str(src), "-L", libdir, "-lfp4attn", "-L", "/usr/local/cuda/lib64", "-lcudart",
                     f"-Wl,-rpath,{libdir}", "-o", str(tmp_path / "use")], check=True)
+
+
+def test_masked_entry_points_reject_bad_mask(fa):
+    L = fa.lib()
+    assert L.fp4attn_forward_masked(16, 16, 16, 16, fa.F16, fa.F32, 1, 1, 64, 128, 128, 0.0, 0, 7, 256, 1 << 30,
+                                    None) == fa.EINVAL
+    assert b"mask_mode" in L.fp4attn_last_error()
+    assert L.fp4attn_attend_masked(16, 16, fa.F16, fa.F32, 1, 1, 64, 128, 128, 0.0, -1, 256, 1 << 30, None) == fa.EINVAL

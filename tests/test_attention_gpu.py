@@ -239,3 +239,65 @@ def test_fma_pipe_exp2_error_bound(fa, cuda):
     assert rel <= 7.6e-5, rel
     low = x <= -126.0
     assert (y[low] < 2.0 ** -125).all() and (y[low] >= 0).all()
+
+
+# ---- causal mask (an extension: the reference has no mask) -----------------
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 160, 256])
+@pytest.mark.parametrize("sq,sk", [(1, 1), (64, 65), (129, 127), (300, 300), (200, 513), (513, 200)])
+def test_causal_shapes(fa, cuda, d, sq, sk):
+    """Bottom-right causal mask: query i sees keys j <= i + sk - sq; with
+    sq > sk the first sq - sk rows see no key and must come out as zeros."""
+    g = torch.Generator().manual_seed(d * 1000 + sq + sk)
+    Q, K, V = (torch.randn(2, sq, d, generator=g), torch.randn(2, sk, d, generator=g),
+               torch.randn(2, sk, d, generator=g))
+    Q, K, V = [x.half().float().numpy() for x in (Q, K, V)]
+    t = [torch.from_numpy(np.ascontiguousarray(a)).half().cuda()[None] for a in (Q, K, V)]
+    out = fa.fused_fp4_attention(*t, out_dtype=torch.float32, causal=True)
+    assert fa.status_query() == fa.OK
+    got = out[0].cpu().numpy()
+    want = oracle.fp4_attention(Q, K, V, causal=True)
+    if sq > sk:
+        assert np.abs(got[:, :sq - sk]).max() == 0.0
+    assert_close(got, want)
+
+
+def test_causal_many_items_and_split_api(fa, cuda):
+    """Several 256-row work items per slice, each stopping at its own last key
+    tile; fp4attn_prepare + fp4attn_attend_masked gives the same bytes as
+    fp4attn_forward_masked."""
+    g = torch.Generator().manual_seed(77)
+    sq = sk = 1500
+    Q, K, V = (torch.randn(1, 3, sq, 128, generator=g).half().cuda() for _ in range(3))
+    out = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float32, causal=True)
+    ws = torch.empty(fa.workspace_size(1, 3, sq, sk, 128), dtype=torch.uint8, device="cuda")
+    out2 = torch.empty_like(out)
+    fa.prepare(Q, K, V, ws)
+    fa.attend(V, out2, ws, fa.F16, 1, 3, sq, sk, 128, causal=True)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(out, out2)
+    want = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy(),
+                                causal=True)
+    assert_close(out[0].cpu().numpy(), want)
+
+
+def test_causal_full_prefill_sampled_rows(fa, cuda):
+    """The bench shape (B2 H32 sq=sk=4096 d128, FP16 out) under the causal
+    mask, checked on sampled rows of sampled slices against the oracle."""
+    import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS["prefill_4k"]
+    Q, K, V = wl.make_inputs(w, 1)
+    Q, K, V = Q[None], K[None], V[None]
+    out = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float16, causal=True)
+    assert fa.status_query() == fa.OK
+    rng = np.random.default_rng(5)
+    for s in (0, 37, 63):
+        kq = K[0, s].float().cpu().numpy()
+        kd = oracle.dequantize(*oracle.quantize(kq))
+        vs = V[0, s].float().cpu().numpy()
+        for r in sorted(rng.choice(4096, 6, replace=False).tolist()) + [0, 4095]:
+            q = Q[0, s, r:r + 1].float().cpu().numpy()
+            qd = oracle.dequantize(*oracle.quantize(q))
+            want = oracle.attention_causal(qd, kd, vs, first_row=r, seq_q_total=4096)
+            got = out[0, s, r:r + 1].float().cpu().numpy()
+            assert_close(got, want)
