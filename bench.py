@@ -367,7 +367,7 @@ def main():
             "frac_of_mixed_roofline_step": value / world / peak,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 2 * args.steps,  # per step: one quantise launch (Q and K) + one attention launch
             "clocks": sampler.summary(t_wall0, t_wall1),
             "device_status": int(status_max),
         }

@@ -178,9 +178,7 @@ int grid_for(int64_t work, int per_block = 256)
     return static_cast<int>(b < 1 ? 1 : b);
 }
 
-template <typename InT>
-int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slices, int seq, int d, int tile_rows,
-                       int ntiles, int ocp, cudaStream_t st)
+fp4attn::QuantTileArgs quant_args(int64_t slices, int seq, int d, int tile_rows, int ntiles, int ocp)
 {
     fp4attn::QuantTileArgs a;
     a.slices = slices;
@@ -192,16 +190,24 @@ int launch_quant_tiles(const void* x, uint8_t* codes, uint8_t* sf, int64_t slice
     a.ntiles = ntiles;
     a.sf_tile_bytes = sf_tile_bytes(d, tile_rows);
     a.ocp_mode = ocp;
-    const int per_slice = a.ntiles * tile_rows * (a.padded_dim / 32);
-    const int gx = static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
-    dim3 grid(gx, static_cast<unsigned>(slices));
-    const InT* xp = static_cast<const InT*>(x);
-    switch (a.padded_dim / 32) {
-        case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
-        case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
-        case 6: fp4attn::quantize_tiles_kernel<InT, 6><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
-        case 8: fp4attn::quantize_tiles_kernel<InT, 8><<<grid, 256, 0, st>>>(xp, codes, sf, a); break;
-        default: return fail(FP4ATTN_EUNSUPPORTED, "padded head_dim %d", a.padded_dim);
+    return a;
+}
+
+// Q and K quantised by one launch (grid z = 0 for Q, 1 for K).
+template <typename InT>
+int launch_quant_qk(const fp4attn::QuantJob& q, const fp4attn::QuantJob& k, int64_t slices, cudaStream_t st)
+{
+    auto gx_for = [&](const fp4attn::QuantTileArgs& a) {
+        const int per_slice = a.ntiles * a.tile_rows * (a.padded_dim / 32);
+        return static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
+    };
+    dim3 grid(std::max(gx_for(q.a), gx_for(k.a)), static_cast<unsigned>(slices), 2);
+    switch (q.a.padded_dim / 32) {
+        case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(q, k); break;
+        case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(q, k); break;
+        case 6: fp4attn::quantize_tiles_kernel<InT, 6><<<grid, 256, 0, st>>>(q, k); break;
+        case 8: fp4attn::quantize_tiles_kernel<InT, 8><<<grid, 256, 0, st>>>(q, k); break;
+        default: return fail(FP4ATTN_EUNSUPPORTED, "padded head_dim %d", q.a.padded_dim);
     }
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
@@ -413,12 +419,12 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     const int bn = block_n_for(d);
     const int nq_sf = q_sf_tiles(sq, d), nk_sf = (sk + bn - 1) / bn;
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
+    const fp4attn::QuantJob jq{Q, ws + p.w.q_codes, ws + p.w.q_sf, quant_args(p.slices, sq, d, 128, nq_sf, ocp)};
+    const fp4attn::QuantJob jk{K, ws + p.w.k_codes, ws + p.w.k_sf, quant_args(p.slices, sk, d, bn, nk_sf, ocp)};
     if (in_dtype == FP4ATTN_F16) {
-        if ((rc = launch_quant_tiles<__half>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, nq_sf, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<__half>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, nk_sf, ocp, st))) return rc;
+        if ((rc = launch_quant_qk<__half>(jq, jk, p.slices, st))) return rc;
     } else {
-        if ((rc = launch_quant_tiles<float>(Q, ws + p.w.q_codes, ws + p.w.q_sf, p.slices, sq, d, 128, nq_sf, ocp, st))) return rc;
-        if ((rc = launch_quant_tiles<float>(K, ws + p.w.k_codes, ws + p.w.k_sf, p.slices, sk, d, bn, nk_sf, ocp, st))) return rc;
+        if ((rc = launch_quant_qk<float>(jq, jk, p.slices, st))) return rc;
         if (need_v) {
             const int64_t n4 = p.slices * static_cast<int64_t>(sk) * d / 4;
             fp4attn::f32_to_f16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4*>(V),

@@ -206,19 +206,31 @@ struct QuantTileArgs {
     int ocp_mode;
 };
 
-// Quantise into the layout the attention kernel loads with TMA:
-// codes [slices][seq][DP/2] (blocks beyond D are zero) and scale tiles
-// [slices][ntiles][sf_tile_bytes].  Rows past seq inside the last tile get
-// scale 127 so the (zero-filled) padding never multiplies an undefined scale.
-// A reference scale of 255 only occurs with all-zero codes and is stored as
-// 254, which the MMA reads as a finite 2^127 (255 would be NaN in E8M0).
-// Grid: x covers one slice's padded rows (4 lanes per block, kNB blocks of 32
-// per row), y is the slice, so all index arithmetic is 32-bit with a
-// compile-time divisor.
+// One tensor to quantise into the layout the attention kernel loads with TMA.
+struct QuantJob {
+    const void* x;      // [slices][seq][head_dim] of InT
+    uint8_t* codes;     // [slices][seq][DP/2]
+    uint8_t* sf;        // [slices][ntiles][sf_tile_bytes]
+    QuantTileArgs a;
+};
+
+// Quantise Q (blockIdx.z == 0) and K (blockIdx.z == 1) in one launch into the
+// layout the attention kernel loads with TMA: codes [slices][seq][DP/2]
+// (blocks beyond D are zero) and scale tiles [slices][ntiles][sf_tile_bytes].
+// Rows past seq inside the last tile get scale 127 so the (zero-filled)
+// padding never multiplies an undefined scale.  A reference scale of 255 only
+// occurs with all-zero codes and is stored as 254, which the MMA reads as a
+// finite 2^127 (255 would be NaN in E8M0).  Grid: x covers one slice's padded
+// rows (kNB blocks of 32 per row, one lane per block), y is the slice, so all
+// index arithmetic is 32-bit with a compile-time divisor.
 template <typename InT, int kNB>
-__global__ void __launch_bounds__(256) quantize_tiles_kernel(const InT* __restrict__ x, uint8_t* __restrict__ codes,
-                                                             uint8_t* __restrict__ sf, QuantTileArgs a)
+__global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, const QuantJob jk)
 {
+    const bool is_k = blockIdx.z != 0;
+    const QuantTileArgs a = is_k ? jk.a : jq.a;
+    const InT* x = static_cast<const InT*>(is_k ? jk.x : jq.x);
+    uint8_t* codes = is_k ? jk.codes : jq.codes;
+    uint8_t* sf = is_k ? jk.sf : jq.sf;
     const int seq_pad = a.ntiles * a.tile_rows;
     const int total = seq_pad * kNB;  // blocks of 32 in this slice (padded rows included)
     const int64_t slice = blockIdx.y;
