@@ -24,7 +24,7 @@
 //               (its partner computes the same value), so the two halves never
 //               wait on each other.  Online max/sum in FP32 (log2 domain), P_j stored as FP16
 //               with tcgen05.st, lazy O rescale (only when the row max grows
-//               by more than 2^8), final O / l for its half of the columns.
+//               by more than 2^15), final O / l for its half of the columns.
 //
 // TMEM columns (512 allocated): S0 [0,BN), S1 [BN,2BN), O [2BN, 2BN+D),
 // P [.., +BN/2), then the Q scale columns and KST stages of K scale columns.
@@ -42,6 +42,11 @@
 #include "ptx_sm100.cuh"
 
 namespace fp4attn {
+
+// Lazy O rescale: O and l keep a reference max until a row's max has grown
+// past it by more than 2^kLazyRescaleLog2.  P is then at most 2^15, finite in
+// FP16 (max 65504), whose relative precision does not depend on magnitude.
+constexpr float kLazyRescaleLog2 = 15.0f;
 
 // Device error word: [0] status code, [1] wait site, [2] block x, [3] block y.
 __device__ int g_fp4attn_error[4];
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 bool rescale = false;
                 if (j == 0) {
                     m = m_new;
-                } else if (m_new > m + 8.0f) {
+                } else if (m_new > m + kLazyRescaleLog2) {
                     alpha = ptx::ex2_approx(m - m_new);
                     m = m_new;
                     rescale = true;

@@ -448,14 +448,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 float alpha = 1.f;
                 bool rescale = false;
                 bool exact = true;
+                float spec_mx = 0.f;  // row max from the speculative pass, when it ran
                 const bool spec_ok =
                     args.causal ? __all_sync(0xffffffffu, valid >= BN && m != -INFINITY) : valid >= BN;
                 if (kSpec && j > 0 && spec_ok) {
                     // Speculative pass against the current reference max m: it
-                    // stands unless some row's max grew by more than 2^8 (the lazy
+                    // stands unless some row's max grew by more than 2^15 (the lazy
                     // rescale threshold), which after the first step is rare.
                     const float mx = exps(m, std::true_type{});
-                    exact = __any_sync(0xffffffffu, mx * c > m + 8.0f);
+                    spec_mx = mx;
+                    exact = __any_sync(0xffffffffu, mx * c > m + kLazyRescaleLog2);
                 }
                 if (exact && __all_sync(0xffffffffu, valid <= 0)) {
                     // No row of this warp sees a key of this step: P = 0.
@@ -466,26 +468,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 } else if (exact) {
                     // Row max first, then the exponentials: the first step, the
                     // ragged or masked steps, and steps where some row's max jumped.
-                    if (valid < BN) {
+                    float row_max;
+                    if (kSpec && j > 0 && spec_ok) {
+                        row_max = spec_mx;  // a failed speculative pass already formed it (no masking there)
+                    } else {
+                        if (valid < BN) {
+#pragma unroll
+                            for (int k = 0; k < NT; k++)
+#pragma unroll
+                                for (int i = 0; i < 32; i++)
+                                    if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
+                        }
+                        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
                         for (int k = 0; k < NT; k++)
 #pragma unroll
-                            for (int i = 0; i < 32; i++)
-                                if (32 * k + i >= valid) sr[k][i] = __float_as_uint(-INFINITY);
+                            for (int i = 0; i < 32; i += 2)
+                                mx4[(i >> 1) & 3] = ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]),
+                                                               __uint_as_float(sr[k][i + 1]));
+                        row_max = ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
                     }
-                    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int k = 0; k < NT; k++)
-#pragma unroll
-                        for (int i = 0; i < 32; i += 2)
-                            mx4[(i >> 1) & 3] =
-                                ptx::fmax3(mx4[(i >> 1) & 3], __uint_as_float(sr[k][i]), __uint_as_float(sr[k][i + 1]));
-                    const float m_new = fmaxf(m, ptx::fmax3(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3])) * c);
+                    const float m_new = fmaxf(m, row_max * c);
                     if (j == 0) {
                         m = m_new;
-                    } else if (m_new > m + 8.0f) {
+                    } else if (m_new > m + kLazyRescaleLog2) {
                         // Lazy rescale: O and l keep the old reference max until
-                        // the row max has grown by more than 2^8.
+                        // the row max has grown by more than 2^15.
                         alpha = ptx::ex2_approx(m - m_new);
                         m = m_new;
                         rescale = true;

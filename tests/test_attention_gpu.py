@@ -117,19 +117,21 @@ def test_large_outliers(fa, cuda):
     assert_close(out, oracle.fp4_attention(Q, K, V))
 
 
+@pytest.mark.parametrize("growth", [3, 4, 6])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
-def test_row_max_jumps_at_later_key_tiles(fa, cuda, out_dtype):
-    """Scores that grow from one 64-key tile to the next by more than the
-    lazy-rescale threshold (2^8) for half of the rows (about half of the steps
-    of each such row): those rows take the max-first path and rescale O at
-    steps after the first, the other rows keep their reference max; the last
-    key tile is ragged."""
+def test_row_max_jumps_at_later_key_tiles(fa, cuda, out_dtype, growth):
+    """Scores of half of the rows grow from one 64-key tile to the next by
+    about 10 (growth 3), 14 (growth 4) or 20 (growth 6) in log2 units.  Below
+    the lazy-rescale threshold (2^15) P values up to ~2^14 enter FP16 and the
+    P.V MMA with no rescale; above it those rows take the max-first path and
+    rescale O at steps after the first.  The other rows keep their reference
+    max; the last key tile is ragged."""
     g = torch.Generator().manual_seed(11)
     sq, sk = 300, 64 * 9 + 17
     Q, K, V = (torch.randn(3, sq, 128, generator=g), torch.randn(3, sk, 128, generator=g),
                torch.randn(3, sk, 128, generator=g))
     for k in range(10):
-        K[:, 64 * k:64 * (k + 1)] *= 1 + 3 * k
+        K[:, 64 * k:64 * (k + 1)] *= 1 + growth * k
     Q[:, 1::2] *= 0.02
     Q, K, V = [x.half().float().numpy() for x in (Q, K, V)]
     out = run_fwd(fa, Q, K, V, out_dtype=out_dtype)
