@@ -552,6 +552,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // the box with TMA; rows past seq_q are clipped by the tensor map.
                 constexpr int OB = 32 * static_cast<int>(sizeof(OutT));  // bytes per staged row
                 const int grow0 = pair * 2 * C::BM + t * C::BM + wq * 32;
+                // The previous item's stores (long finished) must be done
+                // reading the staging buffers before they are rewritten.
+                if (lane == 0) ptx::bulk_wait_group_read<0>();
+                __syncwarp();
 #pragma unroll 1
                 for (int k = 0; k < D / 32; k++) {
                     uint32_t o[32];
@@ -587,9 +591,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::bulk_commit_group();
                     }
                 }
-                // The next item's epilogue reuses the staging buffers.
-                if (lane == 0) ptx::bulk_wait_group_read<0>();
-                __syncwarp();
             }
         }
         // Shared memory must outlive the stores that read it.
