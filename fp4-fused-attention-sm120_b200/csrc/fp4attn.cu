@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -131,32 +132,76 @@ CUtensorMapSwizzle swizzle_for(int bytes)
     return bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
 }
 
+// Per-device set-up, done once per device on its first use from any host
+// thread: check for an sm_100 GPU, upload the scale-rule table to that
+// device's constant memory, and record its SM count.
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    bool done = false;
+    int status = FP4ATTN_OK;
+    std::string msg;
+    int sms = 0;
+};
+std::mutex g_dev_mu;
+DeviceState g_dev[kMaxDevices];
+
+int current_device(int* dev)
+{
+    if (cudaGetDevice(dev) != cudaSuccess) return fail(FP4ATTN_ECUDA, "no CUDA device");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(FP4ATTN_EUNSUPPORTED, "device index %d", *dev);
+    return FP4ATTN_OK;
+}
+
 int device_ready()
 {
-    static std::once_flag once;
-    static int status = FP4ATTN_OK;
-    static std::string msg;
-    std::call_once(once, [] {
-        int dev = 0;
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    DeviceState& d = g_dev[dev];
+    if (!d.done) {
+        d.done = true;
         cudaDeviceProp prop;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
-            status = FP4ATTN_ECUDA;
-            msg = "no CUDA device";
-            return;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+            d.status = FP4ATTN_ECUDA;
+            d.msg = "could not query the CUDA device";
+        } else if (prop.major != 10) {
+            d.status = FP4ATTN_EUNSUPPORTED;
+            d.msg = "libfp4attn requires an sm_100 (B200-class) GPU; found sm_" + std::to_string(prop.major) +
+                    std::to_string(prop.minor);
+        } else if (cudaMemcpyToSymbol(fp4attn::kLog2CeilCompat, kLog2CeilCompatInit, sizeof kLog2CeilCompatInit) !=
+                   cudaSuccess) {
+            d.status = FP4ATTN_ECUDA;
+            d.msg = "could not upload the scale table";
+        } else {
+            d.sms = prop.multiProcessorCount;
         }
-        if (prop.major != 10) {
-            status = FP4ATTN_EUNSUPPORTED;
-            msg = "libfp4attn requires an sm_100 (B200-class) GPU; found sm_" + std::to_string(prop.major) +
-                  std::to_string(prop.minor);
-            return;
-        }
-        if (cudaMemcpyToSymbol(fp4attn::kLog2CeilCompat, kLog2CeilCompatInit, sizeof kLog2CeilCompatInit) !=
-            cudaSuccess) {
-            status = FP4ATTN_ECUDA;
-            msg = "could not upload the scale table";
-        }
-    });
-    if (status != FP4ATTN_OK) return fail(status, "%s", msg.c_str());
+    }
+    if (d.status != FP4ATTN_OK) return fail(d.status, "%s", d.msg.c_str());
+    return FP4ATTN_OK;
+}
+
+// SM count of the current device (device_ready() has run on it).
+int device_sms()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 1;
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    return g_dev[dev].sms > 0 ? g_dev[dev].sms : 1;
+}
+
+// Sets a kernel's dynamic shared memory limit once per device; `done_mask`
+// (one bit per device) belongs to the calling launcher, i.e. to one kernel.
+template <typename Kern>
+int set_smem_once(Kern kern, int bytes, std::atomic<unsigned long long>& done_mask)
+{
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    const unsigned long long bit = 1ull << dev;
+    if (done_mask.load(std::memory_order_acquire) & bit) return FP4ATTN_OK;
+    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done_mask.fetch_or(bit, std::memory_order_release);
     return FP4ATTN_OK;
 }
 
@@ -221,17 +266,20 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     auto kern = fp4attn::fp4_attention_fwd_kernel<D, BN, OutT, kScores, kPoly8>;
     // The kernel re-splits its launch registers with setmaxnreg; refuse to
     // launch unless the pool it was given covers the split.
-    static int launch_regs = -1;
+    static std::atomic<int> launch_regs_cache{-1};
+    int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
         cudaFuncAttributes attr;
         FP4_CUDA(cudaFuncGetAttributes(&attr, kern));
         launch_regs = attr.numRegs;
+        launch_regs_cache.store(launch_regs, std::memory_order_relaxed);
     }
     if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::kCtlRegs + 256 * fp4attn::kSmRegs ||
         launch_regs > fp4attn::kLaunchRegs)
         return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
                     launch_regs, fp4attn::kLaunchRegs);
-    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    static std::atomic<unsigned long long> smem_set{0};
+    if (int rc = set_smem_once(kern, C::SMEM_BYTES, smem_set)) return rc;
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
     dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
     kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
@@ -275,17 +323,20 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 {
     using C = fp4attn::PairCfg<D>;
     auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec>;
-    static int launch_regs = -1;
+    static std::atomic<int> launch_regs_cache{-1};
+    int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
         cudaFuncAttributes attr;
         FP4_CUDA(cudaFuncGetAttributes(&attr, kern));
         launch_regs = attr.numRegs;
+        launch_regs_cache.store(launch_regs, std::memory_order_relaxed);
     }
     if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::kCtlRegs + 256 * fp4attn::kSmRegs ||
         launch_regs > fp4attn::kLaunchRegs)
         return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
                     launch_regs, fp4attn::kLaunchRegs);
-    FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    static std::atomic<unsigned long long> smem_set{0};
+    if (int rc = set_smem_once(kern, C::SMEM_BYTES, smem_set)) return rc;
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
     fp4attn::PairArgs a;
     a.seq_q = fa.seq_q;
@@ -312,10 +363,7 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     const int64_t items = static_cast<int64_t>(a.n_pairs) * slices;
     if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
     a.n_items = static_cast<int>(items);
-    int dev = 0, sms = 0;
-    FP4_CUDA(cudaGetDevice(&dev));
-    FP4_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, std::max(sms, 1)));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
     kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;

@@ -87,3 +87,25 @@ def test_empty_input(fa, cuda):
     x = torch.empty(0, 128, dtype=torch.float16, device="cuda")
     c, s = fa.quantize(x)
     assert c.numel() == 0 and s.numel() == 0 and fa.status_query() == fa.OK
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_devices_in_one_process(fa, cuda):
+    """One host process quantising on two devices: each device gets its own
+    copy of the scale-rule table, so values where the reference's log2f rounds
+    down come out bit-exact on the second device too."""
+    vals = []
+    for p in range(-126, 128):
+        vals += [((p + 127) << 23) + k for k in range(0, 26)]
+    xs = np.array(vals, np.uint32).view(np.float32)
+    blocks = np.zeros((xs.size, 32), np.float32)
+    blocks[:, 0] = xs
+    blocks[:, 1] = -xs / 3
+    oc, os_ = oracle.quantize(blocks)
+    for dev in (0, 1, 0):
+        with torch.cuda.device(dev):
+            x = torch.from_numpy(blocks).to(f"cuda:{dev}")
+            c, s = fa.quantize(x)
+            torch.cuda.synchronize(dev)
+            assert np.array_equal(s.cpu().numpy(), os_)
+            assert np.array_equal(c.cpu().numpy(), oracle.pack_codes(oc))
