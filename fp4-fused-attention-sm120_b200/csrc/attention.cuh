@@ -91,10 +91,16 @@ struct FwdCfg {
     static constexpr int OFF_V = align1k(OFF_KSF + KST * KSF_BYTES);
     static constexpr int V_STRIDE = align1k(V_BYTES);
     static constexpr int OFF_REDL = OFF_V + VST * V_STRIDE;    // [2 halves][128 rows] f32 row sums
-    static constexpr int OFF_BAR = OFF_REDL + 2 * 128 * 4;
+    // Output staging: per softmax warp two buffers of 32 rows x OCH_E columns
+    // (sized for FP32), written swizzled and sent out by TMA stores.
+    static constexpr int OCH_E = (D / 2) % 32 == 0 ? 32 : 16;
+    static constexpr int OST_BYTES = 32 * OCH_E * 4;
+    static constexpr int OFF_OST = OFF_REDL + 2 * 128 * 4;
+    static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
     // q_full, K ring, V ring, s_full[2], p_full[2], pv_done, drain
     static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
 
 struct FwdArgs {
@@ -189,7 +195,8 @@ static_assert((kCtlRegs + 2 * kSmRegs) * 32 <= 16384, "register split exceeds a 
 template <int D, int BN, typename OutT, bool kScores, int kPoly8 = 3>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_v, const FwdArgs args)
+                             const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                             const FwdArgs args)
 {
     using C = FwdCfg<D, BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -249,7 +256,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (warp == 0 && lane == 0) {
         ptx::prefetch_tmap(&tm_q);
         ptx::prefetch_tmap(&tm_k);
-        if (!kScores) ptx::prefetch_tmap(&tm_v);
+        if (!kScores) {
+            ptx::prefetch_tmap(&tm_v);
+            ptx::prefetch_tmap(&tm_o);
+        }
     }
     if (warp == 1) {
         ptx::tmem_alloc(&tmem_base_sh, 512);
@@ -414,7 +424,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         };
         if (kScores) {
             for (int j = 0; j < nk; j++) {
-                if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull))) {
+                    ok = false;
+                    break;
+                }
                 ptx::tc_fence_after();
                 uint32_t sr[NT][32];
                 load_s(j, sr);
@@ -443,7 +456,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             // Keys this row sees: [0, row_lim) (the causal mask, or all keys).
             const int row_lim = causal ? min(q0 + row + args.causal_off + 1, args.seq_k) : args.seq_k;
             for (int j = 0; j < nk; j++) {
-                if (!wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull)) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull))) {
+                    ok = false;
+                    break;
+                }
                 ptx::tc_fence_after();
                 uint32_t sr[NF][32];
                 {
@@ -510,7 +526,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     // PV_{j-1} must be done: it reads the P columns this step
                     // overwrites, and O is rescaled below (waiting every phase
                     // also keeps this barrier's parity unambiguous).
-                    if (!wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
+                    if (!__all_sync(0xffffffffu, wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone))) {
+                        ok = false;
+                        break;
+                    }
                     ptx::tc_fence_after();
                 }
                 const uint32_t p_tm = tmem + lane_off + C::P_COL + half * (HC / 2);
@@ -546,44 +565,59 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             red_l[half * 128 + row] = l;
             ptx::named_bar_sync(1 + wq, 64);
             const float l_tot = l + red_l[(1 - half) * 128 + row];
-            if (wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone)) {
+            // Waits are decided per warp (__all_sync) so that warp-wide steps stay uniform.
+            if (__all_sync(0xffffffffu, wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone))) {
                 ptx::tc_fence_after();
                 const float inv_l = l_tot > 0.f ? 1.0f / l_tot : 0.f;  // a row that saw no key outputs 0
-                const int grow = q0 + row;
-                OutT* dst = reinterpret_cast<OutT*>(args.out) + (static_cast<size_t>(slice) * args.seq_q + grow) * D +
-                            half * HD;
+                // O / l in OCH_E-column chunks: each warp writes its 32 rows
+                // to a staging buffer (swizzled like the TMA box, so a warp's
+                // 16-byte writes hit distinct banks) and lane 0 stores the box
+                // with TMA; rows past seq_q are clipped by the tensor map.
+                constexpr int OE = C::OCH_E;
+                constexpr int OB = OE * static_cast<int>(sizeof(OutT));  // bytes per staged row (32, 64, 128)
+                uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
 #pragma unroll 1
-                for (int t = 0; t < HD / OCH; t++) {
-                    uint32_t o[OCH];
-                    if constexpr (OCH == 32) {
-                        ptx::tmem_ld32(tmem + lane_off + C::O_COL + half * HD + OCH * t, o);
+                for (int t = 0; t < HD / OE; t++) {
+                    uint32_t o[OE];
+                    if constexpr (OE == 32) {
+                        ptx::tmem_ld32(tmem + lane_off + C::O_COL + half * HD + OE * t, o);
                     } else {
-                        ptx::tmem_ld16(tmem + lane_off + C::O_COL + half * HD + OCH * t, o);
+                        ptx::tmem_ld16(tmem + lane_off + C::O_COL + half * HD + OE * t, o);
                     }
                     ptx::tc_wait_ld();
-                    if (grow < args.seq_q) {
-                        if constexpr (sizeof(OutT) == 4) {
+                    uint8_t* buf = ost + (t & 1) * C::OST_BYTES;
+                    if (t >= 2) {
+                        // The store that last read this buffer must be done with it.
+                        if (lane == 0) ptx::bulk_wait_group_read<1>();
+                        __syncwarp();
+                    }
+                    uint32_t ov[OB / 4];
+                    if constexpr (sizeof(OutT) == 4) {
 #pragma unroll
-                            for (int i = 0; i < OCH; i += 4) {
-                                float4 v = make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
-                                                       __uint_as_float(o[i + 2]) * inv_l,
-                                                       __uint_as_float(o[i + 3]) * inv_l);
-                                *reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + OCH * t + i) = v;
-                            }
-                        } else {
+                        for (int i = 0; i < OE; i++) ov[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
+                    } else {
 #pragma unroll
-                            for (int i = 0; i < OCH; i += 8) {
-                                uint32_t w[4];
+                        for (int i = 0; i < OE / 2; i++)
+                            ov[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+                    }
+                    // 16-byte unit u of row `lane` sits at unit u ^ (address bits 7 and up):
+                    // SWIZZLE_128B / 64B / 32B for 128- / 64- / 32-byte rows.
 #pragma unroll
-                                for (int k = 0; k < 4; k++)
-                                    w[k] = ptx::pack_half2(__uint_as_float(o[i + 2 * k]) * inv_l,
-                                                           __uint_as_float(o[i + 2 * k + 1]) * inv_l);
-                                *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(dst) + OCH * t + i) =
-                                    make_uint4(w[0], w[1], w[2], w[3]);
-                            }
-                        }
+                    for (int u = 0; u < OB / 16; u++) {
+                        const int pu = OB == 128 ? (u ^ (lane & 7)) : OB == 64 ? (u ^ ((lane >> 1) & 3)) : (u ^ ((lane >> 2) & 1));
+                        *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
+                            make_uint4(ov[4 * u], ov[4 * u + 1], ov[4 * u + 2], ov[4 * u + 3]);
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        ptx::tma_store_3d(&tm_o, buf, half * HD + OE * t, q0 + wq * 32, slice);
+                        ptx::bulk_commit_group();
                     }
                 }
+                // Shared memory must outlive the stores that read it.
+                if (lane == 0) ptx::bulk_wait_group<0>();
+                __syncwarp();
             }
         }
     }

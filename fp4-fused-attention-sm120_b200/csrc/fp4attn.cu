@@ -281,8 +281,18 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     static std::atomic<unsigned long long> smem_set{0};
     if (int rc = set_smem_once(kern, C::SMEM_BYTES, smem_set)) return rc;
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
+    // Attention output is written by TMA stores in 32-row x OCH_E-column boxes
+    // (the scores path stores from registers and ignores this map).
+    CUtensorMap to = tq;
+    if constexpr (!kScores) {
+        constexpr bool f32 = sizeof(OutT) == 4;
+        const int rc = make_map_3d(&to, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                   static_cast<int>(sizeof(OutT)), a.out, D, a.seq_q, slices, C::OCH_E, 32,
+                                   swizzle_for(C::OCH_E * static_cast<int>(sizeof(OutT))));
+        if (rc) return rc;
+    }
     dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }
