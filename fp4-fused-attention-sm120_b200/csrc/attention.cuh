@@ -64,14 +64,14 @@ struct FwdCfg {
     static constexpr int SFA_ATOMS = (DP + 127) / 128;      // 512-B scale atoms per 128-row tile
     static constexpr int SFB_ATOMS = BN == 128 ? SFA_ATOMS : (DP + 255) / 256;
     static constexpr int SFB_COLS = 4 * SFB_ATOMS;
-    static constexpr int KST = 3;
+    static constexpr int KST = D > 128 && BN == 128 ? 2 : 3;  // (TMEM: K scale columns per stage)
     static constexpr int VST = D > 128 && BN == 128 ? 2 : 3;
     // TMEM
     static constexpr int S_COL = 0;
     static constexpr int O_COL = 2 * BN;
     static constexpr int P_COL = O_COL + D;                 // BN/2 columns of FP16 pairs
     static constexpr int SFA_COL = P_COL + BN / 2;
-    static constexpr int SFB_COL = SFA_COL + 4 * SFA_ATOMS;
+    static constexpr int SFB_COL = SFA_COL + 2 * 4 * SFA_ATOMS;  // Q scales: two buffers (alternate items)
     static constexpr int TMEM_USED = SFB_COL + KST * SFB_COLS;
     static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
     static_assert(D % 32 == 0 && D <= 256, "head_dim");
@@ -83,9 +83,12 @@ struct FwdCfg {
     static constexpr int KSF_BYTES = SFB_ATOMS * 512;
     static constexpr int V_BYTES = VCH * BN * VCW;
     static constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+    // Q and its scale tile are double-buffered (alternate work items), so the
+    // next item's Q can land while the current item's S MMAs still read theirs.
+    static constexpr int Q_STRIDE = align1k(Q_BYTES);
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_QSF = align1k(OFF_Q + Q_BYTES);
-    static constexpr int OFF_K = align1k(OFF_QSF + QSF_BYTES);
+    static constexpr int OFF_QSF = OFF_Q + 2 * Q_STRIDE;
+    static constexpr int OFF_K = align1k(OFF_QSF + 2 * QSF_BYTES);
     static constexpr int K_STRIDE = align1k(K_BYTES);
     static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
     static constexpr int OFF_V = align1k(OFF_KSF + KST * KSF_BYTES);
@@ -97,8 +100,8 @@ struct FwdCfg {
     static constexpr int OST_BYTES = 32 * OCH_E * 4;
     static constexpr int OFF_OST = OFF_REDL + 2 * 128 * 4;
     static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
-    // q_full, K ring, V ring, s_full[2], p_full[2], pv_done, drain
-    static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1;
+    // q_full[2], q_empty[2], K ring, V ring, s_full[2], p_full[2], pv_done, drain, l_ready[4]
+    static constexpr int NUM_BARS = 4 + 2 * KST + 2 * VST + 2 + 2 + 1 + 1 + 4;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -106,6 +109,7 @@ struct FwdCfg {
 struct FwdArgs {
     int seq_q, seq_k;
     int nq_tiles, nk_tiles;
+    int n_items;               // work items = nq_tiles * slices (one 128-row query tile each)
     int q_sf_tiles;            // 128-row scale tiles per slice in q_sf (>= nq_tiles)
     float scale_log2;          // softmax_scale * log2(e)
     void* out;                 // [slices, seq_q, D] (attention) or [slices, seq_q, seq_k] FP32 (scores)
@@ -115,6 +119,39 @@ struct FwdArgs {
     int causal;                // 1: query i sees keys j <= i + causal_off only (attention, not scores)
     int causal_off;            // seq_k - seq_q (bottom-right alignment)
 };
+
+// Work item r of this CTA's static schedule for the one-tile kernel: (slice,
+// query tile) and its number of key steps.  Without a mask items go in slice
+// order (a slice's K/V stay in L2 while its tiles run); with the causal mask a
+// tile needs keys only up to its last row, so items go heaviest first (last
+// tiles first) and are dealt to the CTAs in a snake order.
+struct TileItem {
+    int slice, qt, nk;
+    bool valid;
+};
+
+template <int BN>
+__device__ __forceinline__ TileItem tile_item(const FwdArgs& a, bool causal, int r)
+{
+    const int G = gridDim.x, b = blockIdx.x;
+    TileItem it;
+    if (causal) {
+        const int w = r * G + ((r & 1) ? G - 1 - b : b);
+        const int slices = a.n_items / a.nq_tiles;
+        it.valid = w < a.n_items;
+        it.slice = w % slices;
+        it.qt = a.nq_tiles - 1 - w / slices;
+        const int hi = min(it.qt * 128 + 127, a.seq_q - 1) + a.causal_off;  // last key any row sees
+        it.nk = hi < 0 ? 1 : min(a.nk_tiles, hi / BN + 1);
+    } else {
+        const int w = r * G + b;
+        it.valid = w < a.n_items;
+        it.slice = w / a.nq_tiles;
+        it.qt = w % a.nq_tiles;
+        it.nk = a.nk_tiles;
+    }
+    return it;
+}
 
 enum WaitSite : int {
     kSiteQFull = 1,
@@ -207,8 +244,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint8_t* sKsf = smem + C::OFF_KSF;
     uint8_t* sV = smem + C::OFF_V;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-    uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
+    uint64_t* q_full = bars;              // [2] Q buffer b loaded (TMA)
+    uint64_t* q_empty = bars + 2;         // [2] the S MMAs of Q buffer b's item are done (tcgen05.commit)
+    uint64_t* k_full = bars + 4;
     uint64_t* k_empty = k_full + C::KST;
     uint64_t* v_full = k_empty + C::KST;
     uint64_t* v_empty = v_full + C::VST;
@@ -216,26 +254,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint64_t* p_full = s_full + 2;        // step j done: S_j read, P_j stored, O rescaled (256 threads)
     uint64_t* pv_done = p_full + 2;       // O += P_j V_j complete (tcgen05.commit)
     uint64_t* drain_bar = pv_done + 1;
+    uint64_t* l_ready = drain_bar + 1;    // [lane quarter] both halves' row sums are in red_l (64 threads)
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    // With the causal mask a tile needs keys only up to its last row: the
-    // heaviest tiles (last rows) are launched first, and the key loop stops
-    // at the tile's last visible key.
+    // Persistent: this CTA runs items tile_item(args, causal, r) for r = 0, 1,
+    // ...; barrier phases and ring indices run on across items (global step g).
     const bool causal = !kScores && args.causal;
-    const int qt = causal ? args.nq_tiles - 1 - static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
-    const int slice = blockIdx.y;
-    const int q0 = qt * C::BM;
-    int nk = args.nk_tiles;
-    if (causal) {
-        const int hi = min(q0 + C::BM - 1, args.seq_q - 1) + args.causal_off;
-        nk = hi < 0 ? 1 : min(nk, hi / BN + 1);
-    }
+    const int rounds = (args.n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
 
     if (threadIdx.x == 0) {
-        ptx::mbar_init(q_full, 1);
+        for (int b = 0; b < 2; b++) {
+            ptx::mbar_init(&q_full[b], 1);
+            ptx::mbar_init(&q_empty[b], 1);
+        }
         for (int i = 0; i < C::KST; i++) {
             ptx::mbar_init(&k_full[i], 1);
             ptx::mbar_init(&k_empty[i], 1);
@@ -250,6 +284,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         ptx::mbar_init(pv_done, 1);
         ptx::mbar_init(drain_bar, 2);  // one commit from each MMA issuer
+        for (int q = 0; q < 4; q++) ptx::mbar_init(&l_ready[q], 64);
         abort_sh = 0;
         ptx::fence_mbar_init();
     }
@@ -276,40 +311,57 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (warp == 0) {
             // -------------------------------------------------------- producer
             if (lane == 0) {
-                ptx::mbar_arrive_expect_tx(q_full, C::Q_BYTES + C::QSF_BYTES);
-#pragma unroll
-                for (int c = 0; c < C::NCH; c++)
-                    ptx::tma_load_3d(sQ + c * C::BM * C::CW, &tm_q, q_full, c * C::CW, q0, slice);
-                ptx::bulk_load(sQsf, args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + qt) * C::QSF_BYTES,
-                               C::QSF_BYTES, q_full);
-                int k_issued = 0, v_issued = 0;
-                for (int j = 0; j < nk; j++) {
-                    const int ks = j % C::KST;
-                    if (j >= C::KST && !wait_phase(&k_empty[ks], ((j / C::KST) - 1) & 1, wctx, kSiteKEmpty)) break;
-                    ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::KSF_BYTES);
+                int it = 0, kv = 0, k_issued = 0, v_issued = 0;
+                bool ok = true;
+                for (int r = 0; ok && r < rounds; r++) {
+                    const TileItem item = tile_item<BN>(args, causal, r);
+                    if (!item.valid) continue;
+                    const int qb = it & 1;
+                    // Q buffer qb last held item it-2; its S MMAs must be done.
+                    if (it >= 2 && !wait_phase(&q_empty[qb], ((it >> 1) - 1) & 1, wctx, kSiteQEmpty)) break;
+                    ptx::mbar_arrive_expect_tx(&q_full[qb], C::Q_BYTES + C::QSF_BYTES);
 #pragma unroll
                     for (int c = 0; c < C::NCH; c++)
-                        ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW,
-                                         j * BN, slice);
-                    ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
-                                   args.k_sf + (static_cast<size_t>(slice) * args.nk_tiles + j) * C::KSF_BYTES, C::KSF_BYTES,
-                                   &k_full[ks]);
-                    k_issued = j + 1;
-                    if (!kScores) {
-                        const int vs = j % C::VST;
-                        if (j >= C::VST && !wait_phase(&v_empty[vs], ((j / C::VST) - 1) & 1, wctx, kSiteVEmpty))
+                        ptx::tma_load_3d(sQ + qb * C::Q_STRIDE + c * C::BM * C::CW, &tm_q, &q_full[qb], c * C::CW,
+                                         item.qt * C::BM, item.slice);
+                    ptx::bulk_load(sQsf + qb * C::QSF_BYTES,
+                                   args.q_sf + (static_cast<size_t>(item.slice) * args.q_sf_tiles + item.qt) * C::QSF_BYTES,
+                                   C::QSF_BYTES, &q_full[qb]);
+                    it++;
+                    for (int j = 0; j < item.nk; j++, kv++) {
+                        const int ks = kv % C::KST;
+                        if (kv >= C::KST && !wait_phase(&k_empty[ks], ((kv / C::KST) - 1) & 1, wctx, kSiteKEmpty)) {
+                            ok = false;
                             break;
-                        ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+                        }
+                        ptx::mbar_arrive_expect_tx(&k_full[ks], C::K_BYTES + C::KSF_BYTES);
 #pragma unroll
-                        for (int c = 0; c < C::VCH; c++)
-                            ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
-                                             c * (C::VCW / 2), j * BN, slice);
-                        v_issued = j + 1;
+                        for (int c = 0; c < C::NCH; c++)
+                            ptx::tma_load_3d(sK + ks * C::K_STRIDE + c * BN * C::CW, &tm_k, &k_full[ks], c * C::CW,
+                                             j * BN, item.slice);
+                        ptx::bulk_load(sKsf + ks * C::KSF_BYTES,
+                                       args.k_sf + (static_cast<size_t>(item.slice) * args.nk_tiles + j) * C::KSF_BYTES,
+                                       C::KSF_BYTES, &k_full[ks]);
+                        k_issued = kv + 1;
+                        if (!kScores) {
+                            const int vs = kv % C::VST;
+                            if (kv >= C::VST && !wait_phase(&v_empty[vs], ((kv / C::VST) - 1) & 1, wctx, kSiteVEmpty)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::mbar_arrive_expect_tx(&v_full[vs], C::V_BYTES);
+#pragma unroll
+                            for (int c = 0; c < C::VCH; c++)
+                                ptx::tma_load_3d(sV + vs * C::V_STRIDE + c * BN * C::VCW, &tm_v, &v_full[vs],
+                                                 c * (C::VCW / 2), j * BN, item.slice);
+                            v_issued = kv + 1;
+                        }
                     }
                 }
-                // Every load this thread issued must land before the CTA exits.
+                // Every load this thread issued must land before the CTA exits
+                // (each ring's loads are at most its depth ahead of their use).
                 const unsigned long long drain_ns = 2ull * args.timeout_ns;
-                drain_phase(q_full, 0, drain_ns);
+                for (int i = it - 2 < 0 ? 0 : it - 2; i < it; i++) drain_phase(&q_full[i & 1], (i >> 1) & 1, drain_ns);
                 for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
                     drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
                 for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
@@ -325,48 +377,67 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const uint64_t qdesc0 = ptx::make_sdesc(ptx::smem_u32(sQ), 16, 8 * C::CW, qk_layout);
                 const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::CW, qk_layout);
                 const uint64_t sfdesc0 = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
-                bool ok = wait_phase(q_full, 0, wctx, kSiteQFull);
-                if (ok) {
-                    ptx::tc_fence_after();
+                const uint64_t qsfdesc0 = ptx::make_sdesc(ptx::smem_u32(sQsf), 0, 128, ptx::kSwizzleNone);
+                // Global step g (S buffer g & 1, K ring index g); item counter it (Q buffer it & 1).
+                int g = 0, it = 0;
+                bool ok = true;
+                for (int r = 0; ok && r < rounds; r++) {
+                    const TileItem item = tile_item<BN>(args, causal, r);
+                    if (!item.valid) continue;
+                    const int qb = it & 1;
+                    const uint32_t sfa = tmem + C::SFA_COL + qb * 4 * C::SFA_ATOMS;
+                    for (int j = 0; j < item.nk; j++, g++) {
+                        // S_g reuses S_{g-2}'s buffer once the softmax is done with
+                        // step g-2; it is needed only a whole step later.
+                        if (g >= 2) {
+                            if (!wait_phase(&p_full[g & 1], ((g >> 1) - 1) & 1, wctx, kSitePFull)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                        }
+                        if (j == 0) {
+                            // This item's Q and its scales (the item that last used
+                            // buffer qb finished its S MMAs before Q was loaded).
+                            if (!wait_phase(&q_full[qb], (it >> 1) & 1, wctx, kSiteQFull)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
 #pragma unroll
-                    for (int at = 0; at < C::SFA_ATOMS; at++)
-                        ptx::tc_cp_32x128b_warpx4(
-                            tmem + C::SFA_COL + 4 * at,
-                            ptx::make_sdesc(ptx::smem_u32(sQsf + 512 * at), 0, 128, ptx::kSwizzleNone));
-                }
-                auto issue_s = [&](int j) -> bool {
-                    const int ks = j % C::KST;
-                    if (!wait_phase(&k_full[ks], (j / C::KST) & 1, wctx, kSiteKFull)) return false;
-                    ptx::tc_fence_after();
-                    const uint32_t sfb_base = tmem + C::SFB_COL + ks * C::SFB_COLS;
+                            for (int at = 0; at < C::SFA_ATOMS; at++)
+                                ptx::tc_cp_32x128b_warpx4(
+                                    sfa + 4 * at, qsfdesc0 + static_cast<uint64_t>((qb * C::QSF_BYTES + 512 * at) >> 4));
+                        }
+                        const int ks = g % C::KST;
+                        if (!wait_phase(&k_full[ks], (g / C::KST) & 1, wctx, kSiteKFull)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        const uint32_t sfb_base = tmem + C::SFB_COL + ks * C::SFB_COLS;
 #pragma unroll
-                    for (int at = 0; at < C::SFB_ATOMS; at++)
-                        ptx::tc_cp_32x128b_warpx4(sfb_base + 4 * at,
-                                                  sfdesc0 + static_cast<uint64_t>((ks * C::KSF_BYTES + 512 * at) >> 4));
-                    const uint32_t s_tmem = tmem + C::S_COL + (j & 1) * BN;
-                    const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
+                        for (int at = 0; at < C::SFB_ATOMS; at++)
+                            ptx::tc_cp_32x128b_warpx4(sfb_base + 4 * at,
+                                                      sfdesc0 + static_cast<uint64_t>((ks * C::KSF_BYTES + 512 * at) >> 4));
+                        const uint32_t s_tmem = tmem + C::S_COL + (g & 1) * BN;
+                        const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
+                        const uint64_t qdesc = qdesc0 + static_cast<uint64_t>((qb * C::Q_STRIDE) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < C::KSTEPS; kk++) {
-                        const int off = kk * 32, ch = off / C::CW, in = off % C::CW;
-                        const uint32_t sf_id = 2u * (kk & 1);
-                        ptx::mma_mxf4(s_tmem, qdesc0 + static_cast<uint64_t>((ch * C::BM * C::CW + in) >> 4),
-                                      kdesc + static_cast<uint64_t>((ch * BN * C::CW + in) >> 4),
-                                      ptx::idesc_mxf4(128, BN, sf_id, sf_id),
-                                      (tmem + C::SFA_COL + 4 * (kk >> 1)) | (sf_id << 30),
-                                      (sfb_base + (BN == 128 ? 4 : 2) * (kk >> 1)) | (sf_id << 30), kk > 0 ? 1u : 0u);
+                        for (int kk = 0; kk < C::KSTEPS; kk++) {
+                            const int off = kk * 32, ch = off / C::CW, in = off % C::CW;
+                            const uint32_t sf_id = 2u * (kk & 1);
+                            ptx::mma_mxf4(s_tmem, qdesc + static_cast<uint64_t>((ch * C::BM * C::CW + in) >> 4),
+                                          kdesc + static_cast<uint64_t>((ch * BN * C::CW + in) >> 4),
+                                          ptx::idesc_mxf4(128, BN, sf_id, sf_id), (sfa + 4 * (kk >> 1)) | (sf_id << 30),
+                                          (sfb_base + (BN == 128 ? 4 : 2) * (kk >> 1)) | (sf_id << 30), kk > 0 ? 1u : 0u);
+                        }
+                        ptx::tc_commit(&s_full[g & 1]);
+                        ptx::tc_commit(&k_empty[ks]);
                     }
-                    ptx::tc_commit(&s_full[j & 1]);
-                    ptx::tc_commit(&k_empty[ks]);
-                    return true;
-                };
-                if (ok) ok = issue_s(0);
-                if (ok && nk > 1) ok = issue_s(1);
-                // S_{j+2} reuses S_j's buffer once the softmax is done with step j
-                // (p_full[j]); it is needed only a whole step later.
-                for (int j = 0; ok && j + 2 < nk; j++) {
-                    if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
-                    ptx::tc_fence_after();
-                    if (!issue_s(j + 2)) break;
+                    if (!ok) break;
+                    ptx::tc_commit(&q_empty[qb]);  // the producer may load Q buffer qb again
+                    it++;
                 }
                 // Drain every tcgen05 op this thread issued before TMEM is freed.
                 ptx::tc_commit(drain_bar);
@@ -382,19 +453,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     constexpr uint32_t v_layout = ptx::swizzle_mode_for_bytes(C::VCW);
                     const uint64_t vdesc0 = ptx::make_sdesc(ptx::smem_u32(sV), BN * C::VCW, 8 * C::VCW, v_layout);
                     constexpr uint32_t idesc_pv = ptx::idesc_f16(128, D, true);
-                    for (int j = 0; j < nk; j++) {
-                        if (!wait_phase(&p_full[j & 1], (j >> 1) & 1, wctx, kSitePFull)) break;
-                        const int vs = j % C::VST;
-                        if (!wait_phase(&v_full[vs], (j / C::VST) & 1, wctx, kSiteVFull)) break;
-                        ptx::tc_fence_after();
-                        const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
+                    int g = 0;  // global step: p_full phase and V ring index
+                    bool ok = true;
+                    for (int r = 0; ok && r < rounds; r++) {
+                        const TileItem item = tile_item<BN>(args, causal, r);
+                        if (!item.valid) continue;
+                        for (int j = 0; j < item.nk; j++, g++) {
+                            if (!wait_phase(&p_full[g & 1], (g >> 1) & 1, wctx, kSitePFull)) {
+                                ok = false;
+                                break;
+                            }
+                            const int vs = g % C::VST;
+                            if (!wait_phase(&v_full[vs], (g / C::VST) & 1, wctx, kSiteVFull)) {
+                                ok = false;
+                                break;
+                            }
+                            ptx::tc_fence_after();
+                            const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
+                            // The first step of an item starts O afresh.
 #pragma unroll
-                        for (int kk = 0; kk < BN / 16; kk++)
-                            ptx::mma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
-                                            vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
-                                            (j > 0 || kk > 0) ? 1u : 0u);
-                        ptx::tc_commit(&v_empty[vs]);
-                        ptx::tc_commit(pv_done);
+                            for (int kk = 0; kk < BN / 16; kk++)
+                                ptx::mma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
+                                                vdesc + static_cast<uint64_t>((kk * 16 * C::VCW) >> 4), idesc_pv,
+                                                (j > 0 || kk > 0) ? 1u : 0u);
+                            ptx::tc_commit(&v_empty[vs]);
+                            ptx::tc_commit(pv_done);
+                        }
                     }
                 }
                 ptx::tc_commit(drain_bar);
@@ -415,22 +499,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
         float* red_l = reinterpret_cast<float*>(smem + C::OFF_REDL);
         const float c = args.scale_log2;
-        float m = -INFINITY, l = 0.f;
         bool ok = true;
-        auto load_s = [&](int j, uint32_t (&buf)[NT][32]) {
-            const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN + half * HC;
+        auto load_s = [&](int g, uint32_t (&buf)[NT][32]) {
+            const uint32_t s_tm = tmem + lane_off + C::S_COL + (g & 1) * BN + half * HC;
 #pragma unroll
             for (int t = 0; t < NT; t++) ptx::tmem_ld32(s_tm + 32 * t, buf[t]);
         };
+        int g0 = 0;  // global step of the current item's first step (S buffer and barrier phases)
+        int items_done = 0;  // phase of l_ready
+        for (int r = 0; ok && r < rounds; r++) {
+        const TileItem item = tile_item<BN>(args, causal, r);
+        if (!item.valid) continue;
+        const int slice = item.slice, q0 = item.qt * C::BM, nk = item.nk;
+        float m = -INFINITY, l = 0.f;
         if (kScores) {
             for (int j = 0; j < nk; j++) {
-                if (!__all_sync(0xffffffffu, wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull))) {
+                const int g = g0 + j;
+                if (!__all_sync(0xffffffffu, wait_phase(&s_full[g & 1], (g >> 1) & 1, wctx, kSiteSFull))) {
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
                 uint32_t sr[NT][32];
-                load_s(j, sr);
+                load_s(g, sr);
                 ptx::tc_wait_ld();
                 const int valid = args.seq_k - j * BN - half * HC;
                 const int grow = q0 + row;
@@ -445,7 +536,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
                 }
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(&p_full[j & 1]);  // done with S_j: its buffer may be reused
+                ptx::mbar_arrive(&p_full[g & 1]);  // done with S_g: its buffer may be reused
             }
         } else {
             // Each warp loads the whole S_j row (all BN columns) to form the
@@ -456,14 +547,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             // Keys this row sees: [0, row_lim) (the causal mask, or all keys).
             const int row_lim = causal ? min(q0 + row + args.causal_off + 1, args.seq_k) : args.seq_k;
             for (int j = 0; j < nk; j++) {
-                if (!__all_sync(0xffffffffu, wait_phase(&s_full[j & 1], (j >> 1) & 1, wctx, kSiteSFull))) {
+                const int g = g0 + j;
+                if (!__all_sync(0xffffffffu, wait_phase(&s_full[g & 1], (g >> 1) & 1, wctx, kSiteSFull))) {
                     ok = false;
                     break;
                 }
                 ptx::tc_fence_after();
                 uint32_t sr[NF][32];
                 {
-                    const uint32_t s_tm = tmem + lane_off + C::S_COL + (j & 1) * BN;
+                    const uint32_t s_tm = tmem + lane_off + C::S_COL + (g & 1) * BN;
 #pragma unroll
                     for (int t = 0; t < NF; t++) ptx::tmem_ld32(s_tm + 32 * t, sr[t]);
                 }
@@ -526,7 +618,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     // PV_{j-1} must be done: it reads the P columns this step
                     // overwrites, and O is rescaled below (waiting every phase
                     // also keeps this barrier's parity unambiguous).
-                    if (!__all_sync(0xffffffffu, wait_phase(pv_done, (j - 1) & 1, wctx, kSitePvDone))) {
+                    if (!__all_sync(0xffffffffu, wait_phase(pv_done, (g - 1) & 1, wctx, kSitePvDone))) {
                         ok = false;
                         break;
                     }
@@ -558,15 +650,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 }
                 ptx::tc_wait_st();
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(&p_full[j & 1]);
+                ptx::mbar_arrive(&p_full[g & 1]);
             }
         }
         if (!kScores && ok) {
+            // Exchange the half-row sums through shared memory; the wait is
+            // bounded, so a partner that left early cannot hold this warp.
             red_l[half * 128 + row] = l;
-            ptx::named_bar_sync(1 + wq, 64);
+            ptx::mbar_arrive(&l_ready[wq]);
+            if (!__all_sync(0xffffffffu, wait_phase(&l_ready[wq], items_done & 1, wctx, kSiteSFull))) {
+                ok = false;
+                break;
+            }
+            items_done++;
             const float l_tot = l + red_l[(1 - half) * 128 + row];
             // Waits are decided per warp (__all_sync) so that warp-wide steps stay uniform.
-            if (__all_sync(0xffffffffu, wait_phase(pv_done, (nk - 1) & 1, wctx, kSitePvDone))) {
+            if (__all_sync(0xffffffffu, wait_phase(pv_done, (g0 + nk - 1) & 1, wctx, kSitePvDone))) {
                 ptx::tc_fence_after();
                 const float inv_l = l_tot > 0.f ? 1.0f / l_tot : 0.f;  // a row that saw no key outputs 0
                 // O / l in OCH_E-column chunks: each warp writes its 32 rows
@@ -576,6 +675,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 constexpr int OE = C::OCH_E;
                 constexpr int OB = OE * static_cast<int>(sizeof(OutT));  // bytes per staged row (32, 64, 128)
                 uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
+                // The previous item's stores must be done reading the staging buffers.
+                if (lane == 0) ptx::bulk_wait_group_read<0>();
+                __syncwarp();
 #pragma unroll 1
                 for (int t = 0; t < HD / OE; t++) {
                     uint32_t o[OE];
@@ -615,11 +717,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::bulk_commit_group();
                     }
                 }
-                // Shared memory must outlive the stores that read it.
-                if (lane == 0) ptx::bulk_wait_group<0>();
-                __syncwarp();
+            } else {
+                ok = false;
             }
         }
+        g0 += nk;
+        }
+        // Shared memory must outlive the stores that read it.
+        if (lane == 0) ptx::bulk_wait_group<0>();
+        __syncwarp();
     }
 
     ptx::tc_fence_before();

@@ -291,8 +291,13 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
                                    swizzle_for(C::OCH_E * static_cast<int>(sizeof(OutT))));
         if (rc) return rc;
     }
-    dim3 grid(a.nq_tiles, static_cast<unsigned>(slices));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
+    // Persistent: one CTA per SM walks the (slice, query tile) items.
+    const int64_t items = static_cast<int64_t>(a.nq_tiles) * slices;
+    if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
+    fp4attn::FwdArgs pa = a;
+    pa.n_items = static_cast<int>(items);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, pa);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }
