@@ -303,3 +303,34 @@ def test_causal_full_prefill_sampled_rows(fa, cuda):
             want = oracle.attention_causal(qd, kd, vs, first_row=r, seq_q_total=4096)
             got = out[0, s, r:r + 1].float().cpu().numpy()
             assert_close(got, want)
+
+
+# ---- several work items per persistent CTA ---------------------------------
+# Both kernels run one CTA per SM over (slice, query tile[s]) items; with more
+# items than SMs each CTA carries its barrier phases, rings and Q buffers from
+# one item to the next.  These cases have 300-600 items.
+
+@pytest.mark.parametrize("d", [160, 256])
+@pytest.mark.parametrize("causal", [False, True])
+def test_one_tile_kernel_many_items(fa, cuda, d, causal):
+    g = torch.Generator().manual_seed(d + causal)
+    H, sq, sk = 300, 256 if causal else 128, 200
+    Q, K, V = (torch.randn(1, H, sq, d, generator=g).half(), torch.randn(1, H, sk, d, generator=g).half(),
+               torch.randn(1, H, sk, d, generator=g).half())
+    out = fa.fused_fp4_attention(Q.cuda(), K.cuda(), V.cuda(), out_dtype=torch.float32, causal=causal)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention(Q[0].float().numpy(), K[0].float().numpy(), V[0].float().numpy(), causal=causal)
+    assert_close(out[0].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("d", [64, 256])
+def test_scores_bit_exact_many_items(fa, cuda, d):
+    g = torch.Generator().manual_seed(d + 5)
+    Q = torch.randn(1, 200, 130, d, generator=g).half()
+    K = torch.randn(1, 200, 70, d, generator=g).half()
+    S = fa.debug_scores(Q.cuda(), K.cuda())
+    assert fa.status_query() == fa.OK
+    S = S.cpu().numpy()
+    for h in (0, 77, 199):
+        want = oracle.fp4_scores(Q[0, h].float().numpy(), K[0, h].float().numpy())
+        assert np.array_equal(S[0, h], want)
