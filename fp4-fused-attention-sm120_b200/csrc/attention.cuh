@@ -1,33 +1,41 @@
-// attention.cuh -- warp-specialised FP4 fused attention forward for sm_100a.
+// attention.cuh -- warp-specialised FP4 fused attention forward for sm_100a,
+// one 128-row query tile per work item (head_dim 160 and 256, and the S-only
+// debug path for every head_dim; attention_pair.cuh covers head_dim <= 128).
 //
 // Computes, per (batch, head) slice and 128-row query tile,
 //     Out = softmax(Q K^T * scale) V
 // with Q, K pre-quantised to E2M1 + UE8M0 (block 32 along head_dim) and V in
 // FP16 -- the computation of the reference kernel fused_fp4_attention
-// (common.h:68-328), re-designed for Blackwell:
+// (common.h:68-328), re-designed for Blackwell.  The kernel is persistent: one
+// CTA per SM walks (slice, query tile) items, and barrier phases and rings run
+// on across items.  Roles:
 //
-//   warp 0      TMA producer: Q tile once, then K tiles (codes + scale tiles)
-//               and V tiles through KST/VST-stage mbarrier rings.
-//   warp 1      S issuer (one thread): S_j = Q K_j^T with tcgen05.mma
+//   warp 0      TMA producer: per item the Q tile (double-buffered across
+//               items), then K tiles (codes + scale tiles) and V tiles through
+//               KST/VST-stage mbarrier rings.
+//   warp 1      S issuer (one thread): S_g = Q K_g^T with tcgen05.mma
 //               kind::mxf4 block_scale (scales in TMEM, copied with
-//               tcgen05.cp).  S is double-buffered: S_{j+2} is issued when the
-//               softmax has finished step j, a whole step before it is needed.
-//   warp 2      P.V issuer (one thread): O += P_j V_j with tcgen05.mma
+//               tcgen05.cp).  S is double-buffered: S_{g+2} is issued when the
+//               softmax has finished step g, a whole step before it is needed
+//               (possibly the next item's first steps, hence the Q buffers).
+//   warp 2      P.V issuer (one thread): O += P_g V_g with tcgen05.mma
 //               kind::f16 whose A operand (P) is read from its own TMEM
-//               columns; on its own warp so it is issued as soon as P_j is
-//               ready (tcgen05 issue shares each sub-partition's queue with the
-//               softmax's MUFU traffic, so one thread issuing both is slow).
+//               columns; on its own warp so it is issued as soon as P_g is
+//               ready.
 //   warp 3      idle (completes the control warpgroup for setmaxnreg)
 //   warps 4-11  two softmax warpgroups; thread = query row = TMEM lane, and
-//               each warpgroup owns half of the S_j columns (and half of O's).
-//               Each warp loads the whole S_j row and forms the row max itself
+//               each warpgroup owns half of the S columns (and half of O's).
+//               Each warp loads the whole S row and forms the row max itself
 //               (its partner computes the same value), so the two halves never
-//               wait on each other.  Online max/sum in FP32 (log2 domain), P_j stored as FP16
-//               with tcgen05.st, lazy O rescale (only when the row max grows
-//               by more than 2^15), final O / l for its half of the columns.
+//               wait on each other during a step.  Online max/sum in FP32
+//               (log2 domain), P stored as FP16 with tcgen05.st, lazy O
+//               rescale (only when the row max grows by more than 2^15); at
+//               the end of an item the halves exchange their row sums and
+//               write O / l for their half of the columns.
 //
 // TMEM columns (512 allocated): S0 [0,BN), S1 [BN,2BN), O [2BN, 2BN+D),
-// P [.., +BN/2), then the Q scale columns and KST stages of K scale columns.
+// P [.., +BN/2), then two groups of Q scale columns and KST stages of K scale
+// columns.
 //
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // FP4ATTN_ETIMEOUT in the device error word, all roles leave their loops,

@@ -6,8 +6,8 @@
 // E2M1 + UE8M0 and V, P in FP16 -- with a different division of the work.
 // A work item is 256 query rows of one (batch, head) slice, as two
 // independent 128-row tiles T0, T1, whose keys are walked in 64-row tiles.
-// The kernel is persistent: one CTA per SM takes items blockIdx.x,
-// blockIdx.x + gridDim.x, ... (consecutive items share a slice's K/V in L2),
+// The kernel is persistent: one CTA per SM takes items in rounds of gridDim.x
+// (pair_item: without a mask consecutive items share a slice's K/V in L2),
 // and every barrier phase and ring index runs on across items, so the next
 // item's Q, K, V and first S are fetched and computed while the current
 // item's last step and epilogue run.  Roles:
