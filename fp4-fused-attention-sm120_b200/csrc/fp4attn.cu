@@ -238,20 +238,23 @@ fp4attn::QuantTileArgs quant_args(int64_t slices, int seq, int d, int tile_rows,
     return a;
 }
 
-// Q and K quantised by one launch (grid z = 0 for Q, 1 for K).
+// Q and K quantised by one launch (grid z = 0 for Q, 1 for K), and with a V
+// job (FP32 input) V converted to FP16 by the same launch (z = 2).
 template <typename InT>
-int launch_quant_qk(const fp4attn::QuantJob& q, const fp4attn::QuantJob& k, int64_t slices, cudaStream_t st)
+int launch_quant_qk(const fp4attn::QuantJob& q, const fp4attn::QuantJob& k, const fp4attn::VConvJob* v,
+                    int64_t slices, cudaStream_t st)
 {
     auto gx_for = [&](const fp4attn::QuantTileArgs& a) {
         const int per_slice = a.ntiles * a.tile_rows * (a.padded_dim / 32);
         return static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
     };
-    dim3 grid(std::max(gx_for(q.a), gx_for(k.a)), static_cast<unsigned>(slices), 2);
+    const fp4attn::VConvJob vj = v ? *v : fp4attn::VConvJob{nullptr, nullptr, 0};
+    dim3 grid(std::max(gx_for(q.a), gx_for(k.a)), static_cast<unsigned>(slices), v ? 3 : 2);
     switch (q.a.padded_dim / 32) {
-        case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(q, k); break;
-        case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(q, k); break;
-        case 6: fp4attn::quantize_tiles_kernel<InT, 6><<<grid, 256, 0, st>>>(q, k); break;
-        case 8: fp4attn::quantize_tiles_kernel<InT, 8><<<grid, 256, 0, st>>>(q, k); break;
+        case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(q, k, vj); break;
+        case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(q, k, vj); break;
+        case 6: fp4attn::quantize_tiles_kernel<InT, 6><<<grid, 256, 0, st>>>(q, k, vj); break;
+        case 8: fp4attn::quantize_tiles_kernel<InT, 8><<<grid, 256, 0, st>>>(q, k, vj); break;
         default: return fail(FP4ATTN_EUNSUPPORTED, "padded head_dim %d", q.a.padded_dim);
     }
     FP4_CUDA(cudaGetLastError());
@@ -485,15 +488,11 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     const fp4attn::QuantJob jq{Q, ws + p.w.q_codes, ws + p.w.q_sf, quant_args(p.slices, sq, d, 128, nq_sf, ocp)};
     const fp4attn::QuantJob jk{K, ws + p.w.k_codes, ws + p.w.k_sf, quant_args(p.slices, sk, d, bn, nk_sf, ocp)};
     if (in_dtype == FP4ATTN_F16) {
-        if ((rc = launch_quant_qk<__half>(jq, jk, p.slices, st))) return rc;
+        if ((rc = launch_quant_qk<__half>(jq, jk, nullptr, p.slices, st))) return rc;
     } else {
-        if ((rc = launch_quant_qk<float>(jq, jk, p.slices, st))) return rc;
-        if (need_v) {
-            const int64_t n4 = p.slices * static_cast<int64_t>(sk) * d / 4;
-            fp4attn::f32_to_f16_kernel<<<grid_for(n4), 256, 0, st>>>(static_cast<const float4*>(V),
-                                                                     reinterpret_cast<uint2*>(ws + p.w.v16), n4);
-            FP4_CUDA(cudaGetLastError());
-        }
+        const fp4attn::VConvJob jv{static_cast<const float4*>(V), reinterpret_cast<uint2*>(ws + p.w.v16),
+                                   static_cast<int64_t>(sk) * d / 4};
+        if ((rc = launch_quant_qk<float>(jq, jk, need_v ? &jv : nullptr, p.slices, st))) return rc;
     }
     return FP4ATTN_OK;
 }

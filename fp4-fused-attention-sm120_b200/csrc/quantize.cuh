@@ -214,6 +214,14 @@ struct QuantJob {
     QuantTileArgs a;
 };
 
+// V in FP32, converted to the FP16 copy the attention kernel reads, per slice
+// (n4 float4 per slice).
+struct VConvJob {
+    const float4* src;
+    uint2* dst;
+    int64_t n4;
+};
+
 // Quantise Q (blockIdx.z == 0) and K (blockIdx.z == 1) in one launch into the
 // layout the attention kernel loads with TMA: codes [slices][seq][DP/2]
 // (blocks beyond D are zero) and scale tiles [slices][ntiles][sf_tile_bytes].
@@ -223,9 +231,22 @@ struct QuantJob {
 // finite 2^127 (255 would be NaN in E8M0).  Grid: x covers one slice's padded
 // rows (kNB blocks of 32 per row, one lane per block), y is the slice, so all
 // index arithmetic is 32-bit with a compile-time divisor.
+// With FP32 input the same launch also converts V (blockIdx.z == 2).
 template <typename InT, int kNB>
-__global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, const QuantJob jk)
+__global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, const QuantJob jk, const VConvJob jv)
 {
+    if (blockIdx.z == 2) {
+        // FP32 -> FP16 (round to nearest even) for this slice of V.
+        const float4* src = jv.src + static_cast<int64_t>(blockIdx.y) * jv.n4;
+        uint2* dst = jv.dst + static_cast<int64_t>(blockIdx.y) * jv.n4;
+        for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < jv.n4;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            const float4 f = src[i];
+            __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+            dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+        }
+        return;
+    }
     const bool is_k = blockIdx.z != 0;
     const QuantTileArgs a = is_k ? jk.a : jq.a;
     const InT* x = static_cast<const InT*>(is_k ? jk.x : jq.x);
@@ -268,18 +289,6 @@ __global__ void __launch_bounds__(256) quantize_rowmajor_kernel(const InT* __res
         const uint32_t sb = quantize32<InT>(x + blk * 32, ocp_mode, packed);
         *reinterpret_cast<uint4*>(codes + blk * 16) = packed;
         sf[blk] = static_cast<uint8_t>(sb);
-    }
-}
-
-// FP32 -> FP16 (round to nearest even) for V when the caller passes FP32.
-__global__ void __launch_bounds__(256) f32_to_f16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst,
-                                                         int64_t n4)
-{
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float4 f = src[i];
-        __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
-        dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
     }
 }
 
