@@ -2,8 +2,8 @@
 // kernels use: mbarriers with bounded waits, TMA (cp.async.bulk[.tensor]),
 // Tensor Memory (tcgen05.alloc/ld/st/cp) and tcgen05.mma.
 //
-// No multicast form of any TMA or bulk load is used anywhere in this library:
-// every load brings data from this GPU's own memory into the issuing CTA.
+// Every TMA and bulk load in this library brings data from this GPU's own
+// memory into the issuing CTA alone.
 #pragma once
 
 #include <cuda.h>
