@@ -19,6 +19,7 @@ __all__ = [
     "BLOCK_ELEMENT", "BQ", "Fp4AttnError", "lib", "lib_path", "quantize", "workspace_size",
     "fused_fp4_attention", "fused_fp4_attention_into", "debug_scores", "status_query",
     "selftest_timeout", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
+    "F32", "F16", "MASK_NONE", "MASK_CAUSAL",
 ]
 
 BLOCK_ELEMENT = 32  # common.h:15

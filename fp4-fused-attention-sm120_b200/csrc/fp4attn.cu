@@ -165,7 +165,9 @@ int device_ready()
         if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
             d.status = FP4ATTN_ECUDA;
             d.msg = "could not query the CUDA device";
-        } else if (prop.major != 10) {
+        } else if (prop.major != 10 || prop.minor != 0) {
+            // The library carries sm_100a code only; architecture-specific
+            // code runs on exactly that compute capability.
             d.status = FP4ATTN_EUNSUPPORTED;
             d.msg = "libfp4attn requires an sm_100 (B200-class) GPU; found sm_" + std::to_string(prop.major) +
                     std::to_string(prop.minor);
