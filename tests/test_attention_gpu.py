@@ -334,3 +334,39 @@ def test_scores_bit_exact_many_items(fa, cuda, d):
     for h in (0, 77, 199):
         want = oracle.fp4_scores(Q[0, h].float().numpy(), K[0, h].float().numpy())
         assert np.array_equal(S[0, h], want)
+
+
+# ---- CUDA graphs ----------------------------------------------------------
+# The API makes no allocation and no host synchronisation, so a forward pass
+# with a caller workspace can be captured once and replayed on new inputs
+# copied into the captured buffers.
+
+@pytest.mark.parametrize("d,causal", [(128, False), (128, True), (256, False)])
+def test_cuda_graph_replay(fa, cuda, d, causal):
+    B, H, sq, sk = 1, 8, 300, 700
+    Q, K, V = (torch.empty(B, H, s, d, dtype=torch.float16, device="cuda") for s in (sq, sk, sk))
+    out = torch.empty(B, H, sq, d, dtype=torch.float16, device="cuda")
+    ws = torch.empty(fa.workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+
+    def fill(seed):
+        g = torch.Generator().manual_seed(seed)
+        for t in (Q, K, V):
+            t.copy_(torch.randn(t.shape, generator=g).half())
+
+    fill(0)
+    fa.fused_fp4_attention_into(Q, K, V, out, ws, causal=causal)  # per-device set-up happens outside capture
+    assert fa.status_query() == fa.OK
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fa.fused_fp4_attention_into(Q, K, V, out, ws, causal=causal)
+    for seed in (1, 2):
+        fill(seed)
+        graph.replay()
+        assert fa.status_query() == fa.OK
+        want = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float16, causal=causal)
+        assert fa.status_query() == fa.OK
+        assert torch.equal(out, want)  # the same kernels on the same inputs
+        ref = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(),
+                                   V[0].float().cpu().numpy(), causal=causal)
+        assert_close(out[0].float().cpu().numpy(), ref)
+    del graph
