@@ -17,9 +17,10 @@
  * common.h:99-102); `stream` is a cudaStream_t (0 = legacy default stream).
  * Every call is asynchronous on `stream` and returns an fp4attn_status code;
  * a non-zero code means nothing was launched.  The library keeps no state
- * between calls except a per-device error word (fp4attn_status_query) and
- * cached function attributes.  Calls on different streams may run
- * concurrently; the caller owns all buffers.
+ * between calls except, per device, its first-use set-up (the scale-rule
+ * table, the SM count, cached function attributes), an error word
+ * (fp4attn_status_query) and the fp4attn_forward_noalloc scratch.  Calls on
+ * different streams may run concurrently; the caller owns all buffers.
  */
 #ifndef FP4ATTN_H
 #define FP4ATTN_H
