@@ -80,3 +80,45 @@ def test_two_rank_shards_match_the_whole_job():
         assert p.exitcode == 0
     ok, covered, tmax = q.get(timeout=10)
     assert ok and covered and tmax == float(world)
+
+
+def _failing_worker(rank, world, port, q, fail_rank):
+    """A bench-like rank: joins the group, then meets the others at a barrier
+    before its timed region.  `fail_rank` dies first (as a rank whose device
+    set-up failed would), so the others' barrier must end in an error within
+    the group's short timeout instead of waiting for good."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == fail_rank:
+        os._exit(3)  # no clean-up: the process just disappears
+    t0 = time.monotonic()
+    try:
+        dist.barrier()
+        q.put((rank, "barrier passed", time.monotonic() - t0))
+    except Exception as e:  # gloo reports the lost peer or the timeout
+        q.put((rank, type(e).__name__, time.monotonic() - t0))
+    q.close()
+    q.join_thread()  # the report reaches the pipe before the process goes
+    os._exit(0)
+
+
+def test_a_failed_rank_is_reported_not_waited_for():
+    world, fail_rank = 2, 1
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank was still waiting after 120 s"
+    assert procs[fail_rank].exitcode == 3
+    rank, outcome, waited = q.get(timeout=10)
+    assert rank == 0 and outcome != "barrier passed"
+    assert waited < 60
