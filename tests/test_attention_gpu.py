@@ -370,3 +370,38 @@ def test_cuda_graph_replay(fa, cuda, d, causal):
                                    V[0].float().cpu().numpy(), causal=causal)
         assert_close(out[0].float().cpu().numpy(), ref)
     del graph
+
+
+# ---- guard bytes --------------------------------------------------------------
+# No sanitizer runs here, so writes are checked directly.  The output and the
+# workspace sit inside larger buffers filled with a sentinel byte, and after a
+# forward pass the bytes on both sides (and the inputs) must be unchanged.
+# Ragged seq_q leaves a partial query tile and, for head_dim <= 128, a padding
+# tile of the last pair; their rows must not be stored.
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("sq,causal", [(1, False), (130, False), (300, True)])
+def test_no_writes_outside_the_output_and_workspace(fa, cuda, d, out_dtype, sq, causal):
+    B, H, sk, guard = 1, 3, 200, 4096
+    g = torch.Generator().manual_seed(d + sq)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk, sk))
+    inputs_before = [t.clone() for t in (Q, K, V)]
+    out_bytes = B * H * sq * d * torch.empty((), dtype=out_dtype).element_size()
+    raw_out = torch.full((out_bytes + 2 * guard,), 0xA5, dtype=torch.uint8, device="cuda")
+    out = raw_out[guard:guard + out_bytes].view(out_dtype).view(B, H, sq, d)
+    ws_bytes = fa.workspace_size(B, H, sq, sk, d)
+    raw_ws = torch.full((ws_bytes + 2 * guard,), 0x5A, dtype=torch.uint8, device="cuda")
+    ws = raw_ws[guard:guard + ws_bytes]
+    fa.fused_fp4_attention_into(Q, K, V, out, ws, causal=causal)
+    assert fa.status_query() == fa.OK
+    for raw, fill in ((raw_out, 0xA5), (raw_ws, 0x5A)):
+        assert bool((raw[:guard] == fill).all()) and bool((raw[-guard:] == fill).all())
+    for t, t0 in zip((Q, K, V), inputs_before):
+        assert torch.equal(t, t0)
+    want = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy(),
+                                causal=causal)
+    got = out[0].float().cpu().numpy()
+    if out_dtype == torch.float16:
+        want = want.astype(np.float16).astype(np.float32)
+    assert_close(got, want)
