@@ -405,3 +405,24 @@ def test_no_writes_outside_the_output_and_workspace(fa, cuda, d, out_dtype, sq, 
     if out_dtype == torch.float16:
         want = want.astype(np.float16).astype(np.float32)
     assert_close(got, want)
+
+
+def test_no_writes_outside_the_scores(fa, cuda):
+    """fp4attn_debug_scores writes exactly the [slices, seq_q, seq_k] FP32
+    scores (ragged in both dimensions) and nothing around them."""
+    import ctypes
+    B, H, sq, sk, d, guard = 1, 2, 130, 70, 64, 4096
+    g = torch.Generator().manual_seed(17)
+    Q, K = (torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk))
+    n = B * H * sq * sk * 4
+    raw = torch.full((n + 2 * guard,), 0xA5, dtype=torch.uint8, device="cuda")
+    S = raw[guard:guard + n].view(torch.float32)
+    ws = torch.empty(fa.workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+    rc = fa.lib().fp4attn_debug_scores(Q.data_ptr(), K.data_ptr(), S.data_ptr(), fa.F16, B, H, sq, sk, d,
+                                       fa.SCALE_REFERENCE, ws.data_ptr(), ws.numel(),
+                                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == fa.OK and fa.status_query() == fa.OK
+    assert bool((raw[:guard] == 0xA5).all()) and bool((raw[-guard:] == 0xA5).all())
+    S = S.view(H, sq, sk).cpu().numpy()
+    for h in range(H):
+        assert np.array_equal(S[h], oracle.fp4_scores(Q[0, h].float().cpu().numpy(), K[0, h].float().cpu().numpy()))

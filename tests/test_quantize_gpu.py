@@ -109,3 +109,24 @@ def test_two_devices_in_one_process(fa, cuda):
             torch.cuda.synchronize(dev)
             assert np.array_equal(s.cpu().numpy(), os_)
             assert np.array_equal(c.cpu().numpy(), oracle.pack_codes(oc))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_no_writes_outside_codes_and_scales(fa, cuda, dtype):
+    """fp4attn_quantize writes rows x D/2 code bytes and rows x D/32 scale
+    bytes and nothing around them (guard bytes in place of a sanitizer)."""
+    import ctypes
+    rows, d, guard = 777, 96, 4096
+    x = torch.randn(rows, d, generator=torch.Generator().manual_seed(5)).to(dtype).cuda()
+    raw_c = torch.full((rows * d // 2 + 2 * guard,), 0xA5, dtype=torch.uint8, device="cuda")
+    raw_s = torch.full((rows * d // 32 + 2 * guard,), 0x5A, dtype=torch.uint8, device="cuda")
+    codes, scales = raw_c[guard:guard + rows * d // 2], raw_s[guard:guard + rows * d // 32]
+    rc = fa.lib().fp4attn_quantize(x.data_ptr(), fa.F16 if dtype == torch.float16 else fa.F32, rows, d,
+                                   codes.data_ptr(), scales.data_ptr(), fa.SCALE_REFERENCE, 0,
+                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == fa.OK and fa.status_query() == fa.OK
+    for raw, fill in ((raw_c, 0xA5), (raw_s, 0x5A)):
+        assert bool((raw[:guard] == fill).all()) and bool((raw[-guard:] == fill).all())
+    oc, os_ = oracle.quantize(x.float().cpu().numpy())
+    assert np.array_equal(scales.cpu().numpy().reshape(rows, -1), os_)
+    assert np.array_equal(codes.cpu().numpy().reshape(rows, -1), oracle.pack_codes(oc))
