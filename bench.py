@@ -42,20 +42,29 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--box-steps", type=int, default=5,
+                    help="steps of this rank's share of the box-scale job (0: skip)")
     return ap.parse_args()
 
 
 def measured_peaks():
-    """bf16 dense TFLOP/s and HBM GB/s for the roofline.  The attention kernel
-    is timed inside a long loop of steps at the power cap, so the sustained
-    GEMM figure is its denominator when the measured peaks carry one."""
+    """Dense bf16 TFLOP/s as a burst (a kernel timed alone, at full clock)
+    and sustained (seconds-long back-to-back work at the power cap), HBM
+    GB/s, and where they come from."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        if d.get("bf16_tflops_sustained"):
-            return float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured sustained"
-        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured burst"
-    return 1590.0, 6650.0, "fallback"
+        burst = float(d["bf16_tflops"])
+        return burst, float(d.get("bf16_tflops_sustained") or burst), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def peak_basis(timed_s, reasons):
+    """The bf16 figure a kernel timed over `timed_s` seconds under the
+    sampled throttle `reasons` is held to: the sustained one only when the
+    timed region is seconds long and the clocks were power-capped in it,
+    otherwise the burst one."""
+    return "sustained" if timed_s >= 2.0 and "sw_power_cap" in reasons else "burst"
 
 
 def mixed_roofline(w, bf16_tflops):
@@ -202,12 +211,84 @@ def dist_setup(args):
     return world, rank, local
 
 
-def reference_arm(args, world, rank):
+def time_box_share(args, world, rank, dev):
+    """Quantise + attend over this rank's share of the 512-slice box-scale
+    job (B16 H32 8192^2 d128, FP32 out): (ms per step, attention-kernel ms,
+    slices).  Inputs are drawn on the device and exceed the L2."""
+    import torch
+    import fp4attn_b200 as fa
     import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS["box_sharded_8k"]
+    lo, hi = fa.shard_range(w.slices, world, rank)
+    n = hi - lo
+    Q, K, V = (t[None] for t in wl.make_inputs(w, args.seed, slices=(lo, hi), device=dev))
+    out = torch.empty((1, n, w.seq_q, w.head_dim), dtype=torch.float32, device=dev)
+    ws = torch.empty(fa.workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.box_steps)]
+    for i in range(2 + args.box_steps):
+        e = ev[i - 2] if i >= 2 else None
+        if e:
+            e[0].record(stream)
+        fa.prepare(Q, K, V, ws)
+        if e:
+            e[1].record(stream)
+        fa.attend(V, out, ws, fa.F16, 1, n, w.seq_q, w.seq_k, w.head_dim)
+        if e:
+            e[2].record(stream)
+        if i == 1:
+            torch.cuda.synchronize()
+            if world > 1:
+                import torch.distributed as dist
+                dist.barrier()
+    torch.cuda.synchronize()
+    if fa.status_query() != fa.OK:
+        raise SystemExit("box-scale share reported a device timeout")
+    ms = ev[0][0].elapsed_time(ev[-1][2]) / args.box_steps
+    kms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.box_steps
+    del Q, K, V, out, ws
+    torch.cuda.empty_cache()
+    return ms, kms, n
+
+
+def l2_note(io_bytes, l2_bytes=L2_BYTES):
+    """Whether timed steps are preceded by an L2 flush (inputs + output
+    smaller than twice the L2), and the sentence that says so."""
+    flush = io_bytes < 2 * l2_bytes
+    text = (f"inputs+output {io_bytes / 2**20:.0f} MiB < 2x L2: {2 * l2_bytes / 2**20:.0f} MiB written before "
+            f"every step (L2 flush), outside the step time" if flush else
+            f"inputs+output {io_bytes / 2**20:.0f} MiB > 2x {l2_bytes / 2**20:.0f} MiB L2; no flush")
+    return flush, text
+
+
+def job_config(args, world, rank):
+    """The workload, this rank's slice range and the run's `config` (the same
+    keys and values in both arms)."""
+    import fp4attn_b200.workloads as wl
+    from fp4attn_b200 import shard_range
+    base = wl.WORKLOADS[args.workload]
+    strong = args.workload == "box_sharded_8k"
+    if strong:  # fixed 512-slice job split over the ranks
+        job = base
+        lo, hi = shard_range(job.slices, world, rank)
+    else:  # weak scaling: each rank runs the workload as its shard of a world-times larger batch
+        job = wl.Workload(base.name, base.batch * world, base.heads, base.seq_q, base.seq_k, base.head_dim,
+                          base.std, base.outlier_frac, base.outlier_mult, base.out_dtype)
+        lo, hi = rank * base.slices, (rank + 1) * base.slices
+    n = hi - lo
+    out_bytes = 2 if base.out_dtype == "float16" else 4
+    io_bytes = n * (2 * (base.seq_q + 2 * base.seq_k) + out_bytes * base.seq_q) * base.head_dim
+    _, l2 = l2_note(io_bytes)
+    config = {"workload": base.name, "shape": base.describe(), "slices_per_gpu": n, "job_slices": job.slices,
+              "parallelism": f"slice-shard x{world}", "l2": l2}
+    return base, job, strong, lo, hi, config
+
+
+def reference_arm(args, world, rank):
     if rank != 0:
         return
-    w = wl.WORKLOADS[args.workload]
-    cpu = CpuReference(w)
+    base, _, strong, _, _, config = job_config(args, world, rank)
+    cpu = CpuReference(base)
     cpu.calibrate(max(0.02, 60.0 / max(1, args.steps + args.warmup)))
     rates = []
     for i in range(args.warmup + args.steps):
@@ -219,8 +300,8 @@ def reference_arm(args, world, rank):
     line = {
         "impl": "reference", "metric": "fused FP4 attention TFLOPS", "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU, FP4-dequantised Q/K)", "data": "synthetic",
-        "config": {"workload": w.name, "shape": w.describe(), "per_gpu_slices": w.slices},
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32 (CPU, FP4-dequantised Q/K)",
+        "data": "synthetic", "config": config,
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -243,15 +324,7 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    base = wl.WORKLOADS[args.workload]
-    strong = args.workload == "box_sharded_8k"
-    if strong:  # fixed 512-slice job split over the ranks
-        job = base
-        lo, hi = fa.shard_range(job.slices, world, rank)
-    else:  # weak scaling: each rank runs the workload as its shard of a world-times larger batch
-        job = wl.Workload(base.name, base.batch * world, base.heads, base.seq_q, base.seq_k, base.head_dim,
-                          base.std, base.outlier_frac, base.outlier_mult, base.out_dtype)
-        lo, hi = rank * base.slices, (rank + 1) * base.slices
+    base, job, strong, lo, hi, config = job_config(args, world, rank)
     n = hi - lo
     Q, K, V = wl.make_inputs(job, args.seed, slices=(lo, hi), device=dev)
     Q, K, V = Q[None], K[None], V[None]  # [1, n, seq, d]: batch x head slices flattened
@@ -291,10 +364,9 @@ def main():
     # Inputs smaller than twice the L2 would be served from it: then every
     # timed step is preceded by a write of twice the L2 size, and each step is
     # timed by its own events so the flush stays outside the step time.
-    l2_bytes = int(getattr(props, "L2_cache_size", 126 << 20))
     io_bytes = sum(t.numel() * t.element_size() for t in (Q, K, V, out))
-    flush = io_bytes < 2 * l2_bytes
-    flush_buf = torch.empty(2 * l2_bytes, dtype=torch.uint8, device=dev) if flush else None
+    flush, _ = l2_note(io_bytes)
+    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush else None
     sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
@@ -364,20 +436,31 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in (hQ, hK, hV))
     d2h = hO[0].numel() * hO[0].element_size()
 
-    times = torch.tensor([ms_total, kern_ms, e2e_ms, float(status)], dtype=torch.float64, device=dev)
+    # This rank's share of the box-scale job (512 slices split over the
+    # ranks), timed at every N so that one scaling run also gives the
+    # strong-scaling curve of that job.
+    del d_in, d_out, hQ, hK, hV, hO
+    box_ms, box_kern_ms, box_n = (0.0, 0.0, 0) if args.box_steps <= 0 else time_box_share(args, world, rank, dev)
+
+    times = torch.tensor([ms_total, kern_ms, e2e_ms, float(status), box_ms, box_kern_ms], dtype=torch.float64,
+                         device=dev)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms_total, kern_ms, e2e_ms, status_max = times.tolist()
+    ms_total, kern_ms, e2e_ms, status_max, box_ms, box_kern_ms = times.tolist()
     ms_step = ms_total / args.steps
     total_flops = flops_rank * world
     value = total_flops / (ms_step * 1e-3) / 1e12
     e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
 
     if rank == 0:
-        bf16, hbm, peak_src = measured_peaks()
+        burst, sustained, hbm, peak_src = measured_peaks()
+        clocks = sampler.summary(t_wall0, t_wall1)
+        basis = peak_basis(ms_total * 1e-3, clocks["reasons"])
         w_shard = wl.Workload(base.name, 1, n, base.seq_q, base.seq_k, base.head_dim)
-        peak = mixed_roofline(w_shard, bf16)
+        peak_burst, peak_sust = mixed_roofline(w_shard, burst), mixed_roofline(w_shard, sustained)
+        peak = peak_burst if basis == "burst" else peak_sust
+        bf16 = burst if basis == "burst" else sustained
         achieved = flops_rank / (kern_ms * 1e-3) / 1e12
         kernel = "fp4_attention_pair_kernel" if base.head_dim <= 128 else "fp4_attention_fwd_kernel"
         traffic = profile_traffic(args.workload, kernel)
@@ -392,26 +475,32 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "e2m1 (QK^T) + f16 (PV)",
             "data": "synthetic (seeded N(0,1) FP16 on device)",
-            "config": {"workload": base.name, "shape": base.describe(), "slices_per_gpu": n,
-                       "job_slices": job.slices, "parallelism": f"slice-shard x{world}",
-                       "l2": (f"inputs+output {io_bytes / 2**20:.0f} MiB < 2x L2: {2 * l2_bytes / 2**20:.0f} MiB "
-                              f"written before every step (L2 flush), outside the step time" if flush else
-                              f"inputs+output {io_bytes / 2**20:.0f} MiB > 2x {l2_bytes / 2**20:.0f} MiB L2; no flush")},
+            "config": config,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "peak_basis": f"mixed: QK^T at 4x and PV at 1x the {peak_src} bf16 dense "
-                                       f"{bf16:g} TFLOP/s",
+                         "peak_basis": f"mixed: QK^T at 4x and PV at 1x the {peak_src} {basis} bf16 dense "
+                                       f"{bf16:g} TFLOP/s ({basis}: timed region {ms_total * 1e-3:.3g} s, "
+                                       f"throttle reasons {clocks['reasons'] or 'none'})",
+                         "frac_burst": achieved / peak_burst, "frac_sustained": achieved / peak_sust,
+                         "peak_burst": peak_burst, "peak_sustained": peak_sust,
                          "kernel": kernel, "kernel_ms": kern_ms},
             "frac_of_mixed_roofline_step": value / world / peak,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
                     "overlap": "H2D, compute and D2H of consecutive steps on three streams, two buffer sets"},
             "gpu_launches": 2 * args.steps,  # per step: one quantise launch (Q and K) + one attention launch
-            "clocks": sampler.summary(t_wall0, t_wall1),
+            "clocks": clocks,
             "device_status": int(status_max),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if box_n:
+            box = wl.WORKLOADS["box_sharded_8k"]
+            line["box_8k"] = {
+                "job": box.describe(), "slices_per_gpu": box_n, "steps": args.box_steps,
+                "ms_per_step": box_ms, "kernel_ms": box_kern_ms,
+                "tflops_job": box.flops() / (box_ms * 1e-3) / 1e12,
+                "timing": "quantise + attend over this rank's share, CUDA events, max over ranks"}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -59,7 +59,9 @@ struct PairCfg {
     static constexpr int QK_ROW = DP / 2;                   // bytes per packed code row
     static constexpr int CW = QK_ROW;                       // swizzle chunk = whole row (32 or 64 B)
     static constexpr int KSTEPS = DP / 64;                  // mxf4 MMAs per S tile
-    static constexpr int VCW = D == 32 ? 64 : 128;          // swizzle chunk of a V row (bytes)
+    // Swizzle chunk of a V row (bytes): 128 where it divides the row, else 64
+    // (head_dim 32 and 96), so no chunk carries padding columns into P.V.
+    static constexpr int VCW = (2 * D) % 128 == 0 ? 128 : 64;
     static constexpr int VCH = (2 * D + VCW - 1) / VCW;     // V chunks (TMA boxes) per tile
     static constexpr int L_COL = VCH * VCW / 2;             // O column holding the row sum l
     static constexpr int NPV = L_COL + 16;                  // P.V MMA width: V chunks + the ones block

@@ -19,6 +19,38 @@
 #include "attention_pair.cuh"
 #include "quantize.cuh"
 
+namespace fp4attn {
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId; an id
+// is never reused within a process), or 0 when no context is current yet or
+// the driver lacks the call.  Per-device state that a device reset would
+// invalidate (kernel attributes, symbol addresses) is keyed on it.
+unsigned long long current_context_id()
+{
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    });
+    if (!get_current || !get_id) return 0;
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+    unsigned long long id = 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+}  // namespace fp4attn
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -110,11 +142,40 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
     return fn;
 }
 
+// Recently encoded tensor maps of this host thread.  A map is a pure function
+// of its arguments (no device state), so a repeated call with the same
+// pointers and shape -- a serving loop, a benchmark -- reuses the encoding.
+struct MapKey {
+    const void* base;
+    uint64_t inner, rows, slices;
+    uint32_t box_inner, box_rows;
+    int dt, sw;
+    bool operator==(const MapKey& o) const
+    {
+        return base == o.base && inner == o.inner && rows == o.rows && slices == o.slices &&
+               box_inner == o.box_inner && box_rows == o.box_rows && dt == o.dt && sw == o.sw;
+    }
+};
+struct MapCache {
+    static constexpr int kEntries = 16;
+    MapKey key[kEntries];
+    CUtensorMap map[kEntries];
+    int used = 0, next = 0;
+};
+thread_local MapCache g_map_cache;
+
 // 3-D tensor map over [slices][rows][inner] with a (box_inner, box_rows, 1)
 // box; rows past `rows` read as zero.
 int make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
                 uint64_t rows, uint64_t slices, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw)
 {
+    const MapKey key{base, inner, rows, slices, box_inner, box_rows, static_cast<int>(dt), static_cast<int>(sw)};
+    MapCache& c = g_map_cache;
+    for (int i = 0; i < c.used; i++)
+        if (c.key[i] == key) {
+            *m = c.map[i];
+            return FP4ATTN_OK;
+        }
     auto enc = tensor_map_encoder();
     if (!enc) return fail(FP4ATTN_ECUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[3] = {inner, rows, slices};
@@ -124,6 +185,10 @@ int make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const vo
     CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(FP4ATTN_ECUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    const int slot = c.used < MapCache::kEntries ? c.used++ : c.next;
+    c.next = (slot + 1) % MapCache::kEntries;
+    c.key[slot] = key;
+    c.map[slot] = *m;
     return FP4ATTN_OK;
 }
 
@@ -133,8 +198,8 @@ CUtensorMapSwizzle swizzle_for(int bytes)
 }
 
 // Per-device set-up, done once per device on its first use from any host
-// thread: check for an sm_100 GPU, upload the scale-rule table to that
-// device's constant memory, and record its SM count.
+// thread: check for an sm_100 GPU and record its SM count.  Nothing is
+// uploaded: the scale-rule table is initialised in the module image.
 constexpr int kMaxDevices = 64;
 struct DeviceState {
     bool done = false;
@@ -171,10 +236,6 @@ int device_ready()
             d.status = FP4ATTN_EUNSUPPORTED;
             d.msg = "libfp4attn requires an sm_100 (B200-class) GPU; found sm_" + std::to_string(prop.major) +
                     std::to_string(prop.minor);
-        } else if (cudaMemcpyToSymbol(fp4attn::kLog2CeilCompat, kLog2CeilCompatInit, sizeof kLog2CeilCompatInit) !=
-                   cudaSuccess) {
-            d.status = FP4ATTN_ECUDA;
-            d.msg = "could not upload the scale table";
         } else {
             d.sms = prop.multiProcessorCount;
         }
@@ -192,18 +253,20 @@ int device_sms()
     return g_dev[dev].sms > 0 ? g_dev[dev].sms : 1;
 }
 
-// Sets a kernel's dynamic shared memory limit once per device; `done_mask`
-// (one bit per device) belongs to the calling launcher, i.e. to one kernel.
+// Sets a kernel's dynamic shared memory limit once per device context;
+// `done_ctx` (the context id it was last set in, per device) belongs to the
+// calling launcher, i.e. to one kernel.  A device reset makes a new context,
+// and the attribute is set again there.
 template <typename Kern>
-int set_smem_once(Kern kern, int bytes, std::atomic<unsigned long long>& done_mask)
+int set_smem_once(Kern kern, int bytes, std::atomic<unsigned long long> (&done_ctx)[kMaxDevices])
 {
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
-    const unsigned long long bit = 1ull << dev;
-    if (done_mask.load(std::memory_order_acquire) & bit) return FP4ATTN_OK;
+    const unsigned long long ctx = fp4attn::current_context_id();
+    if (ctx != 0 && done_ctx[dev].load(std::memory_order_acquire) == ctx) return FP4ATTN_OK;
     FP4_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done_mask.fetch_or(bit, std::memory_order_release);
+    done_ctx[dev].store(ctx, std::memory_order_release);
     return FP4ATTN_OK;
 }
 
@@ -283,7 +346,7 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
         launch_regs > fp4attn::kLaunchRegs)
         return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
                     launch_regs, fp4attn::kLaunchRegs);
-    static std::atomic<unsigned long long> smem_set{0};
+    static std::atomic<unsigned long long> smem_set[kMaxDevices]{};
     if (int rc = set_smem_once(kern, C::SMEM_BYTES, smem_set)) return rc;
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
     // Attention output is written by TMA stores in 32-row x OCH_E-column boxes
@@ -355,7 +418,7 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
         launch_regs > fp4attn::kLaunchRegs)
         return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
                     launch_regs, fp4attn::kLaunchRegs);
-    static std::atomic<unsigned long long> smem_set{0};
+    static std::atomic<unsigned long long> smem_set[kMaxDevices]{};
     if (int rc = set_smem_once(kern, C::SMEM_BYTES, smem_set)) return rc;
     if (slices > 65535) return fail(FP4ATTN_EINVAL, "batch*heads = %lld exceeds 65535", static_cast<long long>(slices));
     fp4attn::PairArgs a;
@@ -527,7 +590,8 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     tv = tk;
     if (!scores) {
         const void* v16 = in_dtype == FP4ATTN_F32 ? static_cast<const void*>(ws + p.w.v16) : V;
-        const int vcw = d == 32 ? 64 : 128;
+        // The V chunk width of the kernel that runs (PairCfg / FwdCfg::VCW).
+        const int vcw = paired(d) ? ((2 * d) % 128 == 0 ? 128 : 64) : 128;
         if ((rc = make_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v16, d, sk, p.slices, vcw / 2, bn,
                               swizzle_for(vcw))))
             return rc;

@@ -31,7 +31,8 @@
 #include "../../include/fp4attn.h"
 
 namespace fp4attn {
-void set_error_detail(const char* msg);  // fp4attn.cu
+void set_error_detail(const char* msg);          // fp4attn.cu
+unsigned long long current_context_id();         // fp4attn.cu
 }
 
 namespace {
@@ -41,20 +42,29 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// Per device: the scratch's device address and the context it belongs to.
+struct ScratchAddr {
+    unsigned long long ctx = 0;
+    void* addr = nullptr;
+};
 std::mutex g_setup_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
+ScratchAddr g_scratch_addr[kMaxDevices];
 
-// Device address of the scratch array on `dev`, looked up once per device
-// with that device current (the host-side name of a __device__ array is not a
-// device address).
+// Device address of the scratch array on `dev` (the current device), looked
+// up once per device with that device current: the host-side name of a
+// __device__ array is not a device address.  The lookup is repeated when the
+// device's context has changed since (a device reset destroys the context,
+// and the module, with the array, is loaded again at another address).
 int scratch_address(int dev, void** out)
 {
     if (dev < 0 || dev >= kMaxDevices) {
         fp4attn::set_error_detail("fp4attn_forward_noalloc: device ordinal out of range");
         return FP4ATTN_EUNSUPPORTED;
     }
+    const unsigned long long ctx = fp4attn::current_context_id();
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& s = g_scratch_addr[dev];
+    if (!s.addr || ctx == 0 || s.ctx != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -64,9 +74,11 @@ int scratch_address(int dev, void** out)
             fp4attn::set_error_detail(buf);
             return FP4ATTN_ECUDA;
         }
-        g_scratch_addr[dev] = p;
+        s.addr = p;
+        // The lookup itself makes the primary context current when none was.
+        s.ctx = ctx != 0 ? ctx : fp4attn::current_context_id();
     }
-    *out = g_scratch_addr[dev];
+    *out = s.addr;
     return FP4ATTN_OK;
 }
 

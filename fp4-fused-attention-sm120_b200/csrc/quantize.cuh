@@ -18,7 +18,10 @@ namespace fp4attn {
 
 // See gen_log2_compat.c: largest mantissa remainder, per binade, for which the
 // reference's host build (glibc log2f) rounds ceil(log2(y)) down to p.
-__constant__ uint8_t kLog2CeilCompat[FP4ATTN_LOG2_COMPAT_ENTRIES];
+// The values are part of the module image (no upload), so the table exists
+// on a device as soon as the module is loaded there, including after a
+// context reset.
+__constant__ uint8_t kLog2CeilCompat[FP4ATTN_LOG2_COMPAT_ENTRIES] = FP4ATTN_LOG2_COMPAT_VALUES;
 
 // compute_scale_ue8m0 (common.h:39-48) on the block maximum `amax` (>= +0):
 // exponent = ceilf(log2f(y)) as the reference's host build evaluates it,

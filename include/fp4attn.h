@@ -146,7 +146,8 @@ int fp4attn_attend_masked(const void* V, void* Out, int in_dtype, int out_dtype,
  * first call (or from context creation under CUDA_MODULE_LOADING=EAGER) until
  * the process exits.  Problems whose fp4attn_workspace_size exceeds 64 MiB are
  * rejected with FP4ATTN_EWORKSPACE.  The first call on a device looks up the
- * scratch's device address; make it before any stream capture.  All calls on a
+ * scratch's device address (again after a device reset, which moves it); make
+ * it before any stream capture.  All calls on a
  * device share the scratch: calls that may overlap on the GPU must be
  * serialised by the caller.  No counterpart in the reference (its kernel keeps
  * everything in shared memory and needs no workspace). */
@@ -165,9 +166,14 @@ int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, i
 
 /* Reads and clears the device error word that kernels set when a bounded
  * wait expires.  Synchronises `stream` first.  Returns FP4ATTN_OK or
- * FP4ATTN_ETIMEOUT (or FP4ATTN_ECUDA if the query itself fails).  The
- * reference has no device-side error reporting (callers only poll
- * cudaGetLastError, tests/test_attention.cu:103-105). */
+ * FP4ATTN_ETIMEOUT (or FP4ATTN_ECUDA if the query itself fails).  The word is
+ * one per device, shared by every stream: a kernel still running on another
+ * stream may set it after this call returns (it is then reported by the next
+ * query), and a timeout raised on another stream is reported by whichever
+ * query reads the word first.  To attribute a timeout to one stream's work,
+ * synchronise the other streams that run this library's kernels (or the
+ * device) before querying.  The reference has no device-side error reporting
+ * (callers only poll cudaGetLastError, tests/test_attention.cu:103-105). */
 int fp4attn_status_query(void* stream);
 
 /* Test hook for the failure path: launches one CTA that waits on an mbarrier

@@ -43,6 +43,8 @@ def oracle_lib() -> ctypes.CDLL:
                                               c.c_int, c.c_int]
         L.oracle_fp4_attention_causal.argtypes = ([_f32, _f32, _f32, _f32] + [c.c_int] * 4 +
                                                   [c.c_float, c.c_int, c.c_int])
+        L.oracle_fp4_attention_slice.argtypes = ([_f32, _f32, _f32, _f32] + [c.c_int] * 3 +
+                                                 [c.c_float, c.c_int, c.c_int])
         L.oracle_fp4_scores.argtypes = [_f32, _f32, _f32, c.c_int, c.c_int, c.c_int, c.c_int]
         L.oracle_cosine.argtypes = [_f32, _f32, c.c_int64]
         L.oracle_cosine.restype = c.c_double
@@ -143,6 +145,49 @@ def fp4_attention_rows(Q, K, V, slice_of, rows, scale: float = 0.0, scale_mode: 
     out = np.zeros((len(s), d), np.float32)
     oracle_lib().oracle_fp4_attention_rows(Q, K, V, out, len(s), s, r, sq, sk, d, scale, scale_mode)
     return out
+
+
+def fp4_attention_slice(Q, K, V, scale: float = 0.0, scale_mode: int = 0, threads: int = 0):
+    """The FP4 path for every query row of one slice [seq, head_dim], the rows
+    split over `threads` threads (0: all host cores)."""
+    import os
+    Q, K, V = _c(Q), _c(K), _c(V)
+    out = np.zeros(Q.shape, np.float32)
+    oracle_lib().oracle_fp4_attention_slice(Q, K, V, out, Q.shape[0], K.shape[0], Q.shape[1], scale, scale_mode,
+                                            threads or os.cpu_count() or 1)
+    return out
+
+
+def redo_warp_steps(Q, K, scale: float = 0.0, scale_mode: int = 0, block_n: int = 64,
+                    lazy_log2: float = 15.0) -> tuple[int, int]:
+    """Row-max statistics of one slice: how many (32-row warp, 64-key step)
+    pairs after the first step of each 256-row work item see some row's
+    max of S * scale * log2(e) grow past the running reference max by more
+    than 2^lazy_log2 -- the steps the attention kernel redoes max-first
+    (its lazy-rescale rule) -- and how many such pairs there are.  S is the
+    exact FP4 product (dequantised Q K^T); returns (redone, total)."""
+    import math
+    qd = dequantize(*quantize(Q, scale_mode)).astype(np.float64)
+    kd = dequantize(*quantize(K, scale_mode)).astype(np.float64)
+    d = Q.shape[1]
+    c = (scale if scale > 0 else 1.0 / math.sqrt(d)) * math.log2(math.e)
+    sq, sk = qd.shape[0], kd.shape[0]
+    nk = (sk + block_n - 1) // block_n
+    redone = total = 0
+    for r0 in range(0, sq, 1024):
+        S = (qd[r0:r0 + 1024] @ kd.T) * c
+        pad = nk * block_n - sk
+        if pad:
+            S = np.concatenate([S, np.full((S.shape[0], pad), -np.inf)], axis=1)
+        mx = S.reshape(S.shape[0], nk, block_n).max(axis=2)   # [rows, steps]
+        m = mx[:, 0].copy()
+        for j in range(1, nk):
+            jump = mx[:, j] > m + lazy_log2
+            m = np.where(jump, np.maximum(m, mx[:, j]), m)
+            w = jump[: (len(jump) // 32) * 32].reshape(-1, 32).any(axis=1)
+            redone += int(w.sum())
+            total += len(w)
+    return redone, total
 
 
 def fp4_scores(Q, K, scale_mode: int = 0):

@@ -249,6 +249,44 @@ void oracle_fp4_attention_rows(const float* Q, const float* K, const float* V,
     free(qd); free(kd);
 }
 
+typedef struct {
+    const float *qd, *kd, *V; float* Out;
+    int r0, r1, sk, d; float scale;
+} row_job;
+
+static void* run_rows(void* arg)
+{
+    row_job* j = (row_job*)arg;
+    if (j->r1 > j->r0)
+        oracle_attention(j->qd + (size_t)j->r0 * j->d, j->kd, j->V, j->Out + (size_t)j->r0 * j->d,
+                         j->r1 - j->r0, j->sk, j->d, j->scale);
+    return NULL;
+}
+
+/* Rows of one slice over threads: Q and K are quantised and dequantised once
+ * (as run_slices does per slice), then each thread runs oracle_attention
+ * (tests/test_attention.cu:33-54) on its block of query rows. */
+void oracle_fp4_attention_slice(const float* Q, const float* K, const float* V, float* Out,
+                                int sq, int sk, int d, float scale, int mode, int threads)
+{
+    float* qd = (float*)malloc(sizeof(float) * (size_t)sq * d);
+    float* kd = (float*)malloc(sizeof(float) * (size_t)sk * d);
+    quant_dequant(Q, sq, d, mode, qd);
+    quant_dequant(K, sk, d, mode, kd);
+    if (threads < 1) threads = 1;
+    if (threads > sq) threads = sq;
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * threads);
+    row_job* jobs = (row_job*)malloc(sizeof(row_job) * threads);
+    for (int t = 0; t < threads; t++) {
+        row_job jb = {qd, kd, V, Out, (int)((int64_t)sq * t / threads), (int)((int64_t)sq * (t + 1) / threads),
+                      sk, d, scale};
+        jobs[t] = jb;
+        pthread_create(&tid[t], NULL, run_rows, &jobs[t]);
+    }
+    for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+    free(tid); free(jobs); free(qd); free(kd);
+}
+
 /* common.h:331-398 computes one 64x64 block of Q K^T on FP4 codes; this is the
  * same product with the reference's block scales applied (common.h:208-213). */
 void oracle_fp4_scores(const float* Q, const float* K, float* S, int sq, int sk, int d,

@@ -85,6 +85,14 @@ void oracle_fp4_attention_rows(const float* Q, const float* K, const float* V,
                                int seq_q, int seq_k, int head_dim,
                                float scale, int scale_mode);
 
+/* The same path over every query row of ONE slice, with the rows split over
+ * up to `threads` POSIX threads (for whole-slice parity at full sizes, where
+ * the per-slice threading of oracle_fp4_attention has one slice to run).
+ * Each row is computed exactly as oracle_attention computes it. */
+void oracle_fp4_attention_slice(const float* Q, const float* K, const float* V, float* Out,
+                                int seq_q, int seq_k, int head_dim, float scale, int scale_mode,
+                                int threads);
+
 /* Q K^T for one slice on dequantised FP4 inputs (the S tile of the
  * reference's debug_mma kernel, common.h:331-398, generalised to any
  * seq_q x seq_k with block scales).  No softmax scale applied. */

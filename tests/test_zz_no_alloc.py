@@ -1,8 +1,10 @@
 """fp4attn_forward_noalloc: the forward pass for callers that cannot allocate
 device memory (work done during CUDA graph capture, runtimes that own all
-device memory, loops that must not block on an allocation).  It must give
-the same result as fp4attn_forward with a caller workspace, including on a
-second call that reuses the scratch the first call left behind.
+device memory, loops that must not block on an allocation).  It runs the same
+kernels as fp4attn_forward with a caller workspace, so on the same inputs its
+output must be the same bytes -- including on later calls that reuse the
+scratch an earlier, larger call left behind -- and it must match the oracle at
+the attention tests' tolerance.
 
 This file is named to be collected last, so a run that stops at the first
 failure has already run every other test."""
@@ -29,33 +31,49 @@ def _bind(fa):
     return f
 
 
+def _dt(fa, t):
+    return fa.F32 if t.dtype == torch.float32 else fa.F16
+
+
 def _noalloc(fa, Q, K, V, out):
     B, H, Sq, D = Q.shape
     Sk = K.shape[2]
-    rc = _bind(fa)(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), fa.F16,
-                   fa.F32 if out.dtype == torch.float32 else fa.F16, B, H, Sq, Sk, D, 0.0, fa.SCALE_REFERENCE,
-                   torch.cuda.current_stream().cuda_stream)
-    return rc
+    return _bind(fa)(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), _dt(fa, Q), _dt(fa, out), B, H, Sq,
+                     Sk, D, 0.0, fa.SCALE_REFERENCE, torch.cuda.current_stream().cuda_stream)
 
 
-def _inputs(seed, B, H, Sq, Sk, D):
+def _inputs(seed, B, H, Sq, Sk, D, dtype):
     g = torch.Generator().manual_seed(seed)
-    return [torch.randn(B, H, s, D, generator=g).half().cuda() for s in (Sq, Sk, Sk)]
+    return [torch.randn(B, H, s, D, generator=g).half().to(dtype).cuda() for s in (Sq, Sk, Sk)]
 
 
-def test_two_calls_match_the_workspace_entry_point(fa, cuda):
-    shapes = [(1, 8, 300, 1000, 128), (2, 4, 64, 200, 64)]
-    for call, (B, H, Sq, Sk, D) in enumerate(shapes):
-        Q, K, V = _inputs(100 + call, B, H, Sq, Sk, D)
-        out = torch.full((B, H, Sq, D), float("nan"), dtype=torch.float32, device="cuda")
-        assert _noalloc(fa, Q, K, V, out) == fa.OK, fa.lib().fp4attn_last_error()
-        assert fa.status_query() == fa.OK
-        want = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float32)
-        assert fa.status_query() == fa.OK
-        got, ref = out.cpu().numpy(), want.cpu().numpy()
-        assert np.isfinite(got).all()
-        assert oracle.cosine(got, ref) >= COS_MIN
-        assert float(np.abs(got - ref).max()) <= MAXABS
+def _check_call(fa, seed, shape, in_dtype, out_dtype):
+    B, H, Sq, Sk, D = shape
+    Q, K, V = _inputs(seed, B, H, Sq, Sk, D, in_dtype)
+    out = torch.full((B, H, Sq, D), float("nan"), dtype=out_dtype, device="cuda")
+    assert _noalloc(fa, Q, K, V, out) == fa.OK, fa.lib().fp4attn_last_error()
+    assert fa.status_query() == fa.OK
+    # The workspace entry point on the same inputs: the same kernels, so the
+    # same bytes.
+    want = fa.fused_fp4_attention(Q, K, V, out_dtype=out_dtype)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(out, want)
+    ref = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy())
+    if out_dtype == torch.float16:
+        ref = ref.astype(np.float16).astype(np.float32)
+    got = out[0].float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert oracle.cosine(got, ref) >= COS_MIN
+    assert float(np.abs(got - ref).max()) <= MAXABS
+
+
+@pytest.mark.parametrize("in_dtype", [torch.float16, torch.float32])
+def test_two_calls_match_the_workspace_entry_point(fa, cuda, in_dtype):
+    """A larger call, then a smaller one with the other output type, on the
+    scratch the first call left behind.  FP32 input also stages an FP16 copy
+    of V in the scratch."""
+    _check_call(fa, 100, (1, 8, 300, 1000, 128), in_dtype, torch.float32)
+    _check_call(fa, 101, (1, 4, 64, 200, 64), in_dtype, torch.float16)
 
 
 def test_rejects_problems_larger_than_the_scratch(fa, cuda):
