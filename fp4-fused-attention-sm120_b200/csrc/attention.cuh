@@ -126,6 +126,12 @@ struct FwdArgs {
     unsigned long long timeout_ns;
     int causal;                // 1: query i sees keys j <= i + causal_off only (attention, not scores)
     int causal_off;            // seq_k - seq_q (bottom-right alignment)
+    // The two-query-tile kernel's schedule (PairArgs): query tiles per item,
+    // key partitions and their partial results.
+    int qtiles, n_pairs, kparts, nk_part;
+    float2* part_ml;
+    float* part_o;
+    unsigned* part_count;
 };
 
 // Work item r of this CTA's static schedule for the one-tile kernel: (slice,
@@ -173,6 +179,7 @@ enum WaitSite : int {
     kSiteDrain,
     kSiteSFree,
     kSiteQEmpty,
+    kSitePartDone,
 };
 
 struct WaitCtx {

@@ -36,6 +36,15 @@
 //               threshold is the step redone max-first, so the max is off the
 //               critical path.
 //
+// Small problems (kSmall, a separate instantiation so that the kernel for
+// large problems keeps its own code).  With seq_q <= 128 an item is one query
+// tile (qtiles = 1: tile T1 and its warpgroup stay idle instead of computing
+// padding rows), and when there are fewer (slice, query tile group) groups
+// than SMs the keys of a group are split into kparts partitions, one work item
+// each (flash-decoding): the item writes its unnormalised O, row max and row
+// sum to the workspace, and the CTA whose item completes a group last (a
+// per-group arrival counter) merges the partitions into the output.
+//
 // TMEM columns (512 allocated): S_0 [0,64), S_1 [64,128), O_0, O_1 (NPV each:
 // V's padded width + 16 columns holding l), P_0, P_1 (32 each: 64 FP16
 // pairs), the two Q scale column groups, then KST groups of K scale columns.
@@ -50,6 +59,9 @@
 #include "attention.cuh"
 
 namespace fp4attn {
+
+// Most key partitions per query group (the planner caps kparts at this).
+constexpr int kMaxKParts = 16;
 
 template <int D>
 struct PairCfg {
@@ -94,8 +106,9 @@ struct PairCfg {
     static constexpr int OST_BYTES = 32 * 32 * 4;
     static constexpr int OFF_OST = OFF_V + VST * V_STRIDE;
     static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
-    // q_full, q_empty, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain
-    static constexpr int NUM_BARS = 2 + 2 * KST + 2 * VST + 8 + 1;
+    // q_full, q_empty, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain,
+    // part_done, merge_go
+    static constexpr int NUM_BARS = 2 + 2 * KST + 2 * VST + 8 + 1 + 2;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -103,8 +116,8 @@ struct PairCfg {
 struct PairArgs {
     int seq_q, seq_k;
     int nk_tiles;
-    int n_pairs;               // query tile pairs per slice (q_sf_tiles / 2)
-    int n_items;               // work items = n_pairs * slices
+    int n_pairs;               // query groups (pairs, or single tiles when qtiles == 1) per slice
+    int n_items;               // work items = slices * n_pairs * kparts
     int q_sf_tiles;            // 128-row scale tiles per slice in q_sf (even)
     float scale_log2;          // softmax_scale * log2(e)
     void* out;                 // [slices, seq_q, D]
@@ -113,6 +126,16 @@ struct PairArgs {
     unsigned long long timeout_ns;
     int causal;                // 1: query i sees keys j <= i + causal_off only
     int causal_off;            // seq_k - seq_q (bottom-right alignment)
+    // Small problems (the kSmall kernel; 2, 1, nk_tiles and unused otherwise).
+    int qtiles;                // query tiles per item: 2 (a pair) or 1 (seq_q <= 128)
+    int kparts;                // key partitions per group (1: the whole key range; no mask)
+    int nk_part;               // key tiles per partition (the last may have fewer)
+    // kparts > 1: per (item, tile) 128 rows of (reference max m in log2 units,
+    // row sum l) and, written through tm_p, of unnormalised FP32 O; one
+    // arrival counter per group, zero between launches.
+    float2* part_ml;           // [n_items][qtiles][128]
+    const float* part_o;       // [n_items][qtiles][128][D]
+    unsigned* part_count;      // [slices * n_pairs]
 };
 
 // Work item r of this CTA's static schedule: (slice, query-tile pair) and its
@@ -124,13 +147,17 @@ struct PairArgs {
 struct PairItem {
     int slice, pair, nk;
     bool valid;
+    int k0;                    // kSmall: first key tile of the item's partition
+    int idx;                   // kSmall: item index (partial buffers)
 };
 
+template <bool kSmall>
 __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
 {
     const int G = gridDim.x, b = blockIdx.x;
     PairItem it;
     if (a.causal) {
+        // (With the mask kparts == 1; with qtiles == 1 a slice has one group, pair 0.)
         const int w = r * G + ((r & 1) ? G - 1 - b : b);
         const int slices = a.n_items / a.n_pairs;
         it.valid = w < a.n_items;
@@ -139,6 +166,19 @@ __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
         const int last_row = min(it.pair * 256 + 255, a.seq_q - 1);
         const int hi = last_row + a.causal_off;  // last key any row of the item sees
         it.nk = hi < 0 ? 1 : min(a.nk_tiles, hi / 64 + 1);
+        it.k0 = 0;
+        it.idx = w;
+    } else if constexpr (kSmall) {
+        // Consecutive items: the key partitions of one group, then the next
+        // group of the same slice (the slice's K/V stay in L2).
+        const int w = r * G + b;
+        it.valid = w < a.n_items;
+        const int grp = w / a.kparts, part = w - grp * a.kparts;
+        it.slice = grp / a.n_pairs;
+        it.pair = grp - it.slice * a.n_pairs;
+        it.k0 = part * a.nk_part;
+        it.nk = min(a.nk_tiles - it.k0, a.nk_part);
+        it.idx = w;
     } else {
         const int w = r * G + b;
         it.valid = w < a.n_items;
@@ -149,11 +189,11 @@ __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
     return it;
 }
 
-template <int D, typename OutT, int kPoly8, bool kSpec>
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                              const PairArgs args)
+                              const __grid_constant__ CUtensorMap tm_p, const PairArgs args)
 {
     using C = PairCfg<D>;
     constexpr int BN = C::BN;
@@ -176,9 +216,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint64_t* p_full = s_free + 2;        // [t] P_t stored, O_t rescaled (128 threads)
     uint64_t* pv_done = p_full + 2;       // [t] O_t += P_t V complete (tcgen05.commit)
     uint64_t* drain_bar = pv_done + 2;
+    uint64_t* part_done = drain_bar + 1;  // kSmall: this item's partials are written (one arrive per softmax warp)
+    uint64_t* merge_go = part_done + 1;   // kSmall: the group's arrival count is known (merge_sh)
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
+    __shared__ int merge_sh;             // kSmall: 1 if this CTA completed the group and merges it
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -200,6 +243,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             ptx::mbar_init(&pv_done[t], 1);
         }
         ptx::mbar_init(drain_bar, 2);  // one commit from each MMA issuer
+        if constexpr (kSmall) {
+            ptx::mbar_init(part_done, 4 * args.qtiles);
+            ptx::mbar_init(merge_go, 1);
+        }
         abort_sh = 0;
         ptx::fence_mbar_init();
     }
@@ -208,6 +255,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ptx::prefetch_tmap(&tm_k);
         ptx::prefetch_tmap(&tm_v);
         ptx::prefetch_tmap(&tm_o);
+        if (kSmall && args.kparts > 1) ptx::prefetch_tmap(&tm_p);
     }
     if (warp == 1) {
         ptx::tmem_alloc(&tmem_base_sh, 512);
@@ -246,10 +294,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 int it = 0, kv = 0, k_issued = 0, v_issued = 0;
                 bool ok = true;
                 for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
-                    const PairItem item = pair_item(args, r);
+                    const PairItem item = pair_item<kSmall>(args, r);
                     if (!item.valid) continue;
                     const int slice = item.slice, pair = item.pair, nk = item.nk;
                     if (it > 0 && !wait_phase(q_empty, (it - 1) & 1, wctx, kSiteQEmpty)) break;
+                    if constexpr (kSmall) {
+                        const int qt = args.qtiles;
+                        ptx::mbar_arrive_expect_tx(q_full, qt * (C::Q_BYTES + C::SF_BYTES));
+                        for (int t = 0; t < qt; t++) {
+                            ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, (pair * qt + t) * C::BM, slice);
+                            ptx::bulk_load(sQsf + t * C::SF_BYTES,
+                                           args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + qt * pair + t) *
+                                                           C::SF_BYTES,
+                                           C::SF_BYTES, q_full);
+                        }
+                    } else {
                     ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
 #pragma unroll
                     for (int t = 0; t < 2; t++) {
@@ -259,7 +318,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                                                        C::SF_BYTES,
                                        C::SF_BYTES, q_full);
                     }
-                    for (int j = 0; j < nk; j++, kv++) {
+                    }
+                    for (int jl = 0; jl < nk; jl++, kv++) {
+                        const int j = kSmall ? item.k0 + jl : jl;  // key tile
                         const int ks = kv % C::KST;
                         if (kv >= C::KST && !wait_phase(&k_empty[ks], ((kv / C::KST) - 1) & 1, wctx, kSiteKEmpty)) {
                             ok = false;
@@ -307,7 +368,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 int g = 0, kv = 0, it = 0;
                 bool ok = true;
                 for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
-                    const PairItem item = pair_item(args, r);
+                    const PairItem item = pair_item<kSmall>(args, r);
                     if (!item.valid) continue;
                     const int nk = item.nk;
                     if (!wait_phase(q_full, it & 1, wctx, kSiteQFull)) break;
@@ -315,9 +376,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     // The previous item's S MMAs are complete: the producer
                     // loaded this Q only after their q_empty commit arrived.
                     const uint32_t sfa = tmem + C::SFA_COL;
+                    const int qt = kSmall ? args.qtiles : 2;
 #pragma unroll
                     for (int t = 0; t < 2; t++)
-                        ptx::tc_cp_32x128b_warpx4(sfa + 4 * t, sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
+                        if (t < qt)
+                            ptx::tc_cp_32x128b_warpx4(sfa + 4 * t, sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
                     for (int j = 0; ok && j < nk; j++, kv++, g++) {
                         const int ks = kv % C::KST;
                         if (!wait_phase(&k_full[ks], (kv / C::KST) & 1, wctx, kSiteKFull)) { ok = false; break; }
@@ -327,6 +390,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         const uint64_t kdesc = kdesc0 + static_cast<uint64_t>((ks * C::K_STRIDE) >> 4);
 #pragma unroll
                         for (int t = 0; t < 2; t++) {
+                            if (t >= qt) break;
                             // S_t's columns are free once warpgroup t holds the previous step in registers.
                             if (g > 0) {
                                 if (!wait_phase(&s_free[t], (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
@@ -364,7 +428,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 int g = 0;  // global step: p_full phase and V ring index
                 bool ok = true;
                 for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
-                    const PairItem item = pair_item(args, r);
+                    const PairItem item = pair_item<kSmall>(args, r);
                     if (!item.valid) continue;
                     const int nk = item.nk;
                     for (int j = 0; ok && j < nk; j++, g++) {
@@ -373,6 +437,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         const uint64_t vdesc = vdesc0 + static_cast<uint64_t>((vs * C::V_STRIDE) >> 4);
 #pragma unroll
                         for (int t = 0; t < 2; t++) {
+                            if (kSmall && t >= args.qtiles) break;
                             if (!wait_phase(&p_full[t], g & 1, wctx, kSitePFull)) { ok = false; break; }
                             ptx::tc_fence_after();
                             // The first step of an item starts O_t afresh.
@@ -405,14 +470,202 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t p_tm = tmem + lane_off + C::P_COL + t * (BN / 2);
         const float c = args.scale_log2;
         uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
+        // kSmall: the end of an item of tile t, once its last P.V is done.
+        // Without key partitions O / l goes to the output; with them the item
+        // stores its partials and, if it completes its group, merges them.
+        // Returns false when a wait gave up.
+        auto small_epilogue = [&](const PairItem& item, float m_ref, int& splits) -> bool {
+            ptx::tc_fence_after();
+            uint32_t lsum[16];
+            ptx::tmem_ld16(o_tm + C::L_COL, lsum);
+            ptx::tc_wait_ld();
+            const float lv = __uint_as_float(lsum[0]);
+            const int trow0 = (item.pair * args.qtiles + t) * C::BM;  // first query row of this tile
+            // 32-column chunks of this warp's 32 rows: staged swizzled like the
+            // TMA box (so a warp's 16-byte writes hit distinct banks), then one
+            // lane stores the box with TMA (rows past the map's end are
+            // clipped).  src(k, o) fills o with chunk k of this thread's row.
+            auto store_rows = [&](auto src, auto as_f32, const CUtensorMap* map, int row0, int slice_coord,
+                                  float scale) {
+                constexpr bool f32 = decltype(as_f32)::value || sizeof(OutT) == 4;
+                constexpr int OB = f32 ? 128 : 64;  // bytes per staged row
+                if (lane == 0) ptx::bulk_wait_group_read<0>();
+                __syncwarp();
+#pragma unroll 1
+                for (int k = 0; k < D / 32; k++) {
+                    uint32_t o[32];
+                    src(k, o);
+                    uint8_t* buf = ost + (k & 1) * C::OST_BYTES;
+                    if (k >= 2) {
+                        if (lane == 0) ptx::bulk_wait_group_read<1>();
+                        __syncwarp();
+                    }
+                    uint32_t ov[OB / 4];
+                    if constexpr (f32) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(o[i]) * scale);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            ov[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * scale, __uint_as_float(o[2 * i + 1]) * scale);
+                    }
+#pragma unroll
+                    for (int u = 0; u < OB / 16; u++) {
+                        const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
+                        *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
+                            make_uint4(ov[4 * u], ov[4 * u + 1], ov[4 * u + 2], ov[4 * u + 3]);
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        ptx::tma_store_3d(map, buf, 32 * k, row0, slice_coord);
+                        ptx::bulk_commit_group();
+                    }
+                }
+            };
+            auto from_tmem = [&](int k, uint32_t (&o)[32]) {
+                ptx::tmem_ld32(o_tm + 32 * k, o);
+                ptx::tc_wait_ld();
+            };
+            if (args.kparts == 1) {
+                const float inv_l = lv > 0.f ? 1.0f / lv : 0.f;  // a row that saw no key outputs 0
+                store_rows(from_tmem, std::false_type{}, &tm_o, trow0 + wq * 32, item.slice, inv_l);
+                return true;
+            }
+            // ---- a key partition: its partials ----
+            const int prow0 = (item.idx * args.qtiles + t) * C::BM;  // this tile's rows in the partials
+            args.part_ml[prow0 + row] = make_float2(m_ref, lv);
+            store_rows(from_tmem, std::true_type{}, &tm_p, prow0 + wq * 32, 0, 1.0f);
+            // Visible to the CTA that merges the group: every lane's (m, l), then
+            // lane 0's TMA stores once they are complete.
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::bulk_wait_group<0>();
+                ptx::fence_proxy_async_global();
+                __threadfence();
+                ptx::mbar_arrive(part_done);
+            }
+            if (warp == 4) {
+                // Every softmax warp of this CTA has written its partials: count
+                // this partition; the CTA that brings the count to kparts merges
+                // (and leaves the counter at zero for the next launch).
+                const bool all_in = __all_sync(0xffffffffu, wait_phase(part_done, splits & 1, wctx, kSitePartDone));
+                int last = 0;
+                if (all_in && lane == 0) {
+                    __threadfence();
+                    const unsigned prev = atomicAdd(&args.part_count[item.idx / args.kparts], 1u);
+                    last = prev + 1 == static_cast<unsigned>(args.kparts);
+                    if (last) {
+                        atomicExch(&args.part_count[item.idx / args.kparts], 0u);
+                        __threadfence();
+                    }
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (lane == 0) {
+                    merge_sh = last;
+                    ptx::mbar_arrive(merge_go);
+                }
+            }
+            if (!__all_sync(0xffffffffu, wait_phase(merge_go, splits & 1, wctx, kSitePartDone))) return false;
+            splits++;
+            if (!merge_sh) return true;
+            // ---- the group's last partition: merge the kparts partitions ----
+            // O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p, M = max_p m_p.
+            // Lane i first forms the weights w_p = 2^(m_p - M) / L of row i of
+            // this warp; then the warp walks its 32 rows in batches, each row
+            // read whole by the 32 lanes (D/32 columns each: coalesced), the
+            // batch's rows x 4 partitions of loads issued together, and
+            // writes the output rows directly (rows past seq_q are skipped).
+            const int gbase = (item.idx / args.kparts) * args.kparts;
+            auto prow = [&](int pp, int rr) { return ((gbase + pp) * args.qtiles + t) * C::BM + wq * 32 + rr; };
+            float wgt[kMaxKParts];
+            {
+                float mp[kMaxKParts], lp[kMaxKParts];
+#pragma unroll
+                for (int pp = 0; pp < kMaxKParts; pp++) {
+                    const float2 ml = __ldcg(&args.part_ml[prow(pp < args.kparts ? pp : 0, lane)]);
+                    mp[pp] = pp < args.kparts ? ml.x : -INFINITY;
+                    lp[pp] = ml.y;
+                }
+                float row_m = -INFINITY;
+#pragma unroll
+                for (int pp = 0; pp < kMaxKParts; pp++) row_m = fmaxf(row_m, mp[pp]);
+                float lsum_all = 0.f;
+#pragma unroll
+                for (int pp = 0; pp < kMaxKParts; pp++) {
+                    wgt[pp] = mp[pp] == -INFINITY ? 0.f : ptx::ex2_approx(mp[pp] - row_m);
+                    lsum_all = fmaf(wgt[pp], lp[pp], lsum_all);
+                }
+                const float row_inv = lsum_all > 0.f ? 1.0f / lsum_all : 0.f;  // a row that saw no key outputs 0
+#pragma unroll
+                for (int pp = 0; pp < kMaxKParts; pp++) wgt[pp] *= row_inv;
+            }
+            constexpr int CPL = D / 32;            // output columns per lane
+            constexpr int RB = CPL >= 3 ? 4 : 8;   // rows per batch
+            const int rows_here = min(32, args.seq_q - (trow0 + wq * 32));
+#pragma unroll 1
+            for (int r0 = 0; r0 < rows_here; r0 += RB) {
+                float acc[RB][CPL];
+#pragma unroll
+                for (int u = 0; u < RB; u++)
+#pragma unroll
+                    for (int c = 0; c < CPL; c++) acc[u][c] = 0.f;
+#pragma unroll
+                for (int pg = 0; pg < kMaxKParts; pg += 4) {
+                    if (pg >= args.kparts) break;
+                    float v[4][RB][CPL];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        // A partition past kparts reads partition pg again (weight 0).
+                        const int pp = pg + q < args.kparts ? pg + q : pg;
+#pragma unroll
+                        for (int u = 0; u < RB; u++) {
+                            const float* src = args.part_o + static_cast<size_t>(prow(pp, r0 + u)) * D + lane * CPL;
+                            if constexpr (CPL == 4) {
+                                const float4 x = __ldcg(reinterpret_cast<const float4*>(src));
+                                v[q][u][0] = x.x; v[q][u][1] = x.y; v[q][u][2] = x.z; v[q][u][3] = x.w;
+                            } else if constexpr (CPL == 2) {
+                                const float2 x = __ldcg(reinterpret_cast<const float2*>(src));
+                                v[q][u][0] = x.x; v[q][u][1] = x.y;
+                            } else {
+#pragma unroll
+                                for (int c = 0; c < CPL; c++) v[q][u][c] = __ldcg(src + c);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+#pragma unroll
+                        for (int u = 0; u < RB; u++) {
+                            const float w = __shfl_sync(0xffffffffu, wgt[pg + q], (r0 + u) & 31);
+#pragma unroll
+                            for (int c = 0; c < CPL; c++) acc[u][c] = fmaf(w, v[q][u][c], acc[u][c]);
+                        }
+                }
+#pragma unroll
+                for (int u = 0; u < RB; u++) {
+                    if (r0 + u >= rows_here) break;
+                    const size_t orow = static_cast<size_t>(item.slice) * args.seq_q + trow0 + wq * 32 + r0 + u;
+                    OutT* dst = static_cast<OutT*>(args.out) + orow * D + lane * CPL;
+#pragma unroll
+                    for (int c = 0; c < CPL; c++) {
+                        if constexpr (sizeof(OutT) == 4) dst[c] = acc[u][c];
+                        else dst[c] = __float2half_rn(acc[u][c]);
+                    }
+                }
+            }
+            return true;
+        };
         int g = 0;  // global step: phase of s_full / s_free / p_full / pv_done
-        bool ok = true;
+        int splits = 0;  // kSmall: items of split groups so far (phase of part_done / merge_go)
+        bool ok = !kSmall || t < args.qtiles;  // with one query tile per item, warpgroup 1 has no work
         for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
-            const PairItem item = pair_item(args, r);
+            const PairItem item = pair_item<kSmall>(args, r);
             if (!item.valid) continue;
             const int slice = item.slice, pair = item.pair, nk = item.nk;
             // Keys this row sees: [0, row_lim) (the causal mask, or all keys).
-            const int qi = pair * 2 * C::BM + t * C::BM + row;
+            const int qi = kSmall ? (pair * args.qtiles + t) * C::BM + row : pair * 2 * C::BM + t * C::BM + row;
             const int row_lim = args.causal ? min(qi + args.causal_off + 1, args.seq_k) : args.seq_k;
             float m = -INFINITY;
             for (int j = 0; j < nk; j++, g++) {
@@ -425,7 +678,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // S_t is in registers: the issuer may compute the next step into it.
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&s_free[t]);
-                const int valid = row_lim - j * BN;  // keys of this step this row sees
+                const int valid = row_lim - (kSmall ? item.k0 + j : j) * BN;  // keys of this step this row sees
                 uint32_t pk[NT][16];
                 // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column
                 // pairs take 2^x on the FMA pipe, the rest on MUFU.  With a true
@@ -541,6 +794,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 ok = false;
                 break;
             }
+            if constexpr (kSmall) {
+                if (!small_epilogue(item, m, splits)) {
+                    ok = false;
+                    break;
+                }
+            } else
             {
                 ptx::tc_fence_after();
                 uint32_t lsum[16];

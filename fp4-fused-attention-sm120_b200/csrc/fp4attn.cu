@@ -97,7 +97,7 @@ int sf_tile_bytes(int d, int tile_rows)
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Workspace {
-    size_t q_codes, k_codes, q_sf, k_sf, v16, total;
+    size_t q_codes, k_codes, q_sf, k_sf, v16, part_o, part_ml, part_count, total;
 };
 
 // 128-row Q scale tiles per slice: rounded up to whole pairs for the
@@ -106,6 +106,52 @@ int q_sf_tiles(int sq, int d)
 {
     const int nq = (sq + 127) / 128;
     return paired(d) ? (nq + 1) / 2 * 2 : nq;
+}
+
+// Key partitions per query group are capped by this many work items in all:
+// about one per SM of a B200 (148).  A fixed number, so that the workspace
+// size is a function of the shape alone.
+constexpr int kSplitItems = 148;
+
+// Fewest 64-key tiles a key partition gets (below that the partial results
+// and their merge cost more than the shorter key loop saves).
+// FP4ATTN_KSPLIT overrides it for tuning; 0 keeps every query group on one CTA.
+int ksplit_min_tiles()
+{
+    static int v = [] {
+        const char* s = getenv("FP4ATTN_KSPLIT");
+        return s ? atoi(s) : 4;
+    }();
+    return v;
+}
+
+// Schedule of the two-query-tile kernel for a problem: one query tile per
+// item when seq_q <= 128, otherwise pairs; and, when there are fewer query
+// groups than kSplitItems (and no mask), the keys of each group split into
+// kparts partitions of nk_part 64-key tiles, each its own work item.
+struct PairPlan {
+    int qtiles, n_pairs, kparts, nk_part;
+    int64_t groups;
+};
+
+PairPlan pair_plan(int64_t slices, int sq, int sk, int d, bool causal)
+{
+    PairPlan p;
+    const int nq = (sq + 127) / 128;
+    p.qtiles = nq == 1 ? 1 : 2;
+    p.n_pairs = p.qtiles == 1 ? 1 : q_sf_tiles(sq, d) / 2;
+    p.groups = slices * p.n_pairs;
+    const int nk = (sk + 63) / 64;
+    p.kparts = 1;
+    p.nk_part = nk;
+    const int min_tiles = ksplit_min_tiles();
+    if (!causal && min_tiles > 0 && nk >= 2 * min_tiles && p.groups * 2 <= kSplitItems) {
+        const int want = static_cast<int>(
+            std::min<int64_t>(std::min<int64_t>(nk / min_tiles, kSplitItems / p.groups), fp4attn::kMaxKParts));
+        p.nk_part = (nk + want - 1) / want;
+        p.kparts = (nk + p.nk_part - 1) / p.nk_part;
+    }
+    return p;
 }
 
 Workspace plan_workspace(int64_t slices, int sq, int sk, int d, int in_dtype)
@@ -124,6 +170,20 @@ Workspace plan_workspace(int64_t slices, int sq, int sk, int d, int in_dtype)
     off = align256(off + static_cast<size_t>(slices) * nk * sf_tile_bytes(d, bn));
     w.v16 = off;
     if (in_dtype == FP4ATTN_F32) off = align256(off + static_cast<size_t>(slices) * sk * d * 2);
+    // Key-partition partials of the two-query-tile kernel (see pair_plan).
+    w.part_o = w.part_ml = w.part_count = off;
+    if (paired(d)) {
+        const PairPlan pp = pair_plan(slices, sq, sk, d, false);
+        if (pp.kparts > 1) {
+            const size_t rows = static_cast<size_t>(pp.groups) * pp.kparts * pp.qtiles * 128;
+            w.part_o = off;
+            off = align256(off + rows * d * 4);
+            w.part_ml = off;
+            off = align256(off + rows * 8);
+            w.part_count = off;
+            off = align256(off + static_cast<size_t>(pp.groups) * 4);
+        }
+    }
     w.total = off;
     return w;
 }
@@ -313,8 +373,8 @@ int launch_quant_qk(const fp4attn::QuantJob& q, const fp4attn::QuantJob& k, cons
         const int per_slice = a.ntiles * a.tile_rows * (a.padded_dim / 32);
         return static_cast<int>(std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / slices + 1)));
     };
-    const fp4attn::VConvJob vj = v ? *v : fp4attn::VConvJob{nullptr, nullptr, 0};
-    dim3 grid(std::max(gx_for(q.a), gx_for(k.a)), static_cast<unsigned>(slices), v ? 3 : 2);
+    const fp4attn::VConvJob vj = *v;
+    dim3 grid(std::max(gx_for(q.a), gx_for(k.a)), static_cast<unsigned>(slices), v->src ? 3 : 2);
     switch (q.a.padded_dim / 32) {
         case 2: fp4attn::quantize_tiles_kernel<InT, 2><<<grid, 256, 0, st>>>(q, k, vj); break;
         case 4: fp4attn::quantize_tiles_kernel<InT, 4><<<grid, 256, 0, st>>>(q, k, vj); break;
@@ -400,12 +460,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
 }
 
-template <int D, typename OutT, int kPoly8, bool kSpec>
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false>
 int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
                      int64_t slices, cudaStream_t st)
 {
     using C = fp4attn::PairCfg<D>;
-    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall>;
     static std::atomic<int> launch_regs_cache{-1};
     int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
@@ -433,6 +493,12 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     a.timeout_ns = fa.timeout_ns;
     a.causal = fa.causal;
     a.causal_off = fa.causal_off;
+    a.qtiles = fa.qtiles;
+    a.kparts = fa.kparts;
+    a.nk_part = fa.nk_part;
+    a.part_ml = fa.part_ml;
+    a.part_o = fa.part_o;
+    a.part_count = fa.part_count;
     // Output written by TMA stores in 32-row x 32-column boxes (64-byte rows
     // for FP16, 128-byte rows for FP32, swizzled to match the staging).
     CUtensorMap to;
@@ -441,13 +507,22 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
                          static_cast<int>(sizeof(OutT)), fa.out, D, fa.seq_q, slices, 32, 32,
                          f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
-    // Persistent: one CTA per SM walks the (slice, query-tile pair) items.
-    a.n_pairs = fa.q_sf_tiles / 2;
-    const int64_t items = static_cast<int64_t>(a.n_pairs) * slices;
+    // Key partitions: unnormalised FP32 O of every (item, tile) row, stored
+    // by TMA in 32-row x 32-column boxes (128-byte rows, swizzled).
+    CUtensorMap tp = to;
+    if (fa.kparts > 1) {
+        const uint64_t rows = static_cast<uint64_t>(slices) * fa.n_pairs * fa.kparts * fa.qtiles * 128;
+        if ((rc = make_map_3d(&tp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, fa.part_o, D, rows, 1, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+    }
+    // Persistent: one CTA per SM walks the (slice, query group, key partition) items.
+    a.n_pairs = fa.n_pairs;
+    const int64_t items = static_cast<int64_t>(a.n_pairs) * slices * fa.kparts;
     if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
     a.n_items = static_cast<int>(items);
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, a);
+    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, tp, a);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }
@@ -456,6 +531,8 @@ template <int D, typename OutT>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                 int64_t slices, cudaStream_t st)
 {
+    // One query tile per item or key partitions: the small-problem kernel.
+    if (a.qtiles == 1 || a.kparts > 1) return launch_pair_poly<D, OutT, 3, true, true>(tq, tk, tv, a, slices, st);
     if constexpr (D == 128 && sizeof(OutT) == 2) {
         const bool spec = spec_setting() != 0;
         switch (poly8_setting()) {
@@ -552,12 +629,19 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
     const fp4attn::QuantJob jq{Q, ws + p.w.q_codes, ws + p.w.q_sf, quant_args(p.slices, sq, d, 128, nq_sf, ocp)};
     const fp4attn::QuantJob jk{K, ws + p.w.k_codes, ws + p.w.k_sf, quant_args(p.slices, sk, d, bn, nk_sf, ocp)};
-    if (in_dtype == FP4ATTN_F16) {
-        if ((rc = launch_quant_qk<__half>(jq, jk, nullptr, p.slices, st))) return rc;
+    // The attention kernel's key-partition arrival counters start at zero (it
+    // leaves them at zero when it completes).
+    const int n_zero = static_cast<int>((p.w.part_count == p.w.total ? 0 : p.w.total - p.w.part_count) / 4);
+    uint32_t* zero = reinterpret_cast<uint32_t*>(ws + p.w.part_count);
+    if (in_dtype == FP4ATTN_F16 || !need_v) {
+        const fp4attn::VConvJob jv{nullptr, nullptr, 0, zero, n_zero};
+        if (in_dtype == FP4ATTN_F16) rc = launch_quant_qk<__half>(jq, jk, &jv, p.slices, st);
+        else rc = launch_quant_qk<float>(jq, jk, &jv, p.slices, st);
+        if (rc) return rc;
     } else {
         const fp4attn::VConvJob jv{static_cast<const float4*>(V), reinterpret_cast<uint2*>(ws + p.w.v16),
-                                   static_cast<int64_t>(sk) * d / 4};
-        if ((rc = launch_quant_qk<float>(jq, jk, need_v ? &jv : nullptr, p.slices, st))) return rc;
+                                   static_cast<int64_t>(sk) * d / 4, zero, n_zero};
+        if ((rc = launch_quant_qk<float>(jq, jk, &jv, p.slices, st))) return rc;
     }
     return FP4ATTN_OK;
 }
@@ -610,6 +694,16 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     a.timeout_ns = wait_timeout_ns();
     a.causal = mask_mode == FP4ATTN_MASK_CAUSAL ? 1 : 0;
     a.causal_off = sk - sq;
+    {
+        const PairPlan pp = pair_plan(p.slices, sq, sk, d, a.causal != 0);
+        a.qtiles = pp.qtiles;
+        a.n_pairs = pp.n_pairs;
+        a.kparts = paired(d) ? pp.kparts : 1;
+        a.nk_part = pp.nk_part;
+        a.part_o = reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + p.w.part_o);
+        a.part_ml = reinterpret_cast<float2*>(const_cast<uint8_t*>(ws) + p.w.part_ml);
+        a.part_count = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(ws) + p.w.part_count);
+    }
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
     return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, p.slices, st);
 }

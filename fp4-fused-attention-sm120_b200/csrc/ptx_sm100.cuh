@@ -239,6 +239,13 @@ __device__ __forceinline__ void fence_proxy_async_smem()
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's async-proxy accesses to global memory (completed bulk
+// stores) before its later generic-proxy accesses and fences.
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Arrives on named barrier `id` without waiting (the other side bar.syncs).
 __device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads)
 {

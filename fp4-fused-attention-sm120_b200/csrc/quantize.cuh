@@ -218,11 +218,15 @@ struct QuantJob {
 };
 
 // V in FP32, converted to the FP16 copy the attention kernel reads, per slice
-// (n4 float4 per slice).
+// (n4 float4 per slice); and n_zero words of the workspace the attention
+// kernel needs at zero (its key-partition arrival counters), cleared by the
+// first CTA of the launch.
 struct VConvJob {
     const float4* src;
     uint2* dst;
     int64_t n4;
+    uint32_t* zero;
+    int n_zero;
 };
 
 // Quantise Q (blockIdx.z == 0) and K (blockIdx.z == 1) in one launch into the
@@ -238,6 +242,8 @@ struct VConvJob {
 template <typename InT, int kNB>
 __global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, const QuantJob jk, const VConvJob jv)
 {
+    if (jv.n_zero > 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+        for (int i = threadIdx.x; i < jv.n_zero; i += blockDim.x) jv.zero[i] = 0u;
     if (blockIdx.z == 2) {
         // FP32 -> FP16 (round to nearest even) for this slice of V.
         const float4* src = jv.src + static_cast<int64_t>(blockIdx.y) * jv.n4;

@@ -447,3 +447,56 @@ def test_no_writes_outside_the_scores(fa, cuda):
     S = S.view(H, sq, sk).cpu().numpy()
     for h in range(H):
         assert np.array_equal(S[h], oracle.fp4_scores(Q[0, h].float().cpu().numpy(), K[0, h].float().cpu().numpy()))
+
+
+# ---- small problems: one query tile per item, key partitions ---------------
+# With seq_q <= 128 a work item is one query tile, and with fewer query groups
+# than SMs the keys of each group are split into partitions whose partial
+# results the last-finishing CTA merges.  The arrival counters that pick that
+# CTA are back at zero after every launch, so repeated launches on one
+# prepared workspace give the same bytes.
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128])
+@pytest.mark.parametrize("B,H,sq,sk", [(1, 32, 64, 128), (1, 32, 64, 1024), (1, 2, 1, 4000), (1, 3, 128, 77),
+                                       (1, 2, 300, 1000), (2, 1, 700, 3000)])
+def test_key_partitions(fa, cuda, d, B, H, sq, sk):
+    g = torch.Generator().manual_seed(d * 31 + sq + sk)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half() for s in (sq, sk, sk))
+    for odt in (torch.float32, torch.float16):
+        out = fa.fused_fp4_attention(Q.cuda(), K.cuda(), V.cuda(), out_dtype=odt)
+        assert fa.status_query() == fa.OK
+        want = oracle.fp4_attention(Q.reshape(-1, sq, d).float().numpy(), K.reshape(-1, sk, d).float().numpy(),
+                                    V.reshape(-1, sk, d).float().numpy())
+        if odt == torch.float16:
+            want = want.astype(np.float16).astype(np.float32)
+        assert_close(out.reshape(-1, sq, d).float().cpu().numpy(), want)
+
+
+def test_key_partitions_repeat_on_one_workspace(fa, cuda):
+    """Launch after launch on one prepared workspace: the same bytes."""
+    B, H, sq, sk, d = 1, 4, 64, 2000, 64
+    g = torch.Generator().manual_seed(5)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk, sk))
+    ws = torch.empty(fa.workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+    fa.prepare(Q, K, V, ws)
+    outs = []
+    for _ in range(3):
+        out = torch.empty(B, H, sq, d, dtype=torch.float32, device="cuda")
+        fa.attend(V, out, ws, fa.F16, B, H, sq, sk, d)
+        outs.append(out)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    want = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy())
+    assert_close(outs[0][0].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("sq", [1, 64, 128])
+def test_single_tile_items_many_slices(fa, cuda, sq):
+    """seq_q <= 128 with more slices than SMs: one query tile per item and
+    several items per persistent CTA, no key partitions."""
+    g = torch.Generator().manual_seed(sq)
+    Q, K, V = (torch.randn(1, 400, s, 128, generator=g).half() for s in (sq, 300, 300))
+    out = fa.fused_fp4_attention(Q.cuda(), K.cuda(), V.cuda(), out_dtype=torch.float32)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention(Q[0].float().numpy(), K[0].float().numpy(), V[0].float().numpy())
+    assert_close(out[0].cpu().numpy(), want)
