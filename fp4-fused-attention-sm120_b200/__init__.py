@@ -18,7 +18,7 @@ import pathlib
 __all__ = [
     "BLOCK_ELEMENT", "BQ", "Fp4AttnError", "lib", "lib_path", "quantize", "workspace_size",
     "fused_fp4_attention", "fused_fp4_attention_into", "debug_scores", "status_query",
-    "selftest_timeout", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
+    "selftest_timeout", "selftest_abort", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
     "F32", "F16", "MASK_NONE", "MASK_CAUSAL",
 ]
 
@@ -80,6 +80,8 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_status_query.restype = i32
     L.fp4attn_selftest_timeout.argtypes = [ctypes.c_uint, vp]
     L.fp4attn_selftest_timeout.restype = i32
+    L.fp4attn_selftest_abort.argtypes = [vp, vp, i32, i32, i32, i32, vp, sz, ctypes.c_uint, vp]
+    L.fp4attn_selftest_abort.restype = i32
     L.fp4attn_selftest_exp2.argtypes = [vp, vp, i64, vp]
     L.fp4attn_selftest_exp2.restype = i32
     L.fp4attn_error_string.argtypes = [i32]
@@ -267,6 +269,16 @@ def selftest_exp2(x, stream=None):
 def status_query(stream=None) -> int:
     """Synchronise `stream` and return (and clear) the device error word."""
     return int(lib().fp4attn_status_query(_stream_ptr(stream)))
+
+
+def selftest_abort(V, out, workspace, batch, heads, seq_q, seq_k, timeout_us: int = 20000, stream=None) -> int:
+    """Run the attention kernel's abort self-test (fp4attn_selftest_abort) on a
+    workspace prepared for this head_dim-64 FP16 problem; returns
+    status_query() (FP4ATTN_ETIMEOUT when the failure path ran)."""
+    _check(lib().fp4attn_selftest_abort(V.data_ptr(), out.data_ptr(), batch, heads, seq_q, seq_k,
+                                        workspace.data_ptr(), workspace.numel(), timeout_us, _stream_ptr(stream)),
+           "fp4attn_selftest_abort")
+    return status_query(stream)
 
 
 def selftest_timeout(timeout_us: int = 2000, stream=None) -> int:

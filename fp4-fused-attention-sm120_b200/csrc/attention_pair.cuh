@@ -189,7 +189,11 @@ __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
     return it;
 }
 
-template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false>
+// kWithhold (test instantiation only): the first softmax thread never makes
+// its first s_free arrival, so the S issuer's bounded wait for step 1 runs out
+// and the kernel's own abort path runs: every role leaves its loop, in-flight
+// copies and MMAs drain, TMEM is freed and FP4ATTN_ETIMEOUT is recorded.
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -677,7 +681,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 ptx::tc_wait_ld();
                 // S_t is in registers: the issuer may compute the next step into it.
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(&s_free[t]);
+                if (!kWithhold || threadIdx.x != 128 || g != 0) ptx::mbar_arrive(&s_free[t]);
                 const int valid = row_lim - (kSmall ? item.k0 + j : j) * BN;  // keys of this step this row sees
                 uint32_t pk[NT][16];
                 // P = 2^(S * c - mref) as FP16 pairs; kPoly8 of every 8 column

@@ -460,12 +460,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
 }
 
-template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false>
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false>
 int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
                      int64_t slices, cudaStream_t st)
 {
     using C = fp4attn::PairCfg<D>;
-    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall, kWithhold>;
     static std::atomic<int> launch_regs_cache{-1};
     int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
@@ -646,9 +646,12 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     return FP4ATTN_OK;
 }
 
+// test_timeout_ns > 0: the abort self-test (fp4attn_selftest_abort) -- the
+// head_dim 64, FP32-output pair kernel with one withheld arrival, waits
+// bounded by test_timeout_ns.
 int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int sq, int sk, int d,
               float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores,
-              int mask_mode = FP4ATTN_MASK_NONE)
+              int mask_mode = FP4ATTN_MASK_NONE, unsigned long long test_timeout_ns = 0)
 {
     if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
         return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
@@ -705,6 +708,13 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
         a.part_count = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(ws) + p.w.part_count);
     }
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
+    if (test_timeout_ns) {
+        if (d != 64 || out_dtype != FP4ATTN_F32 || a.qtiles != 2 || a.kparts != 1 || a.causal)
+            return fail(FP4ATTN_EINVAL, "the abort self-test runs head_dim 64, FP32 output, seq_q > 128, no key "
+                                        "partitions, no mask");
+        a.timeout_ns = test_timeout_ns;
+        return launch_pair_poly<64, float, 3, true, false, true>(tq, tk, tv, a, p.slices, st);
+    }
     return dispatch_dim<false>(d, out_dtype, tq, tk, tv, a, p.slices, st);
 }
 
@@ -846,6 +856,15 @@ int fp4attn_selftest_timeout(unsigned timeout_us, void* stream)
         static_cast<unsigned long long>(timeout_us) * 1000ull);
     FP4_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
+}
+
+int fp4attn_selftest_abort(const void* V, void* Out, int batch, int heads, int seq_q, int seq_k,
+                           const void* workspace, size_t workspace_bytes, unsigned timeout_us, void* stream)
+{
+    g_last_error.clear();
+    if (timeout_us < 1 || timeout_us > 10000000u) return fail(FP4ATTN_EINVAL, "timeout_us in [1, 1e7]");
+    return do_attend(V, Out, FP4ATTN_F16, FP4ATTN_F32, batch, heads, seq_q, seq_k, 64, 0.f, workspace,
+                     workspace_bytes, stream, false, FP4ATTN_MASK_NONE, static_cast<unsigned long long>(timeout_us) * 1000ull);
 }
 
 int fp4attn_selftest_exp2(const float* x, float* y, int64_t n, void* stream)

@@ -181,6 +181,18 @@ int fp4attn_status_query(void* stream);
  * out and sets the error word.  No fault, trap or hang is involved. */
 int fp4attn_selftest_timeout(unsigned timeout_us, void* stream);
 
+/* Test hook for the attention kernel's own failure path: runs the
+ * head_dim-64, FP32-output attention kernel (seq_q > 128, a problem without
+ * key partitions) over a workspace filled by fp4attn_prepare (FP16 input), in
+ * a build in which one softmax thread never makes its first "S copied"
+ * arrival.  The kernel's bounded wait for it expires after timeout_us; every
+ * role then leaves its loop, drains its in-flight copies and MMAs, frees its
+ * tensor memory and returns, and fp4attn_status_query reports
+ * FP4ATTN_ETIMEOUT.  No fault, trap or hang is involved; later calls on the
+ * same context run normally.  No counterpart in the reference. */
+int fp4attn_selftest_abort(const void* V, void* Out, int batch, int heads, int seq_q, int seq_k,
+                           const void* workspace, size_t workspace_bytes, unsigned timeout_us, void* stream);
+
 /* Test hook: y[i] = 2^x[i] computed by the FMA-pipe polynomial the softmax
  * uses for part of its exponentials (n even, 16-byte aligned device arrays).
  * No counterpart in the reference, whose softmax calls expf (common.h:236). */

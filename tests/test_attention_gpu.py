@@ -147,6 +147,39 @@ def test_timeout_path_reports_and_recovers(fa, cuda):
     assert_close(run_fwd(fa, Q, K, V), oracle.fp4_attention(Q, K, V))
 
 
+def test_attention_kernel_abort_path_drains_and_recovers(fa, cuda):
+    """The attention kernel's own failure path, made to run without a fault: a
+    test build in which one softmax thread withholds its first "S copied"
+    arrival, so the S issuer's bounded wait for the next step expires.  Every
+    role must leave its loop, drain its in-flight TMA loads and MMAs, free its
+    tensor memory and return: the call reports FP4ATTN_ETIMEOUT, and the
+    normal kernel then runs on the same context and workspace and matches
+    the oracle."""
+    B, H, sq, sk, d = 1, 2, 256, 256, 64
+    g = torch.Generator().manual_seed(21)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk, sk))
+    ws = torch.empty(fa.workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+    out = torch.zeros(B, H, sq, d, dtype=torch.float32, device="cuda")
+    fa.prepare(Q, K, V, ws)
+    assert fa.status_query() == fa.OK
+    assert fa.selftest_abort(V, out, ws, B, H, sq, sk, timeout_us=20000) == fa.ETIMEOUT
+    assert b"device wait expired" in fa.lib().fp4attn_last_error()
+    assert fa.status_query() == fa.OK  # the query cleared the word
+    fa.attend(V, out, ws, fa.F16, B, H, sq, sk, d)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy())
+    assert_close(out[0].cpu().numpy(), want)
+
+
+def test_abort_self_test_rejects_other_shapes(fa, cuda):
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    V = torch.zeros(1, 1, 256, 128, dtype=torch.float16, device="cuda")
+    out = torch.zeros(1, 1, 256, 128, dtype=torch.float32, device="cuda")
+    rc = fa.lib().fp4attn_selftest_abort(V.data_ptr(), out.data_ptr(), 1, 1, 64, 256, ws.data_ptr(), ws.numel(),
+                                         1000, torch.cuda.current_stream().cuda_stream)
+    assert rc == fa.EINVAL  # seq_q <= 128 runs the small-problem kernel, not the test build
+
+
 def test_misaligned_pointer_rejected(fa, cuda):
     x = torch.zeros(1, 1, 65, 128, dtype=torch.float16, device="cuda")
     bad = x.view(-1)[1:1 + 64 * 128].view(1, 1, 64, 128)
