@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_prepare.restype = i32
     L.fp4attn_attend.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, vp, sz, vp]
     L.fp4attn_attend.restype = i32
+    L.fp4attn_forward_fused_q.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, vp, sz, vp]
+    L.fp4attn_forward_fused_q.restype = i32
     L.fp4attn_forward_masked.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, i32, vp, sz, vp]
     L.fp4attn_forward_masked.restype = i32
     L.fp4attn_attend_masked.argtypes = [vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, vp, sz, vp]
@@ -178,10 +180,14 @@ def _check_qkv(Q, K, V):
 
 
 def fused_fp4_attention_into(Q, K, V, out, workspace, softmax_scale=None, scale_mode="reference", stream=None,
-                             causal=False):
+                             causal=False, fuse_q=False):
     """Launch into caller-provided `out` and `workspace` (uint8 CUDA tensor of
     at least workspace_size(...) bytes); no allocation, async on `stream`.
-    causal=True applies the bottom-right causal mask (fp4attn_forward_masked)."""
+    causal=True applies the bottom-right causal mask (fp4attn_forward_masked);
+    fuse_q=True quantises Q inside the attention kernel
+    (fp4attn_forward_fused_q, same result)."""
+    if causal and fuse_q:
+        raise ValueError("fuse_q has no causal variant")
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
     if out.shape != Q.shape or not out.is_contiguous():
         raise ValueError("out must be contiguous with Q's shape")
@@ -190,6 +196,8 @@ def fused_fp4_attention_into(Q, K, V, out, workspace, softmax_scale=None, scale_
     tail = (workspace.data_ptr(), workspace.numel(), _stream_ptr(stream))
     if causal:
         _check(lib().fp4attn_forward_masked(*args, MASK_CAUSAL, *tail), "fp4attn_forward_masked")
+    elif fuse_q:
+        _check(lib().fp4attn_forward_fused_q(*args, *tail), "fp4attn_forward_fused_q")
     else:
         _check(lib().fp4attn_forward(*args, *tail), "fp4attn_forward")
     return out
@@ -230,7 +238,7 @@ def shard_range(n_slices: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode="reference", stream=None,
-                        causal=False):
+                        causal=False, fuse_q=False):
     """softmax(Q K^T * scale) V with FP4 (E2M1 + UE8M0/32) Q and K: the
     reference kernel fused_fp4_attention<HEAD_DIM> (common.h:68-328) for
     [batch, heads, seq, head_dim] tensors of any seq_q / seq_k.  causal=True
@@ -239,7 +247,7 @@ def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode=
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
     out = torch.empty((B, H, Sq, D), dtype=out_dtype or Q.dtype, device=Q.device)
     ws = torch.empty(workspace_size(B, H, Sq, Sk, D, _dtype_code(Q)), dtype=torch.uint8, device=Q.device)
-    return fused_fp4_attention_into(Q, K, V, out, ws, softmax_scale, scale_mode, stream, causal)
+    return fused_fp4_attention_into(Q, K, V, out, ws, softmax_scale, scale_mode, stream, causal, fuse_q)
 
 
 def debug_scores(Q, K, scale_mode="reference", stream=None):

@@ -132,6 +132,9 @@ struct FwdArgs {
     float2* part_ml;
     float* part_o;
     unsigned* part_count;
+    // In-kernel Q quantisation (fp4attn_forward_fused_q): FP16 Q and the scale rule.
+    const void* q_in;
+    int ocp_mode;
 };
 
 // Work item r of this CTA's static schedule for the one-tile kernel: (slice,

@@ -57,13 +57,16 @@
 #include <type_traits>
 
 #include "attention.cuh"
+#include "quantize.cuh"
 
 namespace fp4attn {
 
 // Most key partitions per query group (the planner caps kparts at this).
 constexpr int kMaxKParts = 16;
 
-template <int D>
+// QB: Q buffers (2 tiles each).  The kernel that quantises Q itself
+// (kFuseQ) writes item i+1's Q into one buffer while item i reads the other.
+template <int D, int QB = 1>
 struct PairCfg {
     static constexpr int BM = 128;                          // rows per query tile (MMA M)
     static constexpr int BN = 64;                           // keys per step
@@ -95,8 +98,8 @@ struct PairCfg {
     static constexpr int SF_BYTES = 512;                    // one scale atom (Q: 128 rows x 4, K: 64 rows x 8)
     static constexpr int V_BYTES = VCH * BN * VCW;          // loaded by TMA; the ones chunk follows
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_QSF = align1k(OFF_Q + 2 * Q_BYTES);
-    static constexpr int OFF_K = align1k(OFF_QSF + 2 * SF_BYTES);
+    static constexpr int OFF_QSF = align1k(OFF_Q + QB * 2 * Q_BYTES);
+    static constexpr int OFF_K = align1k(OFF_QSF + QB * 2 * SF_BYTES);
     static constexpr int K_STRIDE = align1k(K_BYTES);
     static constexpr int OFF_KSF = OFF_K + KST * K_STRIDE;
     static constexpr int OFF_V = align1k(OFF_KSF + KST * SF_BYTES);
@@ -107,8 +110,8 @@ struct PairCfg {
     static constexpr int OFF_OST = OFF_V + VST * V_STRIDE;
     static constexpr int OFF_BAR = OFF_OST + 8 * 2 * OST_BYTES;
     // q_full, q_empty, K ring, V ring, s_full[2], s_free[2], p_full[2], pv_done[2], drain,
-    // part_done, merge_go
-    static constexpr int NUM_BARS = 2 + 2 * KST + 2 * VST + 8 + 1 + 2;
+    // part_done, merge_go, q_full / q_empty of the second Q buffer, q_first
+    static constexpr int NUM_BARS = 2 + 2 * KST + 2 * VST + 8 + 1 + 2 + 3;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;  // +1024 for base alignment
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -136,6 +139,10 @@ struct PairArgs {
     float2* part_ml;           // [n_items][qtiles][128]
     const float* part_o;       // [n_items][qtiles][128][D]
     unsigned* part_count;      // [slices * n_pairs]
+    // kFuseQ: FP16 Q [slices][seq_q][D], quantised by the kernel itself, and
+    // the scale rule (1: the OCP "/6" rule).
+    const __half* q_in;
+    int ocp_mode;
 };
 
 // Work item r of this CTA's static schedule: (slice, query-tile pair) and its
@@ -193,13 +200,22 @@ __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
 // its first s_free arrival, so the S issuer's bounded wait for step 1 runs out
 // and the kernel's own abort path runs: every role leaves its loop, in-flight
 // copies and MMAs drain, TMEM is freed and FP4ATTN_ETIMEOUT is recorded.
-template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false>
+// kFuseQ: Q is quantised inside the kernel (fp4attn_forward_fused_q), the
+// quantiser of the reference kernel (common.h:108-124) moved into this one:
+// each CTA's first item is TMA-loaded from the pre-pass as usual (the pre-pass
+// quantises just those rows), and the otherwise idle warp 3 quantises every
+// later item into the other Q buffer while the current item runs.  The codes and scales are the pre-pass's, bit
+// for bit (the same encoder, quantize.cuh), written in the TMA's swizzled
+// layout.  Only the large-problem schedule (kSmall false) has this variant.
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false,
+          bool kFuseQ = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                               const __grid_constant__ CUtensorMap tm_p, const PairArgs args)
 {
-    using C = PairCfg<D>;
+    static_assert(!(kFuseQ && kSmall), "in-kernel Q quantisation runs the large-problem schedule only");
+    using C = PairCfg<D, kFuseQ ? 2 : 1>;
     constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -222,6 +238,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     uint64_t* drain_bar = pv_done + 2;
     uint64_t* part_done = drain_bar + 1;  // kSmall: this item's partials are written (one arrive per softmax warp)
     uint64_t* merge_go = part_done + 1;   // kSmall: the group's arrival count is known (merge_sh)
+    // kFuseQ: Q buffer b's barriers (buffer 0 uses q_full / q_empty): qf(b)
+    // completes when warp 3 has quantised an item into buffer b, qe(b) when
+    // the S MMAs of buffer b's item are done (tcgen05.commit); q_first when the
+    // CTA's first item's Q (pre-pass codes) has landed by TMA in buffer 0.
+    auto qf = [&](int b) { return b ? merge_go + 1 : q_full; };
+    auto qe = [&](int b) { return b ? merge_go + 2 : q_empty; };
+    uint64_t* q_first = merge_go + 3;
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
@@ -250,6 +273,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if constexpr (kSmall) {
             ptx::mbar_init(part_done, 4 * args.qtiles);
             ptx::mbar_init(merge_go, 1);
+        }
+        if constexpr (kFuseQ) {
+            ptx::mbar_init(qf(1), 1);
+            ptx::mbar_init(qe(1), 1);
+            ptx::mbar_init(q_first, 1);
         }
         abort_sh = 0;
         ptx::fence_mbar_init();
@@ -286,6 +314,50 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
     const WaitCtx wctx{&abort_sh, args.timeout_ns};
+    // kFuseQ: quantise the 256 query rows of `item` into Q buffer qb -- units
+    // of one 32-element block, unit u = tid, tid + nthr, ... (consecutive
+    // threads take consecutive blocks of a row: coalesced 64-byte reads), the
+    // next unit's loads in flight while this one is encoded.  Codes go to the
+    // swizzled Q tile exactly as the TMA would have placed the pre-pass's
+    // codes, scales to the tile's scale atom; rows past seq_q and blocks past
+    // head_dim get zero codes and scale 127, as in the pre-pass.
+    auto quantize_q = [&](const PairItem& item, int qb, int tid, int nthr) {
+        constexpr int NB = C::DP / 32, NBR = D / 32;
+        uint8_t* qbuf = sQ + qb * 2 * C::Q_BYTES;
+        uint8_t* sfbuf = sQsf + qb * 2 * C::SF_BYTES;
+        const __half* qsl = args.q_in + static_cast<size_t>(item.slice) * args.seq_q * D;
+        const int row_base = item.pair * 2 * C::BM;
+        constexpr int kUnits = 2 * C::BM * NB;
+        auto load = [&](int u, uint4 (&raw)[4]) {
+            const int r = u / NB, b = u % NB, grow = row_base + r;
+            const bool has = b < NBR && grow < args.seq_q;
+            if (has) load_raw32(qsl + static_cast<size_t>(grow) * D + b * 32, raw);
+            return has;
+        };
+        uint4 nxt[4];
+        bool nxt_has = tid < kUnits && load(tid, nxt);
+        for (int u = tid; u < kUnits; u += nthr) {
+            uint4 cur[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) cur[k] = nxt[k];
+            const bool has = nxt_has;
+            nxt_has = u + nthr < kUnits && load(u + nthr, nxt);
+            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+            uint32_t sb = 127u;
+            if (has) {
+                float v[32];
+                raw32_to_float(cur, v);
+                sb = encode32<__half>(v, args.ocp_mode, packed);
+                if (sb == 255u) sb = 254u;  // as the pre-pass stores it (255 is NaN in E8M0)
+            }
+            const int r = u / NB, b = u % NB, t = r / C::BM, rr = r % C::BM;
+            // 16-byte unit b of a QK_ROW-byte row under the TMA's 64- or 32-byte swizzle.
+            const int pu = C::QK_ROW == 64 ? (b ^ ((rr >> 1) & 3)) : (b ^ ((rr >> 2) & 1));
+            *reinterpret_cast<uint4*>(qbuf + t * C::Q_BYTES + rr * C::QK_ROW + pu * 16) = packed;
+            sfbuf[t * C::SF_BYTES + sf_tile_offset(128, rr, b)] = static_cast<uint8_t>(sb);
+        }
+        ptx::fence_proxy_async_smem();  // visible to the tensor cores' reads
+    };
 
     if (warp < 4) {
         ptx::setmaxnreg_dec<kCtlRegs>();
@@ -301,26 +373,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const PairItem item = pair_item<kSmall>(args, r);
                     if (!item.valid) continue;
                     const int slice = item.slice, pair = item.pair, nk = item.nk;
-                    if (it > 0 && !wait_phase(q_empty, (it - 1) & 1, wctx, kSiteQEmpty)) break;
-                    if constexpr (kSmall) {
+                    uint64_t* qload = kFuseQ ? q_first : q_full;  // (kFuseQ: the first item only)
+                    if (kFuseQ && it > 0) {
+                        // Q of later items is quantised in the kernel (warp 3).
+                    } else if (it > 0 && !wait_phase(q_empty, (it - 1) & 1, wctx, kSiteQEmpty)) {
+                        break;
+                    } else if constexpr (kSmall) {
                         const int qt = args.qtiles;
-                        ptx::mbar_arrive_expect_tx(q_full, qt * (C::Q_BYTES + C::SF_BYTES));
+                        ptx::mbar_arrive_expect_tx(qload, qt * (C::Q_BYTES + C::SF_BYTES));
                         for (int t = 0; t < qt; t++) {
-                            ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, (pair * qt + t) * C::BM, slice);
+                            ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, qload, 0, (pair * qt + t) * C::BM, slice);
                             ptx::bulk_load(sQsf + t * C::SF_BYTES,
                                            args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + qt * pair + t) *
                                                            C::SF_BYTES,
-                                           C::SF_BYTES, q_full);
+                                           C::SF_BYTES, qload);
                         }
                     } else {
-                    ptx::mbar_arrive_expect_tx(q_full, 2 * (C::Q_BYTES + C::SF_BYTES));
+                    ptx::mbar_arrive_expect_tx(qload, 2 * (C::Q_BYTES + C::SF_BYTES));
 #pragma unroll
                     for (int t = 0; t < 2; t++) {
-                        ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, q_full, 0, pair * 2 * C::BM + t * C::BM, slice);
+                        ptx::tma_load_3d(sQ + t * C::Q_BYTES, &tm_q, qload, 0, pair * 2 * C::BM + t * C::BM, slice);
                         ptx::bulk_load(sQsf + t * C::SF_BYTES,
                                        args.q_sf + (static_cast<size_t>(slice) * args.q_sf_tiles + 2 * pair + t) *
                                                        C::SF_BYTES,
-                                       C::SF_BYTES, q_full);
+                                       C::SF_BYTES, qload);
                     }
                     }
                     for (int jl = 0; jl < nk; jl++, kv++) {
@@ -353,7 +429,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // Every load this thread issued must land before the CTA exits
                 // (Q loads are at most one phase ahead of their consumer).
                 const unsigned long long drain_ns = 2ull * args.timeout_ns;
-                if (it > 0) drain_phase(q_full, (it - 1) & 1, drain_ns);
+                if (it > 0) drain_phase(kFuseQ ? q_first : q_full, kFuseQ ? 0 : (it - 1) & 1, drain_ns);
                 for (int i = k_issued - C::KST < 0 ? 0 : k_issued - C::KST; i < k_issued; i++)
                     drain_phase(&k_full[i % C::KST], (i / C::KST) & 1, drain_ns);
                 for (int i = v_issued - C::VST < 0 ? 0 : v_issued - C::VST; i < v_issued; i++)
@@ -375,7 +451,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                     const PairItem item = pair_item<kSmall>(args, r);
                     if (!item.valid) continue;
                     const int nk = item.nk;
-                    if (!wait_phase(q_full, it & 1, wctx, kSiteQFull)) break;
+                    // kFuseQ: item it reads Q buffer it & 1; item 0 comes by TMA
+                    // (q_first), and item it > 0 is warp 3's ci-th item in that
+                    // buffer (buffer 0 holds items 2, 4, ..., buffer 1 items 1, 3, ...).
+                    const int qb = kFuseQ ? (it & 1) : 0;
+                    const int ci = (it >> 1) - (qb == 0 ? 1 : 0);
+                    uint64_t* qwait = !kFuseQ ? q_full : it == 0 ? q_first : qf(qb);
+                    if (!wait_phase(qwait, !kFuseQ ? it & 1 : it == 0 ? 0 : ci & 1, wctx, kSiteQFull)) break;
                     ptx::tc_fence_after();
                     // The previous item's S MMAs are complete: the producer
                     // loaded this Q only after their q_empty commit arrived.
@@ -384,7 +466,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
                     for (int t = 0; t < 2; t++)
                         if (t < qt)
-                            ptx::tc_cp_32x128b_warpx4(sfa + 4 * t, sfdesc0 + static_cast<uint64_t>((t * C::SF_BYTES) >> 4));
+                            ptx::tc_cp_32x128b_warpx4(sfa + 4 * t, sfdesc0 + static_cast<uint64_t>(((qb * 2 + t) * C::SF_BYTES) >> 4));
                     for (int j = 0; ok && j < nk; j++, kv++, g++) {
                         const int ks = kv % C::KST;
                         if (!wait_phase(&k_full[ks], (kv / C::KST) & 1, wctx, kSiteKFull)) { ok = false; break; }
@@ -404,7 +486,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                             for (int kk = 0; kk < C::KSTEPS; kk++) {
                                 const uint32_t sf_id = 2u * (kk & 1);
                                 ptx::mma_mxf4(tmem + C::S_COL + t * BN,
-                                              qdesc0 + static_cast<uint64_t>((t * C::Q_BYTES + kk * 32) >> 4),
+                                              qdesc0 + static_cast<uint64_t>(((qb * 2 + t) * C::Q_BYTES + kk * 32) >> 4),
                                               kdesc + static_cast<uint64_t>((kk * 32) >> 4),
                                               ptx::idesc_mxf4(128, BN, sf_id, sf_id), (sfa + 4 * t) | (sf_id << 30),
                                               sfb | (sf_id << 30), kk > 0 ? 1u : 0u);
@@ -415,7 +497,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         ptx::tc_commit(&k_empty[ks]);
                     }
                     if (!ok) break;
-                    ptx::tc_commit(q_empty);  // the producer may load the next item's Q
+                    ptx::tc_commit(kFuseQ ? qe(qb) : q_empty);  // the next Q may be written into this buffer
                     it++;
                 }
                 // Drain every tcgen05 op this thread issued before TMEM is freed.
@@ -460,6 +542,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
             }
             __syncwarp();
+        } else if constexpr (kFuseQ) {
+            // -------------------------------------------------------- warp 3: Q quantiser
+            // Items after the CTA's first, each into the Q buffer its S MMAs
+            // will read, once the item two back is done with that buffer.
+            int it = 0;
+            for (int r = 0; r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                const PairItem item = pair_item<kSmall>(args, r);
+                if (!item.valid) continue;
+                if (it > 0) {
+                    const int qb = it & 1;
+                    if (it >= 2 && !__all_sync(0xffffffffu, wait_phase(qe(qb), ((it >> 1) - 1) & 1, wctx, kSiteQEmpty)))
+                        break;
+                    quantize_q(item, qb, lane, 32);
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(qf(qb));
+                }
+                it++;
+            }
         }
     } else {
         ptx::setmaxnreg_inc<kSmRegs>();

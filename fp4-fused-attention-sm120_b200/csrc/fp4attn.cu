@@ -460,12 +460,13 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     return launch_fwd_poly<D, BN, OutT, kScores, 3>(tq, tk, tv, a, slices, st);
 }
 
-template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false>
+template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false,
+          bool kFuseQ = false>
 int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
                      int64_t slices, cudaStream_t st)
 {
-    using C = fp4attn::PairCfg<D>;
-    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall, kWithhold>;
+    using C = fp4attn::PairCfg<D, kFuseQ ? 2 : 1>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall, kWithhold, kFuseQ>;
     static std::atomic<int> launch_regs_cache{-1};
     int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
@@ -499,6 +500,8 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     a.part_ml = fa.part_ml;
     a.part_o = fa.part_o;
     a.part_count = fa.part_count;
+    a.q_in = static_cast<const __half*>(fa.q_in);
+    a.ocp_mode = fa.ocp_mode;
     // Output written by TMA stores in 32-row x 32-column boxes (64-byte rows
     // for FP16, 128-byte rows for FP32, swizzled to match the staging).
     CUtensorMap to;
@@ -531,6 +534,8 @@ template <int D, typename OutT>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                 int64_t slices, cudaStream_t st)
 {
+    // Q quantised inside the attention kernel (the large-problem schedule).
+    if (a.q_in) return launch_pair_poly<D, OutT, 3, true, false, false, true>(tq, tk, tv, a, slices, st);
     // One query tile per item or key partitions: the small-problem kernel.
     if (a.qtiles == 1 || a.kparts > 1) return launch_pair_poly<D, OutT, 3, true, true>(tq, tk, tv, a, slices, st);
     if constexpr (D == 128 && sizeof(OutT) == 2) {
@@ -613,8 +618,10 @@ int check_workspace(const Problem& p, const void* workspace, size_t ws_bytes)
     return FP4ATTN_OK;
 }
 
+// q_slices >= 0: quantise Q of the first q_slices slices only (the rest is
+// quantised by the attention kernel itself, fp4attn_forward_fused_q).
 int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int batch, int heads, int sq, int sk, int d,
-               int scale_mode, void* workspace, size_t ws_bytes, void* stream, bool need_v)
+               int scale_mode, void* workspace, size_t ws_bytes, void* stream, bool need_v, int64_t q_slices = -1)
 {
     int rc = check_problem(Q, K, V, Q, in_dtype, FP4ATTN_F32, batch, heads, sq, sk, d, scale_mode, need_v);
     if (rc) return rc;
@@ -627,7 +634,9 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
     const int bn = block_n_for(d);
     const int nq_sf = q_sf_tiles(sq, d), nk_sf = (sk + bn - 1) / bn;
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
-    const fp4attn::QuantJob jq{Q, ws + p.w.q_codes, ws + p.w.q_sf, quant_args(p.slices, sq, d, 128, nq_sf, ocp)};
+    const fp4attn::QuantJob jq{Q, ws + p.w.q_codes, ws + p.w.q_sf,
+                               quant_args(q_slices >= 0 ? std::min(q_slices, p.slices) : p.slices, sq, d, 128, nq_sf,
+                                          ocp)};
     const fp4attn::QuantJob jk{K, ws + p.w.k_codes, ws + p.w.k_sf, quant_args(p.slices, sk, d, bn, nk_sf, ocp)};
     // The attention kernel's key-partition arrival counters start at zero (it
     // leaves them at zero when it completes).
@@ -651,7 +660,8 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
 // bounded by test_timeout_ns.
 int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int sq, int sk, int d,
               float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores,
-              int mask_mode = FP4ATTN_MASK_NONE, unsigned long long test_timeout_ns = 0)
+              int mask_mode = FP4ATTN_MASK_NONE, unsigned long long test_timeout_ns = 0, const void* q_in = nullptr,
+              int ocp_mode = 0)
 {
     if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
         return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
@@ -707,6 +717,8 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
         a.part_ml = reinterpret_cast<float2*>(const_cast<uint8_t*>(ws) + p.w.part_ml);
         a.part_count = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(ws) + p.w.part_count);
     }
+    a.q_in = q_in;
+    a.ocp_mode = ocp_mode;
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
     if (test_timeout_ns) {
         if (d != 64 || out_dtype != FP4ATTN_F32 || a.qtiles != 2 || a.kparts != 1 || a.causal)
@@ -791,6 +803,36 @@ int fp4attn_forward(const void* Q, const void* K, const void* V, void* Out, int 
         return rc;
     return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
                      workspace_bytes, stream, false);
+}
+
+int fp4attn_forward_fused_q(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                            int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                            int scale_mode, void* workspace, size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, true);
+    if (rc) return rc;
+    const PairPlan pp = pair_plan(static_cast<int64_t>(batch) * heads, seq_q, seq_k, head_dim, false);
+    // Warp 3 quantises one item's 256 query rows while the item before it
+    // runs; with fewer than kFusedQMinKeyTiles 64-key steps per item it would
+    // hold the kernel up, so shorter key ranges keep the pre-pass.
+    constexpr int kFusedQMinKeyTiles = 48;
+    if (in_dtype != FP4ATTN_F16 || !paired(head_dim) || pp.qtiles != 2 || pp.kparts != 1 ||
+        (seq_k + 63) / 64 < kFusedQMinKeyTiles)
+        // Outside the in-kernel quantiser's scope: the two-launch path (same result).
+        return fp4attn_forward(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale,
+                               scale_mode, workspace, workspace_bytes, stream);
+    // The pre-pass quantises the Q rows of each CTA's first work item (items
+    // 0 .. grid-1 of the persistent schedule, the leading slices); the kernel
+    // quantises every later item's Q while the item before it runs.
+    if ((rc = device_ready())) return rc;
+    const int64_t grid = std::min<int64_t>(pp.groups, device_sms());
+    const int64_t q_slices = (grid + pp.n_pairs - 1) / pp.n_pairs;
+    if ((rc = do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
+                         workspace_bytes, stream, true, q_slices)))
+        return rc;
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false, FP4ATTN_MASK_NONE, 0, Q, scale_mode == FP4ATTN_SCALE_OCP);
 }
 
 int fp4attn_attend_masked(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q,

@@ -19,10 +19,12 @@
 // Every call on a device uses the same scratch.  Calls that can overlap on the
 // GPU (different streams, no ordering between them) race on it; serialise them
 // (one stream, or events).  The scratch keeps whatever the previous call left
-// in it; nothing needs to start at zero, because each call's quantiser writes
-// every byte of the workspace that the attention kernel later reads (codes of
-// every real row, scale tiles of every row including padding rows, and the
-// FP16 copy of V for FP32 input).
+// in it.  The only words that must start at zero -- the arrival counters of
+// the key partitions small problems are split into -- are cleared by each
+// call's quantiser launch; every other byte the attention kernel reads is
+// written by that same call first (codes of every real row, scale tiles of
+// every row including padding rows, the FP16 copy of V for FP32 input, and
+// the partitions' partial results).
 #include <cuda_runtime.h>
 
 #include <cstdio>

@@ -108,17 +108,11 @@ __device__ __forceinline__ void load8<float>(const float* src, float (&v)[8])
 //    sum) takes the exact encoder.
 //  * FP32 input: a block with a possible tie (21 low mantissa bits zero),
 //    -0.0 or NaN is redone with the exact encoder.
+// The encoding of one block held in registers (InT: the type it was read as,
+// which selects the tie handling below); returns the scale byte.
 template <typename InT>
-__device__ __forceinline__ uint32_t quantize32(const InT* __restrict__ src, int ocp_mode, uint4& packed)
+__device__ __forceinline__ uint32_t encode32(const float (&v)[32], int ocp_mode, uint4& packed)
 {
-    float v[32];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        float t[8];
-        load8<InT>(src + 8 * k, t);
-#pragma unroll
-        for (int i = 0; i < 8; i++) v[8 * k + i] = t[i];
-    }
     float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; i += 8) {
@@ -184,6 +178,42 @@ __device__ __forceinline__ uint32_t quantize32(const InT* __restrict__ src, int 
     return sb;
 }
 
+template <typename InT>
+__device__ __forceinline__ uint32_t quantize32(const InT* __restrict__ src, int ocp_mode, uint4& packed)
+{
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float t[8];
+        load8<InT>(src + 8 * k, t);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[8 * k + i] = t[i];
+    }
+    return encode32<InT>(v, ocp_mode, packed);
+}
+
+// One FP16 block as raw 16-byte words (so a caller can have the next block's
+// loads in flight while it encodes this one), and its conversion to floats.
+__device__ __forceinline__ void load_raw32(const __half* __restrict__ src, uint4 (&u)[4])
+{
+#pragma unroll
+    for (int k = 0; k < 4; k++) u[k] = __ldg(reinterpret_cast<const uint4*>(src) + k);
+}
+
+__device__ __forceinline__ void raw32_to_float(const uint4 (&u)[4], float (&v)[32])
+{
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const __half2* h = reinterpret_cast<const __half2*>(&u[k]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = __half22float2(h[i]);
+            v[8 * k + 2 * i] = f.x;
+            v[8 * k + 2 * i + 1] = f.y;
+        }
+    }
+}
+
 // Byte offset of scale (row rr of a tile, scale index b along head_dim) inside
 // one tile of the tensor-core scale layout.  For 128-row tiles a 512-byte atom
 // holds 128 rows x 4 scales: byte = (rr%32)*16 + (rr/32)*4 + b%4, atoms in
@@ -198,7 +228,7 @@ __host__ __device__ __forceinline__ uint32_t sf_tile_offset(int tile_rows, int r
 }
 
 struct QuantTileArgs {
-    int64_t slices;
+    int64_t slices;  // slices quantised: the first `slices` of the launch's (the rest are skipped)
     int seq;         // rows per slice
     int head_dim;    // D (multiple of 32)
     int padded_dim;  // DP, multiple of 64 (the MMA's K step)
@@ -258,6 +288,7 @@ __global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, 
     }
     const bool is_k = blockIdx.z != 0;
     const QuantTileArgs a = is_k ? jk.a : jq.a;
+    if (blockIdx.y >= a.slices) return;
     const InT* x = static_cast<const InT*>(is_k ? jk.x : jq.x);
     uint8_t* codes = is_k ? jk.codes : jq.codes;
     uint8_t* sf = is_k ? jk.sf : jq.sf;

@@ -139,6 +139,20 @@ int fp4attn_attend_masked(const void* V, void* Out, int in_dtype, int out_dtype,
                           int seq_k, int head_dim, float softmax_scale, int mask_mode, const void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* fp4attn_forward with Q quantised inside the attention kernel instead of in
+ * the pre-pass launch, as the reference quantises its Q tile inside its own
+ * kernel (common.h:108-124): the pre-pass quantises only K, and the attention
+ * kernel reads FP16 Q and encodes it with the same encoder, so the codes,
+ * scales and output are those of fp4attn_forward, bit for bit.  Applies to
+ * FP16 input with head_dim <= 128, seq_k >= 3008 (48 key tiles of 64) on the
+ * large-problem schedule (seq_q > 128 and at least 75 query groups of 256
+ * rows); any other problem runs the fp4attn_forward path.  Same arguments and
+ * workspace as fp4attn_forward.
+ * Replaces: the quantisation prologue of fused_fp4_attention (common.h:108-124). */
+int fp4attn_forward_fused_q(const void* Q, const void* K, const void* V, void* Out, int in_dtype, int out_dtype,
+                            int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                            int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
+
 /* fp4attn_forward for callers that cannot allocate device memory (code running
  * during CUDA graph capture, runtimes that own all device memory, loops that
  * must not block on an allocation): the same computation, with the workspace

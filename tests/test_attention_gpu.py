@@ -533,3 +533,53 @@ def test_single_tile_items_many_slices(fa, cuda, sq):
     assert fa.status_query() == fa.OK
     want = oracle.fp4_attention(Q[0].float().numpy(), K[0].float().numpy(), V[0].float().numpy())
     assert_close(out[0].cpu().numpy(), want)
+
+
+# ---- Q quantised inside the attention kernel (fp4attn_forward_fused_q) -----
+# The in-kernel quantiser uses the pre-pass's encoder, so codes, scales and
+# output are those of the two-launch path bit for bit; checked with
+# torch.equal, and against the oracle.
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_fused_q_matches_the_two_launch_path(fa, cuda, d, out_dtype):
+    B, H, sq, sk = 1, 80, 300, 3100  # 160 query groups, 49 key tiles: the in-kernel quantiser; ragged seq_q, seq_k
+    g = torch.Generator().manual_seed(d + 3)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk, sk))
+    Q[0, 5, 17, 3] = float("nan")  # a block with a NaN takes the exact encoder in both quantisers (code 0)
+    Q[0, 6] *= 40.0
+    base = fa.fused_fp4_attention(Q, K, V, out_dtype=out_dtype)
+    fused = fa.fused_fp4_attention(Q, K, V, out_dtype=out_dtype, fuse_q=True)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(base, fused)
+    want = oracle.fp4_attention(Q[0].float().cpu().numpy(), K[0].float().cpu().numpy(), V[0].float().cpu().numpy())
+    if out_dtype == torch.float16:
+        want = want.astype(np.float16).astype(np.float32)
+    assert_close(fused[0].float().cpu().numpy(), want)
+
+
+def test_fused_q_ocp_scale_rule_and_fallbacks(fa, cuda):
+    g = torch.Generator().manual_seed(8)
+    Q, K, V = (torch.randn(1, 80, s, 64, generator=g).half().cuda() for s in (260, 3100, 3100))
+    a = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float32, scale_mode="ocp")
+    b = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float32, scale_mode="ocp", fuse_q=True)
+    assert torch.equal(a, b)
+    # Outside the in-kernel quantiser's scope (FP32 input; seq_q <= 128; d=256; short keys): the two-launch path.
+    for (dt, sq, sk, d) in ((torch.float32, 260, 3100, 64), (torch.float16, 100, 3100, 64),
+                            (torch.float16, 260, 3100, 256), (torch.float16, 260, 300, 64)):
+        Q2, K2, V2 = (torch.randn(1, 80, s, d, generator=g).to(dt).cuda() for s in (sq, sk, sk))
+        a = fa.fused_fp4_attention(Q2, K2, V2, out_dtype=torch.float32)
+        b = fa.fused_fp4_attention(Q2, K2, V2, out_dtype=torch.float32, fuse_q=True)
+        assert torch.equal(a, b)
+    assert fa.status_query() == fa.OK
+
+
+def test_fused_q_full_prefill_4k(fa, cuda):
+    """The bench workload through the fused path: the same bytes as the two-launch path."""
+    import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS["prefill_4k"]
+    Q, K, V = (t[None] for t in wl.make_inputs(w, 3))
+    a = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float16)
+    b = fa.fused_fp4_attention(Q, K, V, out_dtype=torch.float16, fuse_q=True)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(a, b)
