@@ -323,6 +323,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     ptx::tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
     const WaitCtx wctx{&abort_sh, args.timeout_ns};
+    // Everything above overlaps the quantiser's tail when this grid was
+    // launched as its programmatic dependent; from here on the workspace it
+    // wrote is read.
+    ptx::grid_dependency_wait();
 
     if (warp < 4) {
         ptx::setmaxnreg_dec<kCtlRegs>();

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/fp4attn.h"
 #include "attention_pair.cuh"
@@ -330,6 +331,39 @@ int set_smem_once(Kern kern, int bytes, std::atomic<unsigned long long> (&done_c
     return FP4ATTN_OK;
 }
 
+// FP4ATTN_PDL=0 launches the attention kernels without programmatic stream
+// serialization (for comparison).
+bool pdl_enabled()
+{
+    static bool v = [] {
+        const char* s = getenv("FP4ATTN_PDL");
+        return !(s && atoi(s) == 0);
+    }();
+    return v;
+}
+
+// Launches an attention kernel as the programmatic dependent of whatever
+// precedes it in the stream (normally the quantiser): its launch and
+// prologue overlap that grid's tail, and the kernel waits for that grid's
+// completion (griddepcontrol.wait) before it reads the workspace.
+template <typename... KArgs, typename... Args>
+int launch_dependent(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                     Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    FP4_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+    return FP4ATTN_OK;
+}
+
 unsigned long long wait_timeout_ns()
 {
     static unsigned long long ns = [] {
@@ -425,9 +459,7 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     fp4attn::FwdArgs pa = a;
     pa.n_items = static_cast<int>(items);
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, pa);
-    FP4_CUDA(cudaGetLastError());
-    return FP4ATTN_OK;
+    return launch_dependent(kern, grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st, tq, tk, tv, to, pa);
 }
 
 // Share of the exponentials computed by the FMA-pipe polynomial, in eighths
@@ -525,9 +557,7 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
     a.n_items = static_cast<int>(items);
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
-    kern<<<grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st>>>(tq, tk, tv, to, tp, a);
-    FP4_CUDA(cudaGetLastError());
-    return FP4ATTN_OK;
+    return launch_dependent(kern, grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st, tq, tk, tv, to, tp, a);
 }
 
 template <int D, typename OutT>

@@ -71,6 +71,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch: a grid launched with programmatic stream
+// serialization may start while the grid before it in the stream finishes;
+// this waits until that grid has completed and its memory is visible (it
+// returns at once for a grid launched without the attribute).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the grid after this one in the stream (if launched with programmatic
+// stream serialization) be scheduled before this grid has finished.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m)
 {

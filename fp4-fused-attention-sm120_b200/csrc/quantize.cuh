@@ -313,6 +313,10 @@ __global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, 
         const int tile = r >> a.tile_shift, rr = r & (a.tile_rows - 1);
         fs[static_cast<int64_t>(tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] = static_cast<uint8_t>(sb);
     }
+    // This CTA's stores are issued: the attention kernel (launched as this
+    // grid's programmatic dependent) may be scheduled; it waits for this
+    // grid's completion before it reads the workspace.
+    ptx::grid_launch_dependents();
 }
 
 // Row-major quantisation for the public fp4attn_quantize: codes rows x D/2,
