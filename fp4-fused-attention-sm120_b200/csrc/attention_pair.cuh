@@ -925,15 +925,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // reading the staging buffers before they are rewritten.
                 if (lane == 0) ptx::bulk_wait_group_read<0>();
                 __syncwarp();
+                // The warp's staging (2 x OST_BYTES) holds NSLOT chunks: they
+                // are written, then made visible to the TMA with one proxy
+                // fence, and stored as a group.
+                constexpr int CB = 32 * OB;
+                constexpr int NSLOT = 2 * C::OST_BYTES / CB;
 #pragma unroll 1
                 for (int k = 0; k < D / 32; k++) {
                     uint32_t o[32];
                     ptx::tmem_ld32(o_tm + 32 * k, o);
                     ptx::tc_wait_ld();
-                    uint8_t* buf = ost + (k & 1) * C::OST_BYTES;
-                    if (k >= 2) {
-                        // The store that last read this buffer must be done with it.
-                        if (lane == 0) ptx::bulk_wait_group_read<1>();
+                    const int slot = k % NSLOT;
+                    uint8_t* buf = ost + slot * CB;
+                    if (k >= NSLOT && slot == 0) {
+                        // The previous group's stores must be done reading the staging.
+                        if (lane == 0) ptx::bulk_wait_group_read<0>();
                         __syncwarp();
                     }
                     uint32_t ov[OB / 4];
@@ -945,19 +951,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                         for (int i = 0; i < 16; i++)
                             ov[i] = ptx::pack_half2(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
                     }
-                    // 16-byte unit u of row `lane` sits at unit u ^ (address bits 7+):
-                    // SWIZZLE_128B for 128-byte rows, SWIZZLE_64B for 64-byte rows.
 #pragma unroll
                     for (int u = 0; u < OB / 16; u++) {
                         const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
                         *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
                             make_uint4(ov[4 * u], ov[4 * u + 1], ov[4 * u + 2], ov[4 * u + 3]);
                     }
-                    ptx::fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        ptx::tma_store_3d(&tm_o, buf, 32 * k, grow0, slice);
-                        ptx::bulk_commit_group();
+                    if (slot == NSLOT - 1 || k == D / 32 - 1) {
+                        ptx::fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            for (int kk = k - slot; kk <= k; kk++)
+                                ptx::tma_store_3d(&tm_o, ost + (kk % NSLOT) * CB, 32 * kk, grow0, slice);
+                            ptx::bulk_commit_group();
+                        }
                     }
                 }
             }
