@@ -17,10 +17,14 @@
  * common.h:99-102); `stream` is a cudaStream_t (0 = legacy default stream).
  * Every call is asynchronous on `stream` and returns an fp4attn_status code;
  * a non-zero code means nothing was launched.  The library keeps no state
- * between calls except, per device, its first-use set-up (the scale-rule
- * table, the SM count, cached function attributes), an error word
- * (fp4attn_status_query) and the fp4attn_forward_noalloc scratch.  Calls on
- * different streams may run concurrently; the caller owns all buffers.
+ * between calls except, per device, its first-use set-up (the device check
+ * and the SM count; kernel attributes per device context), an error word
+ * (fp4attn_status_query), the fp4attn_forward_noalloc scratch, and per host
+ * thread a cache of recently encoded TMA descriptors.  Calls on different
+ * streams may run concurrently; the caller owns all buffers.  The attention
+ * kernel of a call is launched as the programmatic dependent of the launch
+ * before it in the stream (normally this call's quantiser): it starts while
+ * that launch finishes and waits for it before reading the workspace.
  */
 #ifndef FP4ATTN_H
 #define FP4ATTN_H
@@ -89,8 +93,10 @@ int fp4attn_quantize(const void* x, int dtype, int64_t rows, int head_dim, uint8
                      uint8_t* scales, int scale_mode, int layout, void* stream);
 
 /* Bytes of device workspace fp4attn_forward needs for this problem (the
- * quantised Q/K tiles, their scale tiles, and an FP16 copy of V when V is
- * FP32).  Returns 0 for an invalid shape. */
+ * quantised Q/K tiles, their scale tiles, an FP16 copy of V when V is FP32,
+ * and, for a small problem whose keys are split over several CTAs, the
+ * partial results of the key partitions and their arrival counters).  The
+ * same for every mask mode.  Returns 0 for an invalid shape. */
 size_t fp4attn_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype);
 
 /* Out = softmax(Q K^T * softmax_scale) V per (batch, head) slice, with Q and K
@@ -121,7 +127,9 @@ int fp4attn_prepare(const void* Q, const void* K, const void* V, int in_dtype, i
                     int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Runs the attention kernel on a workspace filled by fp4attn_prepare with the
- * same shape and in_dtype.  V is read directly when in_dtype is FP16.
+ * same shape and in_dtype.  V is read directly when in_dtype is FP16.  May be
+ * called any number of times on one prepared workspace (one call at a time);
+ * after a call that reported FP4ATTN_ETIMEOUT, prepare the workspace again.
  * Replaces: the main loop of the reference kernel (common.h:140-327). */
 int fp4attn_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int seq_q, int seq_k,
                    int head_dim, float softmax_scale, const void* workspace, size_t workspace_bytes, void* stream);
