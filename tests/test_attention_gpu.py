@@ -505,6 +505,42 @@ def test_key_partitions(fa, cuda, d, B, H, sq, sk):
         assert_close(out.reshape(-1, sq, d).float().cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("B,H,sq,sk,d", [(1, 1, 64, 32768, 128), (1, 3, 200, 5000, 96), (1, 2, 128, 700, 32)])
+def test_key_partitions_fp32_input_and_long_keys(fa, cuda, B, H, sq, sk, d):
+    """FP32 input (V staged as FP16 by the quantiser launch) with key
+    partitions, up to the 16-partition cap (32768 keys on one slice)."""
+    g = torch.Generator().manual_seed(sk + d)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half().float() for s in (sq, sk, sk))
+    out = fa.fused_fp4_attention(Q.cuda(), K.cuda(), V.cuda(), out_dtype=torch.float32)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention(Q.reshape(-1, sq, d).numpy(), K.reshape(-1, sk, d).numpy(),
+                                V.reshape(-1, sk, d).numpy())
+    assert_close(out.reshape(-1, sq, d).cpu().numpy(), want)
+
+
+def test_concurrent_calls_on_two_streams(fa, cuda):
+    """Two problems (one split into key partitions, one not) on two streams
+    with their own workspaces, launched back to back so that they can run
+    concurrently: both match the same calls made one at a time."""
+    g = torch.Generator().manual_seed(99)
+    shapes = [(1, 4, 64, 3000, 64), (1, 16, 1000, 900, 128)]
+    ins = [[torch.randn(B, H, s, d, generator=g).half().cuda() for s in (sq, sk, sk)] for B, H, sq, sk, d in shapes]
+    outs = [torch.empty(x[0].shape, dtype=torch.float32, device="cuda") for x in ins]
+    wss = [torch.empty(fa.workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+           for B, H, sq, sk, d in shapes]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for _ in range(3):
+        for x, o, w, st in zip(ins, outs, wss, streams):
+            fa.fused_fp4_attention_into(*x, o, w, stream=st)
+    torch.cuda.synchronize()
+    assert fa.status_query() == fa.OK
+    for x, o in zip(ins, outs):
+        want = fa.fused_fp4_attention(*x, out_dtype=torch.float32)
+        assert fa.status_query() == fa.OK
+        assert torch.equal(o, want)
+
+
 def test_key_partitions_repeat_on_one_workspace(fa, cuda):
     """Launch after launch on one prepared workspace: the same bytes."""
     B, H, sq, sk, d = 1, 4, 64, 2000, 64
