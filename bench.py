@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fuse-q", action="store_true",
+                    help="quantise Q inside the attention kernel (fp4attn_forward_fused_q) in the timed step")
     ap.add_argument("--box-steps", type=int, default=5,
                     help="steps of this rank's share of the box-scale job (0: skip)")
     return ap.parse_args()
@@ -339,6 +341,15 @@ def main():
     flops_rank = shard.flops()
 
     def step(ev_a=None, ev_b=None):
+        if args.fuse_q:
+            # The fused forward is one public call: the attention kernel cannot
+            # be separated from the K pre-pass by events, so its events bracket both.
+            if ev_a is not None:
+                ev_a.record(stream)
+            fa.fused_fp4_attention_into(Q, K, V, out, ws, fuse_q=True)
+            if ev_b is not None:
+                ev_b.record(stream)
+            return
         fa.prepare(Q, K, V, ws)
         if ev_a is not None:
             ev_a.record(stream)
@@ -474,6 +485,8 @@ def main():
         bf16 = burst if basis == "burst" else sustained
         achieved = flops_rank / (kern_ms * 1e-3) / 1e12
         kernel = "fp4_attention_pair_kernel" if base.head_dim <= 128 else "fp4_attention_fwd_kernel"
+        if args.fuse_q:
+            kernel += " (Q quantised in the kernel; kernel_ms includes the K pre-pass)"
         traffic = profile_traffic(args.workload, kernel)
         cpu = None
         if not args.no_cpu_baseline and world == 1:

@@ -126,6 +126,7 @@ struct FwdArgs {
     unsigned long long timeout_ns;
     int causal;                // 1: query i sees keys j <= i + causal_off only (attention, not scores)
     int causal_off;            // seq_k - seq_q (bottom-right alignment)
+    int scores_tma;            // scores: 1 if tm_o maps S (seq_k % 4 == 0) and S goes out by TMA stores
     // The two-query-tile kernel's schedule (PairArgs): query tiles per item,
     // key partitions and their partial results.
     int qtiles, n_pairs, kparts, nk_part;
@@ -529,6 +530,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         };
         int g0 = 0;  // global step of the current item's first step (S buffer and barrier phases)
         int items_done = 0;  // phase of l_ready
+        int sbox = 0;        // scores: boxes this warp has stored (staging buffer alternation)
+        uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
         for (int r = 0; ok && r < rounds; r++) {
         const TileItem item = tile_item<BN>(args, causal, r);
         if (!item.valid) continue;
@@ -545,6 +548,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 uint32_t sr[NT][32];
                 load_s(g, sr);
                 ptx::tc_wait_ld();
+                if (args.scores_tma) {
+                    // This warp's 32 rows x HC columns of S in OCH_E-column boxes:
+                    // each staged swizzled like the TMA box and stored by lane 0;
+                    // rows past seq_q and columns past seq_k are clipped by the map.
+                    constexpr int OE = C::OCH_E, OB = OE * 4;
+#pragma unroll
+                    for (int b = 0; b < HC / OE; b++, sbox++) {
+                        uint8_t* buf = ost + (sbox & 1) * C::OST_BYTES;
+                        if (sbox >= 2) {
+                            // The store that last read this buffer must be done with it.
+                            if (lane == 0) ptx::bulk_wait_group_read<1>();
+                            __syncwarp();
+                        }
+#pragma unroll
+                        for (int u = 0; u < OB / 16; u++) {
+                            const int c = b * OE + 4 * u;  // first column of this 16-byte unit
+                            const int pu = OB == 128 ? (u ^ (lane & 7)) : (u ^ ((lane >> 1) & 3));
+                            *reinterpret_cast<uint4*>(buf + lane * OB + pu * 16) =
+                                make_uint4(sr[c / 32][c % 32], sr[c / 32][c % 32 + 1], sr[c / 32][c % 32 + 2],
+                                           sr[c / 32][c % 32 + 3]);
+                        }
+                        ptx::fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            ptx::tma_store_3d(&tm_o, buf, j * BN + half * HC + b * OE, q0 + wq * 32, slice);
+                            ptx::bulk_commit_group();
+                        }
+                    }
+                } else {
                 const int valid = args.seq_k - j * BN - half * HC;
                 const int grow = q0 + row;
                 if (grow < args.seq_q) {
@@ -556,6 +588,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
                         for (int i = 0; i < 32; i++)
                             if (32 * t + i < valid) dst[32 * t + i] = __uint_as_float(sr[t][i]);
+                }
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&p_full[g & 1]);  // done with S_g: its buffer may be reused
@@ -696,7 +729,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 // with TMA; rows past seq_q are clipped by the tensor map.
                 constexpr int OE = C::OCH_E;
                 constexpr int OB = OE * static_cast<int>(sizeof(OutT));  // bytes per staged row (32, 64, 128)
-                uint8_t* ost = smem + C::OFF_OST + (warp - 4) * 2 * C::OST_BYTES;
                 // The previous item's stores must be done reading the staging buffers.
                 if (lane == 0) ptx::bulk_wait_group_read<0>();
                 __syncwarp();

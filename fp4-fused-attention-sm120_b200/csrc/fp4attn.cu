@@ -446,7 +446,18 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     // Attention output is written by TMA stores in 32-row x OCH_E-column boxes
     // (the scores path stores from registers and ignores this map).
     CUtensorMap to = tq;
-    if constexpr (!kScores) {
+    fp4attn::FwdArgs pa = a;
+    pa.scores_tma = 0;
+    if constexpr (kScores) {
+        // S [slices][seq_q][seq_k] FP32 leaves by TMA stores in 32-row x OCH_E
+        // boxes when its rows are a whole number of 16-byte units.
+        if (a.seq_k % 4 == 0) {
+            const int rc = make_map_3d(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.out, a.seq_k, a.seq_q, slices,
+                                       C::OCH_E, 32, swizzle_for(C::OCH_E * 4));
+            if (rc) return rc;
+            pa.scores_tma = 1;
+        }
+    } else {
         constexpr bool f32 = sizeof(OutT) == 4;
         const int rc = make_map_3d(&to, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                                    static_cast<int>(sizeof(OutT)), a.out, D, a.seq_q, slices, C::OCH_E, 32,
@@ -456,7 +467,6 @@ int launch_fwd_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
     // Persistent: one CTA per SM walks the (slice, query tile) items.
     const int64_t items = static_cast<int64_t>(a.nq_tiles) * slices;
     if (items > INT32_MAX) return fail(FP4ATTN_EINVAL, "too many query tiles");
-    fp4attn::FwdArgs pa = a;
     pa.n_items = static_cast<int>(items);
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
     return launch_dependent(kern, grid, fp4attn::kFwdThreads, C::SMEM_BYTES, st, tq, tk, tv, to, pa);
