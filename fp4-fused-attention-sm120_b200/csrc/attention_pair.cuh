@@ -196,6 +196,21 @@ __device__ __forceinline__ PairItem pair_item(const PairArgs& a, int r)
     return it;
 }
 
+// Register split of the pair kernel.  Its control warpgroup needs fewer
+// registers than the one-tile kernel's, so it hands 64 back and the softmax
+// warpgroups take 216: 128 x 64 + 256 x 216 = 63,488 <= 384 x 168, and
+// 64 + 2 x 216 = 496 registers x 32 lanes per sub-partition.  Measured on the
+// 4k x 4k d128 prefill against 80 / 208: 1.1 % faster, d64 1.8 %.  With
+// in-kernel Q quantisation warp 3 quantises, which spills at 64 registers, so
+// that variant keeps the one-tile kernel's 80 / 208.
+template <bool kFuseQ>
+struct PairRegs {
+    static constexpr int kCtl = kFuseQ ? kCtlRegs : 64;
+    static constexpr int kSm = kFuseQ ? kSmRegs : 216;
+    static_assert(128 * kCtl + 256 * kSm <= kFwdThreads * kLaunchRegs, "register split exceeds the launch pool");
+    static_assert((kCtl + 2 * kSm) * 32 <= 16384, "register split exceeds a sub-partition");
+};
+
 // kWithhold (test instantiation only): the first softmax thread never makes
 // its first s_free arrival, so the S issuer's bounded wait for step 1 runs out
 // and the kernel's own abort path runs: every role leaves its loop, in-flight
@@ -364,7 +379,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     };
 
     if (warp < 4) {
-        ptx::setmaxnreg_dec<kCtlRegs>();
+        ptx::setmaxnreg_dec<PairRegs<kFuseQ>::kCtl>();
         if (warp == 0) {
             // -------------------------------------------------------- producer
             // Items in order; the K/V ring index kv runs on across items, and
@@ -566,7 +581,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
         }
     } else {
-        ptx::setmaxnreg_inc<kSmRegs>();
+        ptx::setmaxnreg_inc<PairRegs<kFuseQ>::kSm>();
         // ------------------------------------------------------------ softmax warpgroups
         constexpr int NT = BN / 32;                // 32-column chunks of an S row
         const int t = (warp - 4) / 4;              // query tile of this warpgroup

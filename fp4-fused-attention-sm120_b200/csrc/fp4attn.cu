@@ -517,7 +517,7 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
         launch_regs = attr.numRegs;
         launch_regs_cache.store(launch_regs, std::memory_order_relaxed);
     }
-    if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::kCtlRegs + 256 * fp4attn::kSmRegs ||
+    if (launch_regs * fp4attn::kFwdThreads < 128 * fp4attn::PairRegs<kFuseQ>::kCtl + 256 * fp4attn::PairRegs<kFuseQ>::kSm ||
         launch_regs > fp4attn::kLaunchRegs)
         return fail(FP4ATTN_ECUDA, "attention kernel built with %d registers/thread; the register split needs %d",
                     launch_regs, fp4attn::kLaunchRegs);
