@@ -19,7 +19,8 @@ __all__ = [
     "BLOCK_ELEMENT", "BQ", "Fp4AttnError", "lib", "lib_path", "quantize", "workspace_size",
     "fused_fp4_attention", "fused_fp4_attention_into", "debug_scores", "status_query",
     "selftest_timeout", "selftest_abort", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
-    "F32", "F16", "MASK_NONE", "MASK_CAUSAL",
+    "F32", "F16", "MASK_NONE", "MASK_CAUSAL", "fused_fp4_attention_lse", "backward_workspace_size",
+    "fp4_attention_backward", "FP4Attention", "fp4_attention",
 ]
 
 BLOCK_ELEMENT = 32  # common.h:15
@@ -78,6 +79,12 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_attend_masked.restype = i32
     L.fp4attn_debug_scores.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, sz, vp]
     L.fp4attn_debug_scores.restype = i32
+    L.fp4attn_forward_lse.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, i32, vp, sz, vp]
+    L.fp4attn_forward_lse.restype = i32
+    L.fp4attn_backward_workspace_size.argtypes = [i32] * 5
+    L.fp4attn_backward_workspace_size.restype = sz
+    L.fp4attn_backward.argtypes = [vp] * 9 + [i32] * 6 + [f32, i32, i32, vp, sz, vp]
+    L.fp4attn_backward.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
     L.fp4attn_status_query.restype = i32
     L.fp4attn_selftest_timeout.argtypes = [ctypes.c_uint, vp]
@@ -248,6 +255,99 @@ def fused_fp4_attention(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode=
     out = torch.empty((B, H, Sq, D), dtype=out_dtype or Q.dtype, device=Q.device)
     ws = torch.empty(workspace_size(B, H, Sq, Sk, D, _dtype_code(Q)), dtype=torch.uint8, device=Q.device)
     return fused_fp4_attention_into(Q, K, V, out, ws, softmax_scale, scale_mode, stream, causal, fuse_q)
+
+
+def fused_fp4_attention_lse(Q, K, V, out_dtype=None, softmax_scale=None, scale_mode="reference", stream=None,
+                            causal=False):
+    """fused_fp4_attention that also returns, per query row, the natural-log
+    log-sum-exp of the scaled scores (FP32 [batch, heads, seq_q];
+    fp4attn_forward_lse) -- what the backward pass needs.  head_dim 64, 128."""
+    torch = _torch()
+    B, H, Sq, Sk, D = _check_qkv(Q, K, V)
+    out = torch.empty((B, H, Sq, D), dtype=out_dtype or Q.dtype, device=Q.device)
+    lse = torch.empty((B, H, Sq), dtype=torch.float32, device=Q.device)
+    ws = torch.empty(workspace_size(B, H, Sq, Sk, D, _dtype_code(Q)), dtype=torch.uint8, device=Q.device)
+    rc = lib().fp4attn_forward_lse(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), lse.data_ptr(),
+                                   _dtype_code(Q), _dtype_code(out), B, H, Sq, Sk, D, float(softmax_scale or 0.0),
+                                   _scale_mode(scale_mode), MASK_CAUSAL if causal else MASK_NONE, ws.data_ptr(),
+                                   ws.numel(), _stream_ptr(stream))
+    _check(rc, "fp4attn_forward_lse")
+    return out, lse
+
+
+def backward_workspace_size(batch: int, heads: int, seq_q: int, seq_k: int, head_dim: int) -> int:
+    return int(lib().fp4attn_backward_workspace_size(batch, heads, seq_q, seq_k, head_dim))
+
+
+def fp4_attention_backward(Q, K, V, out, dout, lse, softmax_scale=None, scale_mode="reference", stream=None,
+                           causal=False, workspace=None):
+    """Gradients (dQ, dK, dV), FP32, of the FP4 fused attention
+    (fp4attn_backward): FP16 Q, K, V and dout, the forward's `out` (FP16 or
+    FP32) and `lse` from fused_fp4_attention_lse with the same scale, scale
+    mode and mask.  The quantiser is a straight-through estimator."""
+    torch = _torch()
+    B, H, Sq, Sk, D = _check_qkv(Q, K, V)
+    if Q.dtype != torch.float16 or dout.dtype != torch.float16:
+        raise TypeError("the backward pass takes float16 Q, K, V and dout")
+    if out.shape != Q.shape or dout.shape != Q.shape or not out.is_contiguous() or not dout.is_contiguous():
+        raise ValueError("out and dout must be contiguous with Q's shape")
+    if lse.shape != (B, H, Sq) or lse.dtype != torch.float32 or not lse.is_contiguous():
+        raise ValueError("lse must be a contiguous float32 [batch, heads, seq_q] tensor")
+    dq = torch.empty(Q.shape, dtype=torch.float32, device=Q.device)
+    dk = torch.empty(K.shape, dtype=torch.float32, device=Q.device)
+    dv = torch.empty(V.shape, dtype=torch.float32, device=Q.device)
+    if workspace is None:
+        workspace = torch.empty(backward_workspace_size(B, H, Sq, Sk, D), dtype=torch.uint8, device=Q.device)
+    rc = lib().fp4attn_backward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                                lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _dtype_code(out), B, H,
+                                Sq, Sk, D, float(softmax_scale or 0.0), _scale_mode(scale_mode),
+                                MASK_CAUSAL if causal else MASK_NONE, workspace.data_ptr(), workspace.numel(),
+                                _stream_ptr(stream))
+    _check(rc, "fp4attn_backward")
+    return dq, dk, dv
+
+
+_FP4_ATTENTION_FN = None
+
+
+def _autograd_function():
+    global _FP4_ATTENTION_FN
+    if _FP4_ATTENTION_FN is not None:
+        return _FP4_ATTENTION_FN
+    torch = _torch()
+
+    class FP4Attention(torch.autograd.Function):
+        """Differentiable FP4 fused attention: forward = fused_fp4_attention_lse,
+        backward = fp4_attention_backward (straight-through quantiser)."""
+
+        @staticmethod
+        def forward(ctx, Q, K, V, softmax_scale, causal):
+            out, lse = fused_fp4_attention_lse(Q, K, V, softmax_scale=softmax_scale, causal=causal)
+            ctx.save_for_backward(Q, K, V, out, lse)
+            ctx.softmax_scale, ctx.causal = softmax_scale, causal
+            return out
+
+        @staticmethod
+        def backward(ctx, dout):
+            Q, K, V, out, lse = ctx.saved_tensors
+            dq, dk, dv = fp4_attention_backward(Q, K, V, out, dout.to(torch.float16).contiguous(), lse,
+                                                softmax_scale=ctx.softmax_scale, causal=ctx.causal)
+            return dq.to(Q.dtype), dk.to(K.dtype), dv.to(V.dtype), None, None
+
+    _FP4_ATTENTION_FN = FP4Attention
+    return FP4Attention
+
+
+def __getattr__(name):
+    if name == "FP4Attention":
+        return _autograd_function()
+    raise AttributeError(name)
+
+
+def fp4_attention(Q, K, V, softmax_scale=None, causal=False):
+    """softmax(Q K^T * scale) V with FP4 Q, K that autograd can differentiate
+    (float16 [batch, heads, seq, head_dim], head_dim 64 or 128)."""
+    return _autograd_function().apply(Q, K, V, softmax_scale, causal)
 
 
 def debug_scores(Q, K, scale_mode="reference", stream=None):

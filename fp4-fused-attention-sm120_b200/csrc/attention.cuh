@@ -136,6 +136,9 @@ struct FwdArgs {
     // In-kernel Q quantisation (fp4attn_forward_fused_q): FP16 Q and the scale rule.
     const void* q_in;
     int ocp_mode;
+    // fp4attn_forward_lse: per query row the natural-log log-sum-exp of the
+    // scaled scores, [slices][seq_q] FP32 (two-query-tile kernel only).
+    float* lse;
 };
 
 // Work item r of this CTA's static schedule for the one-tile kernel: (slice,

@@ -1,0 +1,692 @@
+// attention_bwd.cuh -- backward pass of the FP4 fused attention on sm_100a
+// (head_dim 64 and 128).
+//
+// The forward (attention_pair.cuh, attention.cuh) computes, per slice,
+//     z = scale * Qq Kq^T,   P = softmax(z) (row-wise),   O = P V
+// where Qq, Kq are Q and K after the reference's E2M1 + UE8M0 quantisation
+// (common.h:21-48, :108-169) and dequantisation.  The reference is forward
+// only; this pass differentiates that computation with the quantiser as a
+// straight-through estimator (d Qq / d Q = identity), the usual treatment of
+// a rounding step in low-precision training:
+//     dV = P^T dO,   dP = dO V^T,   Dd_i = sum_c dO_ic O_ic,
+//     dZ = P o (dP - Dd),   dQ = scale * dZ Kq,   dK = scale * dZ^T Qq.
+// P is rebuilt from S = Qq Kq^T (the same block-scaled E2M1 MMA as the
+// forward) and the forward's per-row log-sum-exp: P = 2^(S c - lse2), with
+// c = scale * log2(e) and lse2 = lse * log2(e).
+//
+// One work item is one 128-key tile of one slice; the kernel is persistent
+// (one CTA per SM walks the items).  An item holds its keys' K codes and
+// scales, V (FP16) and Kq (BF16) in shared memory and walks the 64-row query
+// tiles that see its keys.  Per step, with the keys as the MMA M dimension:
+//     S^T  = K Q^T          tcgen05.mma kind::mxf4 block_scale  (M128 N64)
+//     dP^T = V dO^T         kind::f16, F16 operands             (M128 N64)
+//     dV  += P^T dO         kind::f16, F16, P from shared memory (M128 N=D)
+//     dK  += dZ^T Qq        kind::f16, BF16                      (M128 N=D)
+//     dQ^T = Kq^T dZ^T      kind::f16, BF16, A and B MN-major    (M128 N64)
+// dV and dK accumulate in TMEM over the item's steps; each step's dQ^T tile
+// (head_dim rows x 64 queries) is added into an FP32 accumulator in global
+// memory, [slices][D][seq_q padded], by TMA reduce-add (the other key tiles
+// of the slice add theirs), and a last kernel transposes and scales it.
+//
+// Roles (384 threads):
+//   warp 0      TMA producer: per item K codes + scale tile, V, Kq; per step
+//               (QST-stage ring) Q codes + scale tile, dO, Qq, lse2, Dd.
+//   warp 1      MMA issuer (one thread).  S^T and dP^T of step g+1 are issued
+//               as soon as the softmax warpgroup holds step g's in registers,
+//               before step g's dV, dK and dQ^T, so the tensor core computes
+//               them while the warpgroup works on step g.
+//   warps 2-3   idle.
+//   warps 4-7   gradient warpgroup: thread = key row = TMEM lane.  Reads its
+//               S^T and dP^T rows, forms P and dZ for 64 queries, and writes
+//               them (FP16, BF16) to shared memory as 128-byte swizzled rows,
+//               the layout the three MMAs read (K-major for dV and dK,
+//               MN-major for dQ^T).
+//   warps 8-11  dQ warpgroup: thread = head-dim row of dQ^T = TMEM lane.  Per
+//               step it moves its dQ^T row into a per-warp staging buffer and
+//               lane 0 of each warp adds the warp's 32 rows into the global
+//               accumulator with TMA reduce-add.  At the end of an item it
+//               writes dV and scale * dK (thread = key row) to the outputs.
+//
+// TMEM columns (512 allocated): S^T [0,64), dP^T [64,128), dV [128, 128+D),
+// dK [128+D, 128+2D), dQ^T [128+2D, +64), K scales (4), Q scales (4 per stage).
+//
+// Every mbarrier wait is bounded (globaltimer) as in the forward kernels: on
+// expiry the CTA records FP4ATTN_ETIMEOUT, every role leaves its loop,
+// in-flight copies, reductions and MMAs are drained (bounded), TMEM is freed
+// and the CTA returns.  No role waits on a barrier shared by more than one
+// warp except through mbarriers, so a role that gives up cannot strand
+// another one.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <climits>
+
+#include "attention.cuh"
+#include "quantize.cuh"
+
+namespace fp4attn {
+
+template <int D>
+struct BwdCfg {
+    static_assert(D == 64 || D == 128, "the backward kernel covers head_dim 64 and 128");
+    static constexpr int BK = 128;                  // keys per item (MMA M)
+    static constexpr int BQ = 64;                   // queries per step
+    static constexpr int QK_ROW = D / 2;            // bytes per packed code row (swizzle = row)
+    static constexpr int KSTEPS = D / 64;           // mxf4 MMAs per S^T tile (K = 64 each)
+    static constexpr int DCH = D / 64;              // 64-column (128-byte) chunks of a 16-bit row
+    static constexpr int QST = 2;                   // query stages
+    // TMEM
+    static constexpr int S_COL = 0;
+    static constexpr int DP_COL = 64;
+    static constexpr int DV_COL = 128;
+    static constexpr int DK_COL = DV_COL + D;
+    static constexpr int DQ_COL = DK_COL + D;
+    static constexpr int SFA_COL = DQ_COL + 64;
+    static constexpr int SFB_COL = SFA_COL + 4;     // + stage * 4
+    static constexpr int TMEM_USED = SFB_COL + 4 * QST;
+    static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
+    // shared memory (offsets from a 1024-aligned base)
+    static constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+    static constexpr int K_BYTES = BK * QK_ROW;
+    static constexpr int SF_BYTES = 512;
+    static constexpr int OFF_K = 0;
+    static constexpr int OFF_KSF = align1k(K_BYTES);
+    static constexpr int OFF_V = align1k(OFF_KSF + SF_BYTES);
+    static constexpr int V_BYTES = DCH * BK * 128;
+    static constexpr int OFF_KQ = OFF_V + V_BYTES;
+    // Kq: two 64-column chunks, the M of the dQ^T MMA (head_dim 64: the
+    // second chunk is zero and so are dQ^T rows 64..127).
+    static constexpr int KQ_BYTES = 2 * BK * 128;
+    static constexpr int OFF_STAGE = OFF_KQ + KQ_BYTES;
+    // one query stage
+    static constexpr int SQ_Q = 0;
+    static constexpr int Q_BYTES = BQ * QK_ROW;
+    static constexpr int SQ_QSF = align1k(Q_BYTES);
+    static constexpr int SQ_DO = align1k(SQ_QSF + SF_BYTES);
+    static constexpr int DO_BYTES = DCH * BQ * 128;
+    static constexpr int SQ_QQ = SQ_DO + DO_BYTES;
+    static constexpr int SQ_LSE = SQ_QQ + DO_BYTES;
+    static constexpr int SQ_DD = SQ_LSE + BQ * 4;
+    static constexpr int STAGE_BYTES = align1k(SQ_DD + BQ * 4);
+    static constexpr int STAGE_TX = Q_BYTES + SF_BYTES + 2 * DO_BYTES + 2 * BQ * 4;
+    static constexpr int KV_TX = K_BYTES + SF_BYTES + 2 * V_BYTES;  // K codes, scales, V, Kq (D columns)
+    // P and dZ: 128 key rows x 64 queries, 128-byte swizzled rows
+    static constexpr int OFF_P = OFF_STAGE + QST * STAGE_BYTES;
+    static constexpr int OFF_DS = OFF_P + BK * 128;
+    // dQ^T staging: per dQ warp two boxes of 32 head-dim rows x 32 queries (FP32)
+    static constexpr int DQW_BYTES = 2 * 32 * 128;
+    static constexpr int OFF_DQST = OFF_DS + BK * 128;
+    static constexpr int OFF_BAR = OFF_DQST + 4 * DQW_BYTES;
+    // kv_full, kv_empty, q_full[QST], q_empty[QST], s_full, s_free, ds_full,
+    // ds_free, dq_full, dq_free, acc_full, acc_free, drain
+    static constexpr int NUM_BARS = 2 + 2 * QST + 9;
+    static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
+};
+
+struct BwdArgs {
+    int seq_q, seq_k;
+    int sq_pad;                // seq_q rounded up to BQ (row pitch of lse2, dd and the dQ accumulator)
+    int nq_tiles, nk_tiles;    // 64-row query tiles, 128-row key tiles per slice
+    int n_items;               // slices * nk_tiles
+    int slices;
+    float scale_log2;          // softmax_scale * log2(e)
+    float scale;               // softmax_scale
+    const uint8_t* q_sf;       // [slices][nq_tiles][512]  (64-row scale tiles)
+    const uint8_t* k_sf;       // [slices][nk_tiles][512]  (128-row scale tiles)
+    const float* lse2;         // [slices][sq_pad]: lse * log2(e); +inf on padding rows
+    const float* dd;           // [slices][sq_pad]: rowsum(dO o O); 0 on padding rows
+    float* dk;                 // [slices][seq_k][D] FP32
+    float* dv;                 // [slices][seq_k][D] FP32
+    unsigned long long timeout_ns;
+    int causal;                // 1: query i sees keys j <= i + causal_off only
+    int causal_off;            // seq_k - seq_q
+};
+
+// Work item r of this CTA: (slice, key tile) and its query tiles
+// [q_begin, nq_tiles).  With the causal mask a key tile is seen only by the
+// queries at or after its first key (minus the offset), so low key tiles have
+// the most steps: items go heaviest first (key-tile-major) and are dealt in a
+// snake order, as the forward deals its causal items.
+struct BwdItem {
+    int slice, kt, q_begin;
+    bool valid;
+};
+
+__device__ __forceinline__ BwdItem bwd_item(const BwdArgs& a, int r)
+{
+    const int G = gridDim.x, b = blockIdx.x;
+    BwdItem it;
+    if (a.causal) {
+        const int w = r * G + ((r & 1) ? G - 1 - b : b);
+        it.valid = w < a.n_items;
+        it.kt = w / a.slices;
+        it.slice = w % a.slices;
+        const int first_q = it.kt * 128 - a.causal_off;  // first query that sees a key of the tile
+        it.q_begin = first_q <= 0 ? 0 : first_q / 64;
+    } else {
+        const int w = r * G + b;
+        it.valid = w < a.n_items;
+        it.slice = w / a.nk_tiles;
+        it.kt = w % a.nk_tiles;
+        it.q_begin = 0;
+    }
+    return it;
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi)
+{
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int D>
+__global__ void __launch_bounds__(384, 1)
+    fp4_attention_bwd_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kq,
+                             const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_qq,
+                             const __grid_constant__ CUtensorMap tm_dq, const BwdArgs args)
+{
+    using C = BwdCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sK = smem + C::OFF_K;
+    uint8_t* sKsf = smem + C::OFF_KSF;
+    uint8_t* sV = smem + C::OFF_V;
+    uint8_t* sKq = smem + C::OFF_KQ;
+    uint8_t* sStage = smem + C::OFF_STAGE;
+    uint8_t* sP = smem + C::OFF_P;
+    uint8_t* sDS = smem + C::OFF_DS;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* kv_full = bars;
+    uint64_t* kv_empty = bars + 1;             // the item's MMAs are done with K, V, Kq (commit)
+    uint64_t* q_full = bars + 2;               // [QST]
+    uint64_t* q_empty = q_full + C::QST;       // [QST] MMAs done (commit) + gradient warpgroup done (128)
+    uint64_t* s_full = q_empty + C::QST;       // S^T and dP^T computed (commit)
+    uint64_t* s_free = s_full + 1;             // S^T and dP^T copied to registers (128)
+    uint64_t* ds_full = s_free + 1;            // P and dZ written to shared memory (128)
+    uint64_t* ds_free = ds_full + 1;           // dV, dK, dQ^T MMAs done with P and dZ (commit)
+    uint64_t* dq_full = ds_free + 1;           // dQ^T computed (commit)
+    uint64_t* dq_free = dq_full + 1;           // dQ^T copied to registers (128)
+    uint64_t* acc_full = dq_free + 1;          // the item's dV, dK complete (commit)
+    uint64_t* acc_free = acc_full + 1;         // dV, dK copied out (128)
+    uint64_t* drain_bar = acc_free + 1;
+
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int abort_sh;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(kv_full, 1);
+        ptx::mbar_init(kv_empty, 1);
+        for (int i = 0; i < C::QST; i++) {
+            ptx::mbar_init(&q_full[i], 1);
+            ptx::mbar_init(&q_empty[i], 1 + 128);
+        }
+        ptx::mbar_init(s_full, 1);
+        ptx::mbar_init(s_free, 128);
+        ptx::mbar_init(ds_full, 128);
+        ptx::mbar_init(ds_free, 1);
+        ptx::mbar_init(dq_full, 1);
+        ptx::mbar_init(dq_free, 128);
+        ptx::mbar_init(acc_full, 1);
+        ptx::mbar_init(acc_free, 128);
+        ptx::mbar_init(drain_bar, 1);
+        abort_sh = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        ptx::prefetch_tmap(&tm_k);
+        ptx::prefetch_tmap(&tm_q);
+        ptx::prefetch_tmap(&tm_v);
+        ptx::prefetch_tmap(&tm_kq);
+        ptx::prefetch_tmap(&tm_do);
+        ptx::prefetch_tmap(&tm_qq);
+        ptx::prefetch_tmap(&tm_dq);
+    }
+    if (warp == 1) {
+        ptx::tmem_alloc(&tmem_base_sh, 512);
+        ptx::tmem_relinquish();
+    }
+    if constexpr (D == 64) {
+        // The second Kq chunk (head-dim rows 64..127 of the dQ^T MMA's A) is zero.
+        for (int u = threadIdx.x; u < C::BK * 128 / 16; u += blockDim.x)
+            *reinterpret_cast<uint4*>(sKq + C::BK * 128 + 16 * u) = make_uint4(0u, 0u, 0u, 0u);
+        ptx::fence_proxy_async_smem();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const WaitCtx wctx{&abort_sh, args.timeout_ns};
+    // The set-up above overlaps the previous grid's tail (programmatic
+    // dependent launch); the prepared operands are read from here on.
+    ptx::grid_dependency_wait();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int it = 0, g = 0;
+            bool ok = true;
+            for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                const BwdItem item = bwd_item(args, r);
+                if (!item.valid || item.q_begin >= args.nq_tiles) continue;
+                if (it > 0 && !wait_phase(kv_empty, (it - 1) & 1, wctx, kSiteKEmpty)) break;
+                ptx::mbar_arrive_expect_tx(kv_full, C::KV_TX);
+                ptx::tma_load_3d(sK, &tm_k, kv_full, 0, item.kt * C::BK, item.slice);
+                ptx::bulk_load(sKsf, args.k_sf + (static_cast<size_t>(item.slice) * args.nk_tiles + item.kt) * C::SF_BYTES,
+                               C::SF_BYTES, kv_full);
+#pragma unroll
+                for (int c = 0; c < C::DCH; c++) {
+                    ptx::tma_load_3d(sV + c * C::BK * 128, &tm_v, kv_full, 64 * c, item.kt * C::BK, item.slice);
+                    ptx::tma_load_3d(sKq + c * C::BK * 128, &tm_kq, kv_full, 64 * c, item.kt * C::BK, item.slice);
+                }
+                it++;
+                for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
+                    const int qs = g % C::QST;
+                    if (g >= C::QST && !wait_phase(&q_empty[qs], ((g / C::QST) - 1) & 1, wctx, kSiteQEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = sStage + qs * C::STAGE_BYTES;
+                    ptx::mbar_arrive_expect_tx(&q_full[qs], C::STAGE_TX);
+                    ptx::tma_load_3d(st + C::SQ_Q, &tm_q, &q_full[qs], 0, qi * C::BQ, item.slice);
+                    ptx::bulk_load(st + C::SQ_QSF,
+                                   args.q_sf + (static_cast<size_t>(item.slice) * args.nq_tiles + qi) * C::SF_BYTES,
+                                   C::SF_BYTES, &q_full[qs]);
+#pragma unroll
+                    for (int c = 0; c < C::DCH; c++) {
+                        ptx::tma_load_3d(st + C::SQ_DO + c * C::BQ * 128, &tm_do, &q_full[qs], 64 * c, qi * C::BQ,
+                                         item.slice);
+                        ptx::tma_load_3d(st + C::SQ_QQ + c * C::BQ * 128, &tm_qq, &q_full[qs], 64 * c, qi * C::BQ,
+                                         item.slice);
+                    }
+                    const size_t row = static_cast<size_t>(item.slice) * args.sq_pad + qi * C::BQ;
+                    ptx::bulk_load(st + C::SQ_LSE, args.lse2 + row, C::BQ * 4, &q_full[qs]);
+                    ptx::bulk_load(st + C::SQ_DD, args.dd + row, C::BQ * 4, &q_full[qs]);
+                }
+            }
+            // Every copy this thread issued lands before the CTA exits.
+            const unsigned long long drain_ns = 2ull * args.timeout_ns;
+            if (it > 0) drain_phase(kv_full, (it - 1) & 1, drain_ns);
+            for (int i = g - C::QST < 0 ? 0 : g - C::QST; i < g; i++)
+                drain_phase(&q_full[i % C::QST], (i / C::QST) & 1, drain_ns);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::QK_ROW);
+            const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::QK_ROW, qk_layout);
+            const uint64_t ksfdesc = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
+            constexpr uint32_t idesc_dp = ptx::idesc_f16x(128, C::BQ, 0, false, false);
+            constexpr uint32_t idesc_dv = ptx::idesc_f16x(128, D, 0, false, true);
+            constexpr uint32_t idesc_dk = ptx::idesc_f16x(128, D, 1, false, true);
+            constexpr uint32_t idesc_dq = ptx::idesc_f16x(128, C::BQ, 1, true, true);
+            const uint32_t sw128 = ptx::kSwizzle128B;
+            int it = 0, g = 0;
+            bool ok = true;
+            // S^T and dP^T of global step gg (stage gg % QST) into their TMEM columns.
+            auto issue_sdp = [&](int gg) -> bool {
+                const int qs = gg % C::QST;
+                if (!wait_phase(&q_full[qs], (gg / C::QST) & 1, wctx, kSiteQFull)) return false;
+                if (gg > 0 && !wait_phase(s_free, (gg - 1) & 1, wctx, kSiteSFree)) return false;
+                ptx::tc_fence_after();
+                uint8_t* st = sStage + qs * C::STAGE_BYTES;
+                const uint32_t sfb = tmem + C::SFB_COL + 4 * qs;
+                ptx::tc_cp_32x128b_warpx4(sfb, ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QSF), 0, 128, ptx::kSwizzleNone));
+                const uint64_t qdesc = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_Q), 16, 8 * C::QK_ROW, qk_layout);
+#pragma unroll
+                for (int kk = 0; kk < C::KSTEPS; kk++) {
+                    const uint32_t sf_id = 2u * (kk & 1);
+                    ptx::mma_mxf4(tmem + C::S_COL, kdesc0 + static_cast<uint64_t>((kk * 32) >> 4),
+                                  qdesc + static_cast<uint64_t>((kk * 32) >> 4), ptx::idesc_mxf4(128, C::BQ, sf_id, sf_id),
+                                  (tmem + C::SFA_COL) | (sf_id << 30), sfb | (sf_id << 30), kk > 0 ? 1u : 0u);
+                }
+                // dP^T = V dO^T: both K-major (K = head_dim), 16 columns per MMA.
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = (kk % 4) * 32;  // 16 columns = 32 bytes into the chunk's rows
+                    const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sV + (kk / 4) * C::BK * 128) + off, 16, 1024, sw128);
+                    const uint64_t b =
+                        ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO + (kk / 4) * C::BQ * 128) + off, 16, 1024, sw128);
+                    ptx::mma_f16_ss(tmem + C::DP_COL, a, b, idesc_dp, kk > 0 ? 1u : 0u);
+                }
+                ptx::tc_commit(s_full);
+                return true;
+            };
+            for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                const BwdItem item = bwd_item(args, r);
+                if (!item.valid || item.q_begin >= args.nq_tiles) continue;
+                const int n = args.nq_tiles - item.q_begin;
+                if (!wait_phase(kv_full, it & 1, wctx, kSiteKFull)) break;
+                ptx::tc_fence_after();
+                ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL, ksfdesc);
+                if (!issue_sdp(g)) break;
+                for (int i = 0; i < n; i++, g++) {
+                    const int qs = g % C::QST;
+                    uint8_t* st = sStage + qs * C::STAGE_BYTES;
+                    if (i + 1 < n && !issue_sdp(g + 1)) { ok = false; break; }
+                    if (!wait_phase(ds_full, g & 1, wctx, kSitePFull)) { ok = false; break; }
+                    if (i == 0 && it > 0 && !wait_phase(acc_free, (it - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    // dV += P^T dO, dK += dZ^T Qq: A K-major (rows = keys, K = queries),
+                    // B MN-major (N = head_dim in 64-column chunks, K = queries).
+#pragma unroll
+                    for (int kk = 0; kk < C::BQ / 16; kk++) {
+                        const uint64_t ap = ptx::make_sdesc(ptx::smem_u32(sP) + kk * 32, 16, 1024, sw128);
+                        const uint64_t ad = ptx::make_sdesc(ptx::smem_u32(sDS) + kk * 32, 16, 1024, sw128);
+                        const uint64_t bo =
+                            ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
+                        const uint64_t bq =
+                            ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QQ) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
+                        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                        ptx::mma_f16_ss(tmem + C::DV_COL, ap, bo, idesc_dv, acc);
+                        ptx::mma_f16_ss(tmem + C::DK_COL, ad, bq, idesc_dk, acc);
+                    }
+                    if (g > 0 && !wait_phase(dq_free, (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    // dQ^T = Kq^T dZ^T: A MN-major (M = head_dim in 64-row chunks, K = keys),
+                    // B MN-major (N = queries, K = keys).
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 16; kk++) {
+                        const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sKq) + kk * 16 * 128, C::BK * 128, 1024, sw128);
+                        const uint64_t b = ptx::make_sdesc(ptx::smem_u32(sDS) + kk * 16 * 128, C::BK * 128, 1024, sw128);
+                        ptx::mma_f16_ss(tmem + C::DQ_COL, a, b, idesc_dq, kk > 0 ? 1u : 0u);
+                    }
+                    ptx::tc_commit(ds_free);
+                    ptx::tc_commit(dq_full);
+                    ptx::tc_commit(&q_empty[qs]);
+                }
+                if (!ok) break;
+                ptx::tc_commit(acc_full);
+                ptx::tc_commit(kv_empty);
+                it++;
+            }
+            // Every tcgen05 op this thread issued completes before TMEM is freed.
+            ptx::tc_commit(drain_bar);
+            drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------------ gradient warpgroup
+        const int kr = (warp - 4) * 32 + lane;     // key row of the item = TMEM lane
+        const uint32_t lane_off = static_cast<uint32_t>((warp - 4) * 32) << 16;
+        const float c = args.scale_log2;
+        int g = 0;
+        bool ok = true;
+        for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+            const BwdItem item = bwd_item(args, r);
+            if (!item.valid || item.q_begin >= args.nq_tiles) continue;
+            const int key = item.kt * C::BK + kr;
+            const bool key_ok = key < args.seq_k;
+            // Query q sees this key iff q >= lim.
+            const int lim = args.causal ? key - args.causal_off : INT_MIN;
+            for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
+                const int qs = g % C::QST;
+                if (!__all_sync(0xffffffffu, wait_phase(s_full, g & 1, wctx, kSiteSFull))) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t sr[2][32], dr[2][32];
+                ptx::tmem_ld32(tmem + lane_off + C::S_COL, sr[0]);
+                ptx::tmem_ld32(tmem + lane_off + C::S_COL + 32, sr[1]);
+                ptx::tmem_ld32(tmem + lane_off + C::DP_COL, dr[0]);
+                ptx::tmem_ld32(tmem + lane_off + C::DP_COL + 32, dr[1]);
+                ptx::tc_wait_ld();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(s_free);
+                // lse2 and Dd of this stage (the TMA's writes are visible after the wait).
+                if (!__all_sync(0xffffffffu, wait_phase(&q_full[qs], (g / C::QST) & 1, wctx, kSiteQFull))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* st = sStage + qs * C::STAGE_BYTES;
+                const float4* lse4 = reinterpret_cast<const float4*>(st + C::SQ_LSE);
+                const float4* dd4 = reinterpret_cast<const float4*>(st + C::SQ_DD);
+                const int q0 = qi * C::BQ;
+                uint32_t pk[32], dk[32];
+#pragma unroll
+                for (int c4 = 0; c4 < 16; c4++) {
+                    const float4 L = lse4[c4], Dv = dd4[c4];
+                    const float Ls[4] = {L.x, L.y, L.z, L.w}, Ds[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
+                    float pv[4], dv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int q = 4 * c4 + e;
+                        const float s = __uint_as_float(sr[q / 32][q % 32]);
+                        const float dpv = __uint_as_float(dr[q / 32][q % 32]);
+                        float p = ptx::ex2_approx(fmaf(s, c, -Ls[e]));
+                        if (!key_ok || q0 + q < lim) p = 0.f;
+                        pv[e] = p;
+                        dv[e] = p * (dpv - Ds[e]);
+                    }
+                    pk[2 * c4] = ptx::pack_half2(pv[0], pv[1]);
+                    pk[2 * c4 + 1] = ptx::pack_half2(pv[2], pv[3]);
+                    dk[2 * c4] = pack_bf162(dv[0], dv[1]);
+                    dk[2 * c4 + 1] = pack_bf162(dv[2], dv[3]);
+                }
+                // The previous step's dV, dK and dQ^T MMAs must be done reading P and dZ.
+                if (g > 0 && !__all_sync(0xffffffffu, wait_phase(ds_free, (g - 1) & 1, wctx, kSitePvDone))) {
+                    ok = false;
+                    break;
+                }
+                // Row kr: 128 bytes, 16-byte unit u at (u ^ (kr & 7)) (128-byte swizzle).
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int pu = u ^ (kr & 7);
+                    *reinterpret_cast<uint4*>(sP + kr * 128 + pu * 16) =
+                        make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                    *reinterpret_cast<uint4*>(sDS + kr * 128 + pu * 16) =
+                        make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+                }
+                ptx::fence_proxy_async_smem();
+                ptx::mbar_arrive(ds_full);
+                ptx::mbar_arrive(&q_empty[qs]);
+            }
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------ dQ warpgroup
+        const int wq = warp - 8;
+        const int tr = wq * 32 + lane;             // TMEM lane: head-dim row of dQ^T, key row of dV / dK
+        const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+        uint8_t* stg = smem + C::OFF_DQST + wq * C::DQW_BYTES;
+        int g = 0, it = 0;
+        bool ok = true;
+        for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+            const BwdItem item = bwd_item(args, r);
+            if (!item.valid) continue;
+            const int key = item.kt * C::BK + tr;
+            const size_t orow = (static_cast<size_t>(item.slice) * args.seq_k + key) * D;
+            if (item.q_begin >= args.nq_tiles) {
+                // No query sees these keys: dK = dV = 0.
+                if (key < args.seq_k)
+                    for (int k = 0; k < D; k += 4) {
+                        *reinterpret_cast<float4*>(args.dv + orow + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+                        *reinterpret_cast<float4*>(args.dk + orow + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                continue;
+            }
+            for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
+                if (!__all_sync(0xffffffffu, wait_phase(dq_full, g & 1, wctx, kSiteSFull))) { ok = false; break; }
+                ptx::tc_fence_after();
+                uint32_t v[2][32];
+                ptx::tmem_ld32(tmem + lane_off + C::DQ_COL, v[0]);
+                ptx::tmem_ld32(tmem + lane_off + C::DQ_COL + 32, v[1]);
+                ptx::tc_wait_ld();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(dq_free);
+                if (D == 128 || wq < 2) {
+                    // The previous step's reductions must be done reading the staging.
+                    if (lane == 0) ptx::bulk_wait_group_read<0>();
+                    __syncwarp();
+#pragma unroll
+                    for (int b = 0; b < 2; b++)
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const int pu = u ^ (lane & 7);
+                            *reinterpret_cast<uint4*>(stg + b * 32 * 128 + lane * 128 + pu * 16) =
+                                make_uint4(v[b][4 * u], v[b][4 * u + 1], v[b][4 * u + 2], v[b][4 * u + 3]);
+                        }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        ptx::tma_reduce_add_3d(&tm_dq, stg, qi * C::BQ, wq * 32, item.slice);
+                        ptx::tma_reduce_add_3d(&tm_dq, stg + 32 * 128, qi * C::BQ + 32, wq * 32, item.slice);
+                        ptx::bulk_commit_group();
+                    }
+                }
+            }
+            if (!ok) break;
+            // dV and dK of the item: thread = key row.
+            if (!__all_sync(0xffffffffu, wait_phase(acc_full, it & 1, wctx, kSitePvDone))) break;
+            ptx::tc_fence_after();
+#pragma unroll 1
+            for (int k = 0; k < D / 32; k++) {
+                uint32_t a[32], b[32];
+                ptx::tmem_ld32(tmem + lane_off + C::DV_COL + 32 * k, a);
+                ptx::tmem_ld32(tmem + lane_off + C::DK_COL + 32 * k, b);
+                ptx::tc_wait_ld();
+                if (key < args.seq_k) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        *reinterpret_cast<float4*>(args.dv + orow + 32 * k + i) =
+                            make_float4(__uint_as_float(a[i]), __uint_as_float(a[i + 1]), __uint_as_float(a[i + 2]),
+                                        __uint_as_float(a[i + 3]));
+                        *reinterpret_cast<float4*>(args.dk + orow + 32 * k + i) =
+                            make_float4(__uint_as_float(b[i]) * args.scale, __uint_as_float(b[i + 1]) * args.scale,
+                                        __uint_as_float(b[i + 2]) * args.scale, __uint_as_float(b[i + 3]) * args.scale);
+                    }
+                }
+            }
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(acc_free);
+            it++;
+        }
+        // Shared memory must outlive the reductions that read it.
+        if (lane == 0) ptx::bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- prepare
+// Q (blockIdx.z == 0, 64-row scale tiles) and K (z == 1, 128-row scale
+// tiles) quantised exactly as the forward's pre-pass does (codes, scale
+// tiles with scale 127 on padding rows), plus the dequantised values -- the
+// numbers the forward's MMA multiplied -- as BF16 (exact: 3 significant bits
+// and an exponent inside BF16's range for FP16 input).  One lane per block of
+// 32 elements.
+struct BwdQuantJob {
+    const __half* x;        // [slices][seq][D]
+    uint8_t* codes;         // [slices][seq][D/2]
+    uint8_t* sf;            // [slices][ntiles][512]
+    __nv_bfloat16* deq;     // [slices][seq][D]
+    int seq, tile_rows, tile_shift, ntiles;
+};
+
+template <int kNB>
+__global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq, const BwdQuantJob jk, int ocp_mode)
+{
+    const BwdQuantJob& j = blockIdx.z == 0 ? jq : jk;
+    constexpr int D = kNB * 32;
+    const int64_t slice = blockIdx.y;
+    const int total = j.ntiles * j.tile_rows * kNB;
+    const __half* xs = j.x + slice * j.seq * D;
+    uint8_t* cs = j.codes + slice * j.seq * (D / 2);
+    uint8_t* fs = j.sf + slice * j.ntiles * 512;
+    __nv_bfloat16* ds = j.deq + slice * j.seq * D;
+    // Twice the E2M1 magnitude of code bits 0-2 (0, 1, 2, 3, 4, 6, 8, 12), one
+    // nibble each; bit 3 of a code is the sign.
+    constexpr uint32_t kMag2 = 0xC8643210u;
+    auto mag = [](uint32_t n) { return static_cast<float>((kMag2 >> (4u * (n & 7u))) & 15u) * 0.5f; };
+    for (int blk = blockIdx.x * blockDim.x + threadIdx.x; blk < total; blk += gridDim.x * blockDim.x) {
+        const int b = blk % kNB, r = blk / kNB;
+        uint32_t sb = 127u;
+        if (r < j.seq) {
+            uint4 packed;
+            sb = quantize32<__half>(xs + static_cast<int64_t>(r) * D + b * 32, ocp_mode, packed);
+            if (sb == 255u) sb = 254u;  // as the forward stores it (codes are all zero then)
+            *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (D / 2) + b * 16) = packed;
+            // 2^(sb - 127) exactly (sb 0 is the subnormal 2^-127).
+            const float sc = sb ? __uint_as_float(sb << 23) : __uint_as_float(1u << 22);
+            const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+            uint32_t o[16];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    const uint32_t n0 = (w[k] >> (4 * i)) & 15u, n1 = (w[k] >> (4 * i + 4)) & 15u;
+                    const float v0 = (n0 & 8u ? -mag(n0) : mag(n0)) * sc;
+                    const float v1 = (n1 & 8u ? -mag(n1) : mag(n1)) * sc;
+                    o[4 * k + i / 2] = pack_bf162(v0, v1);
+                }
+            uint4* dst = reinterpret_cast<uint4*>(ds + static_cast<int64_t>(r) * D + b * 32);
+#pragma unroll
+            for (int k = 0; k < 4; k++) dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        }
+        const int tile = r >> j.tile_shift, rr = r & (j.tile_rows - 1);
+        fs[static_cast<int64_t>(tile) * 512 + sf_tile_offset(j.tile_rows, rr, b)] = static_cast<uint8_t>(sb);
+    }
+}
+
+// Per query row: Dd = sum_c dO_c O_c (FP32) and lse2 = lse * log2(e); padding
+// rows up to sq_pad get Dd = 0 and lse2 = +inf (their probabilities are 0).
+// One warp per row, D / 32 elements per lane.
+template <int D, typename OT>
+__global__ void __launch_bounds__(256) bwd_rows_kernel(const __half* __restrict__ dout, const OT* __restrict__ out,
+                                                        const float* __restrict__ lse, float* __restrict__ lse2,
+                                                        float* __restrict__ dd, int seq_q, int sq_pad)
+{
+    const int row = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (row >= sq_pad) return;
+    const int64_t slice = blockIdx.y;
+    const int64_t o = slice * sq_pad + row;
+    if (row >= seq_q) {
+        if (lane == 0) {
+            dd[o] = 0.f;
+            lse2[o] = INFINITY;
+        }
+        return;
+    }
+    const int64_t base = (slice * seq_q + row) * D;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < D / 32; k++) {
+        const int col = lane + 32 * k;
+        float ov;
+        if constexpr (sizeof(OT) == 4) ov = out[base + col];
+        else ov = __half2float(out[base + col]);
+        acc = fmaf(__half2float(dout[base + col]), ov, acc);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    if (lane == 0) {
+        dd[o] = acc;
+        lse2[o] = lse[slice * seq_q + row] * 1.4426950408889634f;
+    }
+}
+
+// dQ[slice][q][c] = scale * acc[slice][c][q] for q < seq_q: 32 x 32 tiles
+// transposed through shared memory.
+__global__ void __launch_bounds__(256) bwd_dq_kernel(const float* __restrict__ acc, float* __restrict__ dq, int seq_q,
+                                                      int sq_pad, int d, float scale)
+{
+    __shared__ float t[32][33];
+    const int64_t slice = blockIdx.z;
+    const int q0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    for (int i = ty; i < 32; i += 8) t[i][tx] = acc[(slice * d + c0 + i) * sq_pad + q0 + tx];
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int q = q0 + i;
+        if (q < seq_q) dq[(slice * seq_q + q) * d + c0 + tx] = t[tx][i] * scale;
+    }
+}
+
+}  // namespace fp4attn

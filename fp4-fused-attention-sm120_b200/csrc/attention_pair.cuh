@@ -143,7 +143,14 @@ struct PairArgs {
     // the scale rule (1: the OCP "/6" rule).
     const __half* q_in;
     int ocp_mode;
+    // kLse: per query row ln(sum_j exp(scale * S_ij)) -- the row's reference
+    // max and row sum as one number -- for the backward pass, [slices][seq_q].
+    // A row that sees no key gets +inf (its probabilities are all zero).
+    float* lse;
 };
+
+// ln(2): the log-sum-exp leaves the kernel in natural-log units.
+constexpr float kLn2 = 0.693147180559945309f;
 
 // Work item r of this CTA's static schedule: (slice, query-tile pair) and its
 // number of 64-key steps.  Without a mask items go in slice order (a slice's
@@ -211,6 +218,9 @@ struct PairRegs {
     static_assert((kCtl + 2 * kSm) * 32 <= 16384, "register split exceeds a sub-partition");
 };
 
+// kLse (fp4attn_forward_lse): the epilogue also writes each query row's
+// log-sum-exp (args.lse), which the backward pass needs to rebuild the
+// normalised probabilities.
 // kWithhold (test instantiation only): the first softmax thread never makes
 // its first s_free arrival, so the S issuer's bounded wait for step 1 runs out
 // and the kernel's own abort path runs: every role leaves its loop, in-flight
@@ -223,7 +233,7 @@ struct PairRegs {
 // for bit (the same encoder, quantize.cuh), written in the TMA's swizzled
 // layout.  Only the large-problem schedule (kSmall false) has this variant.
 template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false,
-          bool kFuseQ = false>
+          bool kFuseQ = false, bool kLse = false>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fp4_attention_pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -652,6 +662,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             };
             if (args.kparts == 1) {
                 const float inv_l = lv > 0.f ? 1.0f / lv : 0.f;  // a row that saw no key outputs 0
+                if constexpr (kLse) {
+                    if (trow0 + row < args.seq_q)
+                        args.lse[static_cast<size_t>(item.slice) * args.seq_q + trow0 + row] =
+                            lv > 0.f ? (m_ref + log2f(lv)) * kLn2 : INFINITY;
+                }
                 store_rows(from_tmem, std::false_type{}, &tm_o, trow0 + wq * 32, item.slice, inv_l);
                 return true;
             }
@@ -723,6 +738,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 const float row_inv = lsum_all > 0.f ? 1.0f / lsum_all : 0.f;  // a row that saw no key outputs 0
 #pragma unroll
                 for (int pp = 0; pp < kMaxKParts; pp++) wgt[pp] *= row_inv;
+                if constexpr (kLse) {
+                    if (trow0 + wq * 32 + lane < args.seq_q)
+                        args.lse[static_cast<size_t>(item.slice) * args.seq_q + trow0 + wq * 32 + lane] =
+                            lsum_all > 0.f ? (row_m + log2f(lsum_all)) * kLn2 : INFINITY;
+                }
             }
             constexpr int CPL = D / 32;            // output columns per lane
             constexpr int RB = CPL >= 3 ? 4 : 8;   // rows per batch
@@ -930,6 +950,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 ptx::tc_wait_ld();
                 const float lv = __uint_as_float(lsum[0]);
                 const float inv_l = lv > 0.f ? 1.0f / lv : 0.f;  // a row that saw no key outputs 0
+                if constexpr (kLse) {
+                    const int grow = pair * 2 * C::BM + t * C::BM + row;
+                    if (grow < args.seq_q)
+                        args.lse[static_cast<size_t>(slice) * args.seq_q + grow] =
+                            lv > 0.f ? (m + log2f(lv)) * kLn2 : INFINITY;
+                }
                 // O / l in 32-column chunks: each warp writes its 32 rows x 32
                 // columns to a staging buffer (swizzled like the TMA box, so the
                 // 16-byte writes of a warp hit distinct banks) and lane 0 stores

@@ -1,0 +1,227 @@
+// backward_api.cuh -- fp4attn_backward and fp4attn_backward_workspace_size:
+// the gradient of the FP4 fused attention (attention_bwd.cuh) behind the C
+// ABI.  Included once, at the end of fp4attn.cu: the kernels share that
+// translation unit's device error word (fp4attn_status_query) and its host
+// helpers (fp4attn::host).
+//
+// Launches, in stream order: the quantiser with dequantised BF16 copies of Q
+// and K, the per-row Dd / lse2 pass, a clear of the dQ accumulator, the
+// backward kernel, and the dQ transpose.  The workspace holds everything but
+// the caller's inputs and outputs.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <cstdarg>
+
+#include "attention_bwd.cuh"
+
+namespace fp4attn_bwd {
+
+namespace host = fp4attn::host;
+
+constexpr int kBwdMaxDevices = 64;
+
+bool bwd_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int failf(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int failf(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    return host::error(code, buf);
+}
+
+#define BWD_CUDA(call)                                                                                \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess) return failf(FP4ATTN_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+struct BwdWorkspace {
+    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, dq_acc, total;
+};
+
+struct BwdShape {
+    int64_t slices;
+    int sq, sk, d, sq_pad, nq, nk;
+};
+
+BwdShape bwd_shape(int batch, int heads, int sq, int sk, int d)
+{
+    BwdShape s;
+    s.slices = static_cast<int64_t>(batch) * heads;
+    s.sq = sq;
+    s.sk = sk;
+    s.d = d;
+    s.nq = (sq + 63) / 64;
+    s.nk = (sk + 127) / 128;
+    s.sq_pad = s.nq * 64;
+    return s;
+}
+
+BwdWorkspace plan_bwd_workspace(const BwdShape& s)
+{
+    BwdWorkspace w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = (off + bytes + 255) / 256 * 256;
+        return at;
+    };
+    const size_t n = static_cast<size_t>(s.slices);
+    w.q_codes = take(n * s.sq * (s.d / 2));
+    w.k_codes = take(n * s.sk * (s.d / 2));
+    w.q_sf = take(n * s.nq * 512);
+    w.k_sf = take(n * s.nk * 512);
+    w.qq = take(n * s.sq * s.d * 2);
+    w.kq = take(n * s.sk * s.d * 2);
+    w.lse2 = take(n * s.sq_pad * 4);
+    w.dd = take(n * s.sq_pad * 4);
+    w.dq_acc = take(n * s.d * s.sq_pad * 4);
+    w.total = off;
+    return w;
+}
+
+template <int D>
+int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, const void* Out, int out_dtype,
+               const void* dOut, const float* lse, float* dQ, float* dK, float* dV, float scale, int ocp, bool causal,
+               uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+{
+    using C = fp4attn::BwdCfg<D>;
+    // 1. Q and K: codes, scale tiles and BF16 dequantised copies.
+    fp4attn::BwdQuantJob jq{static_cast<const __half*>(Q), ws + w.q_codes, ws + w.q_sf,
+                            reinterpret_cast<__nv_bfloat16*>(ws + w.qq), s.sq, 64, 6, s.nq};
+    fp4attn::BwdQuantJob jk{static_cast<const __half*>(K), ws + w.k_codes, ws + w.k_sf,
+                            reinterpret_cast<__nv_bfloat16*>(ws + w.kq), s.sk, 128, 7, s.nk};
+    {
+        const int64_t per_slice = std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (D / 32);
+        const int gx = static_cast<int>(
+            std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / s.slices + 1)));
+        fp4attn::bwd_quantize_kernel<D / 32><<<dim3(gx, static_cast<unsigned>(s.slices), 2), 256, 0, st>>>(jq, jk, ocp);
+        BWD_CUDA(cudaGetLastError());
+    }
+    // 2. Dd and lse2 per query row.
+    float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
+    float* dd = reinterpret_cast<float*>(ws + w.dd);
+    {
+        const dim3 grid((s.sq_pad + 7) / 8, static_cast<unsigned>(s.slices));
+        if (out_dtype == FP4ATTN_F32)
+            fp4attn::bwd_rows_kernel<D, float><<<grid, 256, 0, st>>>(
+                static_cast<const __half*>(dOut), static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+        else
+            fp4attn::bwd_rows_kernel<D, __half><<<grid, 256, 0, st>>>(
+                static_cast<const __half*>(dOut), static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+        BWD_CUDA(cudaGetLastError());
+    }
+    // 3. The dQ accumulator starts at zero.
+    float* dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
+    BWD_CUDA(cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(s.slices) * D * s.sq_pad * 4, st));
+    // 4. The backward kernel.
+    CUtensorMap tk, tq, tv, tkq, tdo, tqq, tdq;
+    int rc;
+    const uint64_t n = static_cast<uint64_t>(s.slices);
+    if ((rc = host::map3d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, D / 2, s.sk, n, D / 2, 128, D / 2)) ||
+        (rc = host::map3d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.q_codes, D / 2, s.sq, n, D / 2, 64, D / 2)) ||
+        (rc = host::map3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, V, D, s.sk, n, 64, 128, 128)) ||
+        (rc = host::map3d(&tkq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.kq, D, s.sk, n, 64, 128, 128)) ||
+        (rc = host::map3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dOut, D, s.sq, n, 64, 64, 128)) ||
+        (rc = host::map3d(&tqq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.qq, D, s.sq, n, 64, 64, 128)) ||
+        (rc = host::map3d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dq_acc, s.sq_pad, D, n, 32, 32, 128)))
+        return rc;
+    fp4attn::BwdArgs a;
+    a.seq_q = s.sq;
+    a.seq_k = s.sk;
+    a.sq_pad = s.sq_pad;
+    a.nq_tiles = s.nq;
+    a.nk_tiles = s.nk;
+    a.slices = static_cast<int>(s.slices);
+    const int64_t items = s.slices * s.nk;
+    if (items > INT32_MAX) return failf(FP4ATTN_EINVAL, "too many key tiles");
+    a.n_items = static_cast<int>(items);
+    a.scale = scale;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.q_sf = ws + w.q_sf;
+    a.k_sf = ws + w.k_sf;
+    a.lse2 = lse2;
+    a.dd = dd;
+    a.dk = dK;
+    a.dv = dV;
+    a.timeout_ns = host::timeout_ns();
+    a.causal = causal ? 1 : 0;
+    a.causal_off = s.sk - s.sq;
+    auto kern = fp4attn::fp4_attention_bwd_kernel<D>;
+    static std::atomic<unsigned long long> smem_ctx[kBwdMaxDevices]{};
+    int dev = 0;
+    BWD_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kBwdMaxDevices) return failf(FP4ATTN_EUNSUPPORTED, "device index %d", dev);
+    const unsigned long long ctx = fp4attn::current_context_id();
+    if (ctx == 0 || smem_ctx[dev].load(std::memory_order_acquire) != ctx) {
+        BWD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+        smem_ctx[dev].store(ctx, std::memory_order_release);
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, host::sms()));
+    kern<<<grid, 384, C::SMEM_BYTES, st>>>(tk, tq, tv, tkq, tdo, tqq, tdq, a);
+    BWD_CUDA(cudaGetLastError());
+    // 5. dQ = scale * transpose(accumulator).
+    fp4attn::bwd_dq_kernel<<<dim3(s.sq_pad / 32, D / 32, static_cast<unsigned>(s.slices)), 256, 0, st>>>(
+        dq_acc, dQ, s.sq, s.sq_pad, D, scale);
+    BWD_CUDA(cudaGetLastError());
+    return FP4ATTN_OK;
+}
+
+}  // namespace fp4attn_bwd
+
+extern "C" {
+
+size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim)
+{
+    using namespace fp4attn_bwd;
+    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || (head_dim != 64 && head_dim != 128)) return 0;
+    return plan_bwd_workspace(bwd_shape(batch, heads, seq_q, seq_k, head_dim)).total;
+}
+
+int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
+                     float* dQ, float* dK, float* dV, int out_dtype, int batch, int heads, int seq_q, int seq_k,
+                     int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
+                     size_t workspace_bytes, void* stream)
+{
+    using namespace fp4attn_bwd;
+    fp4attn::set_error_detail("");
+    if (!Q || !K || !V || !Out || !dOut || !lse || !dQ || !dK || !dV) return failf(FP4ATTN_EINVAL, "null pointer");
+    if (!bwd_aligned16(Q) || !bwd_aligned16(K) || !bwd_aligned16(V) || !bwd_aligned16(Out) || !bwd_aligned16(dOut) || !bwd_aligned16(dQ) ||
+        !bwd_aligned16(dK) || !bwd_aligned16(dV) || (reinterpret_cast<uintptr_t>(lse) & 3u))
+        return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned (lse 4-byte)");
+    if (out_dtype != FP4ATTN_F32 && out_dtype != FP4ATTN_F16) return failf(FP4ATTN_EINVAL, "out_dtype %d", out_dtype);
+    if (scale_mode != FP4ATTN_SCALE_REFERENCE && scale_mode != FP4ATTN_SCALE_OCP)
+        return failf(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
+    if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
+        return failf(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
+    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1)
+        return failf(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads,
+                     seq_q, seq_k);
+    if (head_dim != 64 && head_dim != 128)
+        return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 64 and 128 (got %d)", head_dim);
+    if (static_cast<int64_t>(batch) * heads > 65535) return failf(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
+    const BwdShape s = bwd_shape(batch, heads, seq_q, seq_k, head_dim);
+    const BwdWorkspace w = plan_bwd_workspace(s);
+    if (!workspace || workspace_bytes < w.total)
+        return failf(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w.total,
+                     workspace ? workspace_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return failf(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
+    int rc = host::ready();
+    if (rc) return rc;
+    const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+    const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
+    const bool causal = mask_mode == FP4ATTN_MASK_CAUSAL;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (head_dim == 64)
+        return launch_bwd<64>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, dK, dV, scale, ocp, causal, ws, w, st);
+    return launch_bwd<128>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, dK, dV, scale, ocp, causal, ws, w, st);
+}
+
+}  // extern "C"

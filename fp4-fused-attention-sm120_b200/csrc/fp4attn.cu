@@ -503,12 +503,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 }
 
 template <int D, typename OutT, int kPoly8, bool kSpec, bool kSmall = false, bool kWithhold = false,
-          bool kFuseQ = false>
+          bool kFuseQ = false, bool kLse = false>
 int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& fa,
                      int64_t slices, cudaStream_t st)
 {
     using C = fp4attn::PairCfg<D, kFuseQ ? 2 : 1>;
-    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall, kWithhold, kFuseQ>;
+    auto kern = fp4attn::fp4_attention_pair_kernel<D, OutT, kPoly8, kSpec, kSmall, kWithhold, kFuseQ, kLse>;
     static std::atomic<int> launch_regs_cache{-1};
     int launch_regs = launch_regs_cache.load(std::memory_order_relaxed);
     if (launch_regs < 0) {
@@ -544,6 +544,7 @@ int launch_pair_poly(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     a.part_count = fa.part_count;
     a.q_in = static_cast<const __half*>(fa.q_in);
     a.ocp_mode = fa.ocp_mode;
+    a.lse = fa.lse;
     // Output written by TMA stores in 32-row x 32-column boxes (64-byte rows
     // for FP16, 128-byte rows for FP32, swizzled to match the staging).
     CUtensorMap to;
@@ -574,6 +575,16 @@ template <int D, typename OutT>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                 int64_t slices, cudaStream_t st)
 {
+    // The forward that also writes the log-sum-exp rows (head_dim 64 and 128,
+    // the backward pass's head dims).
+    if constexpr (D == 64 || D == 128) {
+        if (a.lse) {
+            if (a.qtiles == 1 || a.kparts > 1)
+                return launch_pair_poly<D, OutT, 3, true, true, false, false, true>(tq, tk, tv, a, slices, st);
+            return launch_pair_poly<D, OutT, 3, true, false, false, false, true>(tq, tk, tv, a, slices, st);
+        }
+    }
+    if (a.lse) return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128");
     // Q quantised inside the attention kernel (the large-problem schedule).
     if (a.q_in) return launch_pair_poly<D, OutT, 3, true, false, false, true>(tq, tk, tv, a, slices, st);
     // One query tile per item or key partitions: the small-problem kernel.
@@ -701,7 +712,7 @@ int do_prepare(const void* Q, const void* K, const void* V, int in_dtype, int ba
 int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, int heads, int sq, int sk, int d,
               float softmax_scale, const void* workspace, size_t ws_bytes, void* stream, bool scores,
               int mask_mode = FP4ATTN_MASK_NONE, unsigned long long test_timeout_ns = 0, const void* q_in = nullptr,
-              int ocp_mode = 0)
+              int ocp_mode = 0, float* lse = nullptr)
 {
     if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
         return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
@@ -759,6 +770,9 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     }
     a.q_in = q_in;
     a.ocp_mode = ocp_mode;
+    a.lse = lse;
+    if (lse && !(d == 64 || d == 128))
+        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128 (got %d)", d);
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
     if (test_timeout_ns) {
         if (d != 64 || out_dtype != FP4ATTN_F32 || a.qtiles != 2 || a.kparts != 1 || a.causal)
@@ -776,6 +790,20 @@ namespace fp4attn {
 // Lets other translation units of the library report a detail through
 // fp4attn_last_error().
 void set_error_detail(const char* msg) { g_last_error = msg; }
+
+// The host helpers above, for the library's other translation units
+// (backward.cu).
+namespace host {
+int error(int code, const char* msg) { return fail(code, "%s", msg); }
+int ready() { return device_ready(); }
+int sms() { return device_sms(); }
+unsigned long long timeout_ns() { return wait_timeout_ns(); }
+int map3d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner, uint64_t rows,
+          uint64_t slices, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes)
+{
+    return make_map_3d(m, dt, elem_bytes, base, inner, rows, slices, box_inner, box_rows, swizzle_for(swizzle_bytes));
+}
+}  // namespace host
 }  // namespace fp4attn
 
 extern "C" {
@@ -900,6 +928,25 @@ int fp4attn_forward_masked(const void* Q, const void* K, const void* V, void* Ou
                      workspace_bytes, stream, false, mask_mode);
 }
 
+int fp4attn_forward_lse(const void* Q, const void* K, const void* V, void* Out, float* lse, int in_dtype,
+                        int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                        int scale_mode, int mask_mode, void* workspace, size_t workspace_bytes, void* stream)
+{
+    g_last_error.clear();
+    if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
+        return fail(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
+    if (!lse || (reinterpret_cast<uintptr_t>(lse) & 3u)) return fail(FP4ATTN_EINVAL, "lse must be a 4-byte aligned pointer");
+    int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, true);
+    if (rc) return rc;
+    if (head_dim != 64 && head_dim != 128)
+        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128 (got %d)", head_dim);
+    if ((rc = do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
+                         workspace_bytes, stream, true)))
+        return rc;
+    return do_attend(V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, softmax_scale, workspace,
+                     workspace_bytes, stream, false, mask_mode, 0, nullptr, 0, lse);
+}
+
 int fp4attn_debug_scores(const void* Q, const void* K, float* S, int in_dtype, int batch, int heads, int seq_q,
                          int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes,
                          void* stream)
@@ -989,3 +1036,6 @@ int fp4attn_supported_head_dims(int* dims, int cap)
 }
 
 }  // extern "C"
+
+// The backward pass (its kernels and C entry points) in this translation unit.
+#include "backward_api.cuh"

@@ -111,6 +111,19 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
                  : "memory");
 }
 
+// 3-D tiled reduction from this CTA's shared memory into global memory:
+// global += tile, element-wise, in the tensor map's type (FP32 add here);
+// elements outside the tensor are skipped.  Completion is tracked per thread
+// with bulk groups, like tma_store_3d.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const void* src, int c0, int c1, int c2)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(m)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until at most N of this thread's bulk groups still read shared memory.
@@ -305,6 +318,16 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major)
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::f16 with every field given: operand formats
+// (0 = F16, 1 = BF16; A and B always the same), A and B major-ness (false:
+// K-major, true: MN-major), F32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_f16x(int M, int N, uint32_t ab_format, bool a_mn_major, bool b_mn_major)
+{
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
+           (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // D[tmem] (+)= A[smem] x B[smem] with per-32 block scales read from TMEM.
 __device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate)
@@ -326,6 +349,18 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// D[tmem] (+)= A[smem] x B[smem], 16-bit operands (F16 or BF16, as the
+// instruction descriptor says), FP32 accumulator.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Eight floats to eight E2M1 codes (round to nearest even, saturating),

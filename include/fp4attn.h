@@ -177,6 +177,35 @@ int fp4attn_forward_noalloc(const void* Q, const void* K, const void* V, void* O
                             int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
                             int scale_mode, void* stream);
 
+/* fp4attn_forward_masked that also writes, per query row, the natural-log
+ * log-sum-exp of the scaled scores, lse[b][h][i] = ln(sum_j exp(scale * S_ij))
+ * over the keys the row sees (FP32 [batch, heads, seq_q]; +inf for a row that
+ * sees no key) -- the statistic the backward pass rebuilds the probabilities
+ * from.  head_dim 64 and 128.  Same workspace as fp4attn_forward.  No
+ * counterpart in the reference (forward only; its row max and sum stay in
+ * registers, common.h:228-265). */
+int fp4attn_forward_lse(const void* Q, const void* K, const void* V, void* Out, float* lse, int in_dtype,
+                        int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
+                        int scale_mode, int mask_mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes fp4attn_backward needs for this shape (0 if unsupported). */
+size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim);
+
+/* Gradient of the FP4 fused attention.  Inputs: the forward's FP16 Q, K, V
+ * and dOut (the gradient of Out), its output Out (out_dtype FP16 or FP32) and
+ * the lse rows of fp4attn_forward_lse (same shape, scale, scale_mode and
+ * mask).  Outputs: FP32 dQ, dK, dV in the layout of Q, K, V.  The quantiser
+ * is treated as a straight-through estimator: with Qq, Kq the dequantised
+ * codes the forward multiplied and P its probabilities,
+ *   dV = P^T dOut,  dZ = P o (dOut V^T - rowsum(dOut o Out)),
+ *   dQ = scale * dZ Kq,  dK = scale * dZ^T Qq.
+ * head_dim 64 and 128.  Every byte of dQ, dK and dV is written.  No
+ * counterpart in the reference, which is inference-only. */
+int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
+                     float* dQ, float* dK, float* dV, int out_dtype, int batch, int heads, int seq_q, int seq_k,
+                     int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
  * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
  * power-of-two scales are exact, S is checkable bit for bit.

@@ -46,6 +46,9 @@ def oracle_lib() -> ctypes.CDLL:
         L.oracle_fp4_attention_slice.argtypes = ([_f32, _f32, _f32, _f32] + [c.c_int] * 3 +
                                                  [c.c_float, c.c_int, c.c_int])
         L.oracle_fp4_scores.argtypes = [_f32, _f32, _f32, c.c_int, c.c_int, c.c_int, c.c_int]
+        L.oracle_fp4_attention_backward.argtypes = ([_f32] * 7 + [c.c_int] * 4 + [c.c_float] +
+                                                    [c.c_int] * 3)
+        L.oracle_fp4_attention_lse.argtypes = [_f32, _f32, _f32] + [c.c_int] * 4 + [c.c_float, c.c_int, c.c_int]
         L.oracle_cosine.argtypes = [_f32, _f32, c.c_int64]
         L.oracle_cosine.restype = c.c_double
         _o = L
@@ -144,6 +147,33 @@ def fp4_attention_rows(Q, K, V, slice_of, rows, scale: float = 0.0, scale_mode: 
     r = _c(rows, np.int32)
     out = np.zeros((len(s), d), np.float32)
     oracle_lib().oracle_fp4_attention_rows(Q, K, V, out, len(s), s, r, sq, sk, d, scale, scale_mode)
+    return out
+
+
+def fp4_attention_backward(Q, K, V, dO, scale: float = 0.0, scale_mode: int = 0, causal: bool = False,
+                           threads: int = 0):
+    """Gradient of the FP4 path (the quantiser as a straight-through
+    estimator) for [slices, seq, head_dim] (or [B, H, seq, head_dim]) inputs:
+    returns (dQ, dK, dV) as float32 arrays shaped like Q, K, V."""
+    import os
+    Q, K, V, dO = _c(Q), _c(K), _c(V), _c(dO)
+    d = Q.shape[-1]
+    sq, sk = Q.shape[-2], K.shape[-2]
+    slices = Q.size // (sq * d)
+    dQ, dK, dV = np.zeros(Q.shape, np.float32), np.zeros(K.shape, np.float32), np.zeros(V.shape, np.float32)
+    oracle_lib().oracle_fp4_attention_backward(Q, K, V, dO, dQ, dK, dV, slices, sq, sk, d, scale, scale_mode,
+                                               int(causal), threads or os.cpu_count() or 1)
+    return dQ, dK, dV
+
+
+def fp4_attention_lse(Q, K, scale: float = 0.0, scale_mode: int = 0, causal: bool = False):
+    """Per query row ln(sum_j exp(scale * Qq_i . Kq_j)) -> [..., seq_q] float32."""
+    Q, K = _c(Q), _c(K)
+    d = Q.shape[-1]
+    sq, sk = Q.shape[-2], K.shape[-2]
+    slices = Q.size // (sq * d)
+    out = np.zeros(Q.shape[:-1], np.float32)
+    oracle_lib().oracle_fp4_attention_lse(Q, K, out, slices, sq, sk, d, scale, scale_mode, int(causal))
     return out
 
 

@@ -316,3 +316,153 @@ double oracle_cosine(const float* a, const float* b, int64_t n)
     }
     return dot / (sqrt(na) * sqrt(nb) + 1e-30);
 }
+
+/* ------------------------------------------------------------------ backward
+ * Not part of the reference, which is forward only (common.h:68-328 has no
+ * gradient path).  The gradient of the FP4 path above with the quantiser as a
+ * straight-through estimator: with Qq, Kq the dequantised Q, K (quant_dequant,
+ * i.e. common.h:21-48 and :115-123 / :160-168 followed by dequantisation),
+ * z = scale * Qq Kq^T over the visible keys, P = softmax(z) row-wise:
+ *   dV = P^T dO,  dP = dO V^T,  Dd_i = sum_j P_ij dP_ij,
+ *   dZ = P o (dP - Dd),  dQ = scale * dZ Kq,  dK = scale * dZ^T Qq.
+ * Everything is accumulated in double.  Dd_i = sum_j P_ij dP_ij equals
+ * sum_c dO_ic O_ic for the exact O = P V. */
+
+typedef struct {
+    const float *qd, *kd, *V, *dO;
+    float* dQ;
+    double *dK, *dV;     /* this job's private accumulators [sk][d] */
+    int r0, r1, sq, sk, d, causal;
+    double scale;
+} bwd_job;
+
+static void* run_bwd_rows(void* arg)
+{
+    bwd_job* j = (bwd_job*)arg;
+    const int sk = j->sk, d = j->d;
+    double* p = (double*)malloc(sizeof(double) * (size_t)(sk > 0 ? sk : 1));
+    double* dp = (double*)malloc(sizeof(double) * (size_t)(sk > 0 ? sk : 1));
+    double* dq = (double*)malloc(sizeof(double) * (size_t)d);
+    for (int i = j->r0; i < j->r1; i++) {
+        long lim = sk;
+        if (j->causal) {
+            lim = (long)i + sk - j->sq + 1;
+            if (lim > sk) lim = sk;
+        }
+        const float* q = j->qd + (size_t)i * d;
+        const float* go = j->dO + (size_t)i * d;
+        for (int c = 0; c < d; c++) dq[c] = 0.0;
+        if (lim > 0) {
+            double m = -INFINITY;
+            for (long k = 0; k < lim; k++) {
+                const float* kr = j->kd + (size_t)k * d;
+                double a = 0.0;
+                for (int c = 0; c < d; c++) a += (double)q[c] * kr[c];
+                p[k] = a * j->scale;
+                if (p[k] > m) m = p[k];
+            }
+            double sum = 0.0;
+            for (long k = 0; k < lim; k++) { p[k] = exp(p[k] - m); sum += p[k]; }
+            double dd = 0.0;
+            for (long k = 0; k < lim; k++) {
+                p[k] /= sum;
+                const float* vr = j->V + (size_t)k * d;
+                double a = 0.0;
+                for (int c = 0; c < d; c++) a += (double)go[c] * vr[c];
+                dp[k] = a;
+                dd += p[k] * a;
+            }
+            for (long k = 0; k < lim; k++) {
+                const double dz = p[k] * (dp[k] - dd);
+                const float* kr = j->kd + (size_t)k * d;
+                double* dkr = j->dK + (size_t)k * d;
+                double* dvr = j->dV + (size_t)k * d;
+                for (int c = 0; c < d; c++) {
+                    dq[c] += dz * kr[c];
+                    dkr[c] += dz * q[c];
+                    dvr[c] += p[k] * go[c];
+                }
+            }
+        }
+        for (int c = 0; c < d; c++) j->dQ[(size_t)i * d + c] = (float)(dq[c] * j->scale);
+    }
+    free(p); free(dp); free(dq);
+    return NULL;
+}
+
+void oracle_fp4_attention_backward(const float* Q, const float* K, const float* V, const float* dO,
+                                   float* dQ, float* dK, float* dV, int slices, int sq, int sk, int d,
+                                   float scale, int mode, int causal, int threads)
+{
+    const double sc = scale > 0.f ? (double)scale : 1.0 / sqrt((double)d);
+    const size_t qn = (size_t)sq * d, kn = (size_t)sk * d;
+    if (threads < 1) threads = 1;
+    if (threads > sq) threads = sq;
+    float* qd = (float*)malloc(sizeof(float) * qn);
+    float* kd = (float*)malloc(sizeof(float) * kn);
+    double* acc = (double*)malloc(sizeof(double) * kn * 2 * (size_t)threads);
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * threads);
+    bwd_job* jobs = (bwd_job*)malloc(sizeof(bwd_job) * threads);
+    for (int s = 0; s < slices; s++) {
+        quant_dequant(Q + s * qn, sq, d, mode, qd);
+        quant_dequant(K + s * kn, sk, d, mode, kd);
+        memset(acc, 0, sizeof(double) * kn * 2 * (size_t)threads);
+        for (int t = 0; t < threads; t++) {
+            bwd_job jb = {qd, kd, V + s * kn, dO + s * qn, dQ + s * qn, acc + kn * 2 * t, acc + kn * (2 * t + 1),
+                          (int)((int64_t)sq * t / threads), (int)((int64_t)sq * (t + 1) / threads), sq, sk, d,
+                          causal, sc};
+            jobs[t] = jb;
+            pthread_create(&tid[t], NULL, run_bwd_rows, &jobs[t]);
+        }
+        for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+        for (size_t e = 0; e < kn; e++) {
+            double gk = 0.0, gv = 0.0;
+            for (int t = 0; t < threads; t++) {
+                gk += acc[kn * 2 * t + e];
+                gv += acc[kn * (2 * t + 1) + e];
+            }
+            dK[s * kn + e] = (float)(gk * sc);
+            dV[s * kn + e] = (float)gv;
+        }
+    }
+    free(qd); free(kd); free(acc); free(tid); free(jobs);
+}
+
+/* Per query row, ln(sum_j exp(scale * Qq_i . Kq_j)) over the visible keys (in
+ * double; +inf for a row that sees no key): the statistic the forward returns
+ * for the backward pass. */
+void oracle_fp4_attention_lse(const float* Q, const float* K, float* lse, int slices, int sq, int sk, int d,
+                              float scale, int mode, int causal)
+{
+    const double sc = scale > 0.f ? (double)scale : 1.0 / sqrt((double)d);
+    const size_t qn = (size_t)sq * d, kn = (size_t)sk * d;
+    float* qd = (float*)malloc(sizeof(float) * qn);
+    float* kd = (float*)malloc(sizeof(float) * kn);
+    double* z = (double*)malloc(sizeof(double) * (size_t)(sk > 0 ? sk : 1));
+    for (int s = 0; s < slices; s++) {
+        quant_dequant(Q + s * qn, sq, d, mode, qd);
+        quant_dequant(K + s * kn, sk, d, mode, kd);
+        for (int i = 0; i < sq; i++) {
+            long lim = sk;
+            if (causal) {
+                lim = (long)i + sk - sq + 1;
+                if (lim > sk) lim = sk;
+            }
+            if (lim <= 0) {
+                lse[(size_t)s * sq + i] = INFINITY;
+                continue;
+            }
+            double m = -INFINITY;
+            for (long k = 0; k < lim; k++) {
+                double a = 0.0;
+                for (int c = 0; c < d; c++) a += (double)qd[(size_t)i * d + c] * kd[(size_t)k * d + c];
+                z[k] = a * sc;
+                if (z[k] > m) m = z[k];
+            }
+            double sum = 0.0;
+            for (long k = 0; k < lim; k++) sum += exp(z[k] - m);
+            lse[(size_t)s * sq + i] = (float)(m + log(sum));
+        }
+    }
+    free(qd); free(kd); free(z);
+}

@@ -99,6 +99,22 @@ void oracle_fp4_attention_slice(const float* Q, const float* K, const float* V, 
 void oracle_fp4_scores(const float* Q, const float* K, float* S,
                        int seq_q, int seq_k, int head_dim, int scale_mode);
 
+/* Gradient of the FP4 path (not part of the reference, which is forward
+ * only), the quantiser taken as a straight-through estimator: for `slices`
+ * contiguous slices, dQ = scale dZ Kq, dK = scale dZ^T Qq, dV = P^T dO with
+ * dZ = P o (dO V^T - rowsum(P o dO V^T)), Qq / Kq the dequantised codes and
+ * P = softmax(scale Qq Kq^T) (causal != 0: the mask of
+ * oracle_attention_causal).  Double accumulation; each slice's query rows are
+ * split over up to `threads` POSIX threads. */
+void oracle_fp4_attention_backward(const float* Q, const float* K, const float* V, const float* dO,
+                                   float* dQ, float* dK, float* dV, int slices, int seq_q, int seq_k, int head_dim,
+                                   float scale, int scale_mode, int causal, int threads);
+
+/* Per query row the natural-log log-sum-exp of scale * Qq Kq^T over the
+ * visible keys (+inf when a row sees none), [slices][seq_q]. */
+void oracle_fp4_attention_lse(const float* Q, const float* K, float* lse, int slices, int seq_q, int seq_k,
+                              int head_dim, float scale, int scale_mode, int causal);
+
 /* cosine_similarity (tests/test_attention.cu:56-65), accumulated in double. */
 double oracle_cosine(const float* a, const float* b, int64_t n);
 

@@ -1,0 +1,160 @@
+"""GPU backward pass (fp4attn_backward) and the forward's log-sum-exp output
+(fp4attn_forward_lse) against the oracle.
+
+The reference is forward only; the oracle's backward
+(oracle_fp4_attention_backward) is pinned against float64 torch autograd on
+the reference-quantised operands in test_oracle_backward.py.
+
+Tolerance (written here): per gradient tensor, cosine with the oracle
+>= 0.9999 (double) and max |gpu - oracle| <= 1e-2 * max |oracle|.  The GPU
+rounds P to FP16 and dZ to BF16 for the tensor cores (relative steps of 2^-11
+and 2^-8 per element); the oracle keeps everything in double.  The
+log-sum-exp is within 2e-3 (absolute) of the oracle's: the forward sums its
+FP16-rounded probabilities."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+REL_MAX = 1e-2
+LSE_ABS = 2e-3
+
+
+def _inputs(seed, B, H, sq, sk, d):
+    g = torch.Generator().manual_seed(seed)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g).half() for s in (sq, sk, sk))
+    dO = torch.randn(B, H, sq, d, generator=g).half()
+    return Q, K, V, dO
+
+
+def _np(t):
+    return t.float().cpu().numpy().reshape(-1, t.shape[-2], t.shape[-1])
+
+
+def _assert_grad(got, want, what):
+    got = got.float().cpu().numpy().reshape(want.shape)
+    assert np.isfinite(got).all(), what
+    cos = oracle.cosine(got, want)
+    rel = float(np.abs(got - want).max()) / max(float(np.abs(want).max()), 1e-30)
+    assert cos >= COS_MIN and rel <= REL_MAX, (what, cos, rel)
+
+
+def _run(fa, shape, causal, out_dtype=torch.float16, seed=0):
+    B, H, sq, sk, d = shape
+    Q, K, V, dO = _inputs(seed, B, H, sq, sk, d)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, out_dtype=out_dtype, causal=causal)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse, causal=causal)
+    assert fa.status_query() == fa.OK
+    return (Q, K, V, dO), out, lse, (dq, dk, dv)
+
+
+SHAPES = [
+    (1, 2, 256, 256, 128),    # whole tiles
+    (1, 2, 200, 333, 64),     # ragged seq_q and seq_k
+    (2, 1, 64, 640, 128),     # one query tile, several key tiles
+    (1, 2, 320, 130, 128),    # seq_k just past one key tile
+    (1, 1, 1, 1, 64),         # one query, one key
+]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_backward_matches_oracle(fa, cuda, shape, causal):
+    (Q, K, V, dO), _, _, (dq, dk, dv) = _run(fa, shape, causal)
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO), causal=causal)
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, name)
+
+
+def test_backward_with_fp32_forward_output(fa, cuda):
+    (Q, K, V, dO), out, _, (dq, dk, dv) = _run(fa, (1, 3, 192, 256, 128), False, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO))
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, name)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", [(1, 4, 256, 512, 128), (2, 2, 100, 300, 64), (1, 2, 64, 2048, 128),
+                                   (1, 1, 300, 100, 64)])
+def test_forward_lse(fa, cuda, shape, causal):
+    """The log-sum-exp variant writes the same output bytes as the plain
+    forward and the oracle's per-row log-sum-exp (+inf where a row sees no
+    key).  The (1, 2, 64, 2048) case runs the small-problem schedule with its
+    keys split into partitions; (1, 1, 300, 100) causal has rows that see no
+    key."""
+    B, H, sq, sk, d = shape
+    Q, K, V, _ = _inputs(3, B, H, sq, sk, d)
+    Qc, Kc, Vc = Q.cuda(), K.cuda(), V.cuda()
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, out_dtype=torch.float32, causal=causal)
+    ref_out = fa.fused_fp4_attention(Qc, Kc, Vc, out_dtype=torch.float32, causal=causal)
+    assert fa.status_query() == fa.OK
+    assert torch.equal(out, ref_out)
+    want = oracle.fp4_attention_lse(_np(Q), _np(K), causal=causal).reshape(B, H, sq)
+    got = lse.cpu().numpy()
+    finite = np.isfinite(want)
+    assert np.array_equal(np.isfinite(got), finite)
+    assert np.all(got[~finite] == np.inf)
+    assert float(np.abs(got[finite] - want[finite]).max()) <= LSE_ABS
+
+
+def test_autograd_function(fa, cuda):
+    """fp4_attention under autograd: the gradients are fp4_attention_backward's
+    (the same kernels, so the same bytes)."""
+    Q, K, V, dO = (t.cuda() for t in _inputs(11, 1, 2, 192, 320, 64))
+    q, k, v = (t.clone().requires_grad_(True) for t in (Q, K, V))
+    out = fa.fp4_attention(q, k, v)
+    out.backward(dO)
+    ref_out, lse = fa.fused_fp4_attention_lse(Q, K, V)
+    dq, dk, dv = fa.fp4_attention_backward(Q, K, V, ref_out, dO, lse)
+    assert torch.equal(out.detach(), ref_out)
+    for g, want in ((q.grad, dq), (k.grad, dk), (v.grad, dv)):
+        assert g.dtype == torch.float16
+        assert torch.equal(g, want.half())
+
+
+def test_backward_repeats_bit_for_bit(fa, cuda):
+    """dK and dV are accumulated by one CTA per key tile in a fixed order, so
+    they repeat exactly; dQ sums the key tiles' partial products with
+    reduce-add in whatever order they arrive, so it may differ in the last
+    bits between runs."""
+    shape = (1, 4, 384, 512, 128)
+    (_, _, _, _), _, _, a = _run(fa, shape, False, seed=21)
+    (_, _, _, _), _, _, b = _run(fa, shape, False, seed=21)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
+    assert float((a[0] - b[0]).abs().max()) <= 1e-5 * float(a[0].abs().max())
+
+
+def test_full_size_prefill_slices(fa, cuda):
+    """The 4k x 4k, head_dim 128 prefill shape (B2 H32): slices 0 and 63 of
+    every gradient against the oracle run on those two slices."""
+    B, H, S, d = 2, 32, 4096, 128
+    Q, K, V, dO = _inputs(7, B, H, S, S, d)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse)
+    assert fa.status_query() == fa.OK
+    for s in (0, B * H - 1):
+        b, h = divmod(s, H)
+        want = oracle.fp4_attention_backward(*(t[b, h].float().numpy()[None] for t in (Q, K, V, dO)))
+        for got, w, name in zip((dq[b, h], dk[b, h], dv[b, h]), want, ("dQ", "dK", "dV")):
+            _assert_grad(got, w[0], f"{name} slice {s}")
+
+
+def test_backward_rejects_bad_arguments(fa, cuda):
+    Q, K, V, dO = (t.cuda() for t in _inputs(1, 1, 1, 64, 64, 96))
+    out, lse = torch.zeros_like(Q), torch.zeros(1, 1, 64, device="cuda")
+    with pytest.raises(fa.Fp4AttnError) as e:
+        fa.fp4_attention_backward(Q, K, V, out, dO, lse)
+    assert e.value.code == fa.EUNSUPPORTED
+    Q, K, V, dO = (t.cuda() for t in _inputs(1, 1, 1, 64, 64, 64))
+    out = torch.zeros_like(Q)
+    ws = torch.empty(fa.backward_workspace_size(1, 1, 64, 64, 64) - 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(fa.Fp4AttnError) as e:
+        fa.fp4_attention_backward(Q, K, V, out, dO, lse, workspace=ws)
+    assert e.value.code == fa.EWORKSPACE
