@@ -20,42 +20,47 @@
 // tiles that see its keys.  Per step, with the keys as the MMA M dimension:
 //     S^T  = K Q^T          tcgen05.mma kind::mxf4 block_scale  (M128 N64)
 //     dP^T = V dO^T         kind::f16, F16 operands             (M128 N64)
-//     dV  += P^T dO         kind::f16, F16, P from shared memory (M128 N=D)
+//     dV  += P^T dO         kind::f16, F16, P read from TMEM     (M128 N=D)
 //     dK  += dZ^T Qq        kind::f16, BF16                      (M128 N=D)
 //     dQ^T = Kq^T dZ^T      kind::f16, BF16, A and B MN-major    (M128 N64)
-// dV and dK accumulate in TMEM over the item's steps; each step's dQ^T tile
-// (head_dim rows x 64 queries) is added into an FP32 accumulator in global
-// memory, [slices][D][seq_q padded], by TMA reduce-add (the other key tiles
-// of the slice add theirs), and a last kernel transposes and scales it.
+// dZ carries the softmax scale.  dV and dK accumulate in TMEM over the item's
+// steps; each step's dQ^T tile (head_dim rows x 64 queries) is added into the
+// FP32 dQ output (cleared by the host first) with coalesced reductions (the
+// other key tiles of the slice add theirs).
 //
-// Roles (384 threads):
-//   warp 0      TMA producer: per item K codes + scale tile, V, Kq; per step
-//               (QST-stage ring) Q codes + scale tile, dO, Qq, lse2, Dd.
-//   warp 1      MMA issuer (one thread).  S^T and dP^T of step g+1 are issued
-//               as soon as the softmax warpgroup holds step g's in registers,
-//               before step g's dV, dK and dQ^T, so the tensor core computes
-//               them while the warpgroup works on step g.
-//   warps 2-3   idle.
-//   warps 4-7   gradient warpgroup: thread = key row = TMEM lane.  Reads its
-//               S^T and dP^T rows, forms P and dZ for 64 queries, and writes
-//               them (FP16, BF16) to shared memory as 128-byte swizzled rows,
-//               the layout the three MMAs read (K-major for dV and dK,
-//               MN-major for dQ^T).
-//   warps 8-11  dQ warpgroup: thread = head-dim row of dQ^T = TMEM lane.  Per
-//               step it moves its dQ^T row into a per-warp staging buffer and
-//               lane 0 of each warp adds the warp's 32 rows into the global
-//               accumulator with TMA reduce-add.  At the end of an item it
-//               writes dV and scale * dK (thread = key row) to the outputs.
+// The tensor core reads both operands of an MMA from shared memory unless A
+// is in TMEM; at N = 64 those reads, not the multiply, set the MMA's pace, so
+// P goes to TMEM (dV's A) and dQ^T leaves through registers, keeping shared
+// memory for the operands that must live there.
+//
+// Roles (512 threads):
+//   warp 0       TMA producer: per item K codes + scale tile, V, Kq; per step
+//                (QST-stage ring) Q codes + scale tile, dO, Qq, lse2, Dd.
+//   warp 1       MMA issuer (one thread).  S^T and dP^T of step g+1 are issued
+//                as soon as the gradient warpgroups hold step g's in
+//                registers, before step g's dV, dK and dQ^T, so the tensor core
+//                computes them while the warpgroups work on step g.
+//   warps 2-3    idle.
+//   warps 4-11   two gradient warpgroups; thread = key row = TMEM lane, and
+//                warpgroup h owns queries [32h, 32h + 32) of the step.  Each
+//                reads its S^T and dP^T columns, forms P and dZ, stores P into
+//                TMEM (tcgen05.st) and dZ into shared memory as a 128-byte
+//                swizzled row (K-major for dK, MN-major for dQ^T).
+//   warps 12-15  dQ warpgroup: thread = head-dim row of dQ^T = TMEM lane.  Per
+//                step it reads its dQ^T row and adds it into dQ
+//                (red.global.add; a warp covers 32 consecutive head-dim
+//                entries of one query row: 128 contiguous bytes).  At the end
+//                of an item it writes dV and dK (thread = key row).
 //
 // TMEM columns (512 allocated): S^T [0,64), dP^T [64,128), dV [128, 128+D),
-// dK [128+D, 128+2D), dQ^T [128+2D, +64), K scales (4), Q scales (4 per stage).
+// dK [128+D, 128+2D), dQ^T [128+2D, +64), P [.., +32) (FP16 pairs), K scales
+// (4), Q scales (4).
 //
 // Every mbarrier wait is bounded (globaltimer) as in the forward kernels: on
 // expiry the CTA records FP4ATTN_ETIMEOUT, every role leaves its loop,
-// in-flight copies, reductions and MMAs are drained (bounded), TMEM is freed
-// and the CTA returns.  No role waits on a barrier shared by more than one
-// warp except through mbarriers, so a role that gives up cannot strand
-// another one.
+// in-flight copies and MMAs are drained (bounded), TMEM is freed and the CTA
+// returns.  Roles synchronise through mbarriers only, so a role that gives up
+// cannot strand another one.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -70,21 +75,25 @@ namespace fp4attn {
 template <int D>
 struct BwdCfg {
     static_assert(D == 64 || D == 128, "the backward kernel covers head_dim 64 and 128");
+    static constexpr int THREADS = 512;
     static constexpr int BK = 128;                  // keys per item (MMA M)
     static constexpr int BQ = 64;                   // queries per step
     static constexpr int QK_ROW = D / 2;            // bytes per packed code row (swizzle = row)
     static constexpr int KSTEPS = D / 64;           // mxf4 MMAs per S^T tile (K = 64 each)
     static constexpr int DCH = D / 64;              // 64-column (128-byte) chunks of a 16-bit row
-    static constexpr int QST = 2;                   // query stages
+    static constexpr int QST = 3;                   // query stages
     // TMEM
     static constexpr int S_COL = 0;
     static constexpr int DP_COL = 64;
     static constexpr int DV_COL = 128;
     static constexpr int DK_COL = DV_COL + D;
     static constexpr int DQ_COL = DK_COL + D;
-    static constexpr int SFA_COL = DQ_COL + 64;
-    static constexpr int SFB_COL = SFA_COL + 4;     // + stage * 4
-    static constexpr int TMEM_USED = SFB_COL + 4 * QST;
+    static constexpr int P_COL = DQ_COL + 64;
+    static constexpr int SFA_COL = P_COL + 32;
+    // One Q scale group: step g+1's scales are copied in after S of step g
+    // has completed (its gradient warpgroups have read it).
+    static constexpr int SFB_COL = SFA_COL + 4;
+    static constexpr int TMEM_USED = SFB_COL + 4;
     static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
     // shared memory (offsets from a 1024-aligned base)
     static constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
@@ -111,13 +120,9 @@ struct BwdCfg {
     static constexpr int STAGE_BYTES = align1k(SQ_DD + BQ * 4);
     static constexpr int STAGE_TX = Q_BYTES + SF_BYTES + 2 * DO_BYTES + 2 * BQ * 4;
     static constexpr int KV_TX = K_BYTES + SF_BYTES + 2 * V_BYTES;  // K codes, scales, V, Kq (D columns)
-    // P and dZ: 128 key rows x 64 queries, 128-byte swizzled rows
-    static constexpr int OFF_P = OFF_STAGE + QST * STAGE_BYTES;
-    static constexpr int OFF_DS = OFF_P + BK * 128;
-    // dQ^T staging: per dQ warp two boxes of 32 head-dim rows x 32 queries (FP32)
-    static constexpr int DQW_BYTES = 2 * 32 * 128;
-    static constexpr int OFF_DQST = OFF_DS + BK * 128;
-    static constexpr int OFF_BAR = OFF_DQST + 4 * DQW_BYTES;
+    // dZ: 128 key rows x 64 queries (BF16), 128-byte swizzled rows
+    static constexpr int OFF_DS = OFF_STAGE + QST * STAGE_BYTES;
+    static constexpr int OFF_BAR = OFF_DS + BK * 128;
     // kv_full, kv_empty, q_full[QST], q_empty[QST], s_full, s_free, ds_full,
     // ds_free, dq_full, dq_free, acc_full, acc_free, drain
     static constexpr int NUM_BARS = 2 + 2 * QST + 9;
@@ -137,6 +142,7 @@ struct BwdArgs {
     const uint8_t* k_sf;       // [slices][nk_tiles][512]  (128-row scale tiles)
     const float* lse2;         // [slices][sq_pad]: lse * log2(e); +inf on padding rows
     const float* dd;           // [slices][sq_pad]: rowsum(dO o O); 0 on padding rows
+    float* dq;                 // [slices][seq_q][D] FP32, zero on entry (accumulated by reductions)
     float* dk;                 // [slices][seq_k][D] FP32
     float* dv;                 // [slices][seq_k][D] FP32
     unsigned long long timeout_ns;
@@ -182,11 +188,11 @@ __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi)
 }
 
 template <int D>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     fp4_attention_bwd_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kq,
                              const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_qq,
-                             const __grid_constant__ CUtensorMap tm_dq, const BwdArgs args)
+                             const BwdArgs args)
 {
     using C = BwdCfg<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -196,16 +202,15 @@ __global__ void __launch_bounds__(384, 1)
     uint8_t* sV = smem + C::OFF_V;
     uint8_t* sKq = smem + C::OFF_KQ;
     uint8_t* sStage = smem + C::OFF_STAGE;
-    uint8_t* sP = smem + C::OFF_P;
     uint8_t* sDS = smem + C::OFF_DS;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     uint64_t* kv_full = bars;
     uint64_t* kv_empty = bars + 1;             // the item's MMAs are done with K, V, Kq (commit)
     uint64_t* q_full = bars + 2;               // [QST]
-    uint64_t* q_empty = q_full + C::QST;       // [QST] MMAs done (commit) + gradient warpgroup done (128)
+    uint64_t* q_empty = q_full + C::QST;       // [QST] MMAs done (commit) + gradient warpgroups done (256)
     uint64_t* s_full = q_empty + C::QST;       // S^T and dP^T computed (commit)
-    uint64_t* s_free = s_full + 1;             // S^T and dP^T copied to registers (128)
-    uint64_t* ds_full = s_free + 1;            // P and dZ written to shared memory (128)
+    uint64_t* s_free = s_full + 1;             // S^T and dP^T copied to registers (256)
+    uint64_t* ds_full = s_free + 1;            // P in TMEM and dZ in shared memory (256)
     uint64_t* ds_free = ds_full + 1;           // dV, dK, dQ^T MMAs done with P and dZ (commit)
     uint64_t* dq_full = ds_free + 1;           // dQ^T computed (commit)
     uint64_t* dq_free = dq_full + 1;           // dQ^T copied to registers (128)
@@ -222,11 +227,11 @@ __global__ void __launch_bounds__(384, 1)
         ptx::mbar_init(kv_empty, 1);
         for (int i = 0; i < C::QST; i++) {
             ptx::mbar_init(&q_full[i], 1);
-            ptx::mbar_init(&q_empty[i], 1 + 128);
+            ptx::mbar_init(&q_empty[i], 1 + 256);
         }
         ptx::mbar_init(s_full, 1);
-        ptx::mbar_init(s_free, 128);
-        ptx::mbar_init(ds_full, 128);
+        ptx::mbar_init(s_free, 256);
+        ptx::mbar_init(ds_full, 256);
         ptx::mbar_init(ds_free, 1);
         ptx::mbar_init(dq_full, 1);
         ptx::mbar_init(dq_free, 128);
@@ -243,7 +248,6 @@ __global__ void __launch_bounds__(384, 1)
         ptx::prefetch_tmap(&tm_kq);
         ptx::prefetch_tmap(&tm_do);
         ptx::prefetch_tmap(&tm_qq);
-        ptx::prefetch_tmap(&tm_dq);
     }
     if (warp == 1) {
         ptx::tmem_alloc(&tmem_base_sh, 512);
@@ -334,7 +338,7 @@ __global__ void __launch_bounds__(384, 1)
                 if (gg > 0 && !wait_phase(s_free, (gg - 1) & 1, wctx, kSiteSFree)) return false;
                 ptx::tc_fence_after();
                 uint8_t* st = sStage + qs * C::STAGE_BYTES;
-                const uint32_t sfb = tmem + C::SFB_COL + 4 * qs;
+                const uint32_t sfb = tmem + C::SFB_COL;
                 ptx::tc_cp_32x128b_warpx4(sfb, ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QSF), 0, 128, ptx::kSwizzleNone));
                 const uint64_t qdesc = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_Q), 16, 8 * C::QK_ROW, qk_layout);
 #pragma unroll
@@ -371,18 +375,18 @@ __global__ void __launch_bounds__(384, 1)
                     if (!wait_phase(ds_full, g & 1, wctx, kSitePFull)) { ok = false; break; }
                     if (i == 0 && it > 0 && !wait_phase(acc_free, (it - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
                     ptx::tc_fence_after();
-                    // dV += P^T dO, dK += dZ^T Qq: A K-major (rows = keys, K = queries),
-                    // B MN-major (N = head_dim in 64-column chunks, K = queries).
+                    // dV += P^T dO (P from TMEM: lanes = keys, columns = queries),
+                    // dK += dZ^T Qq (dZ K-major in shared memory); B MN-major
+                    // (N = head_dim in 64-column chunks, K = queries).
 #pragma unroll
                     for (int kk = 0; kk < C::BQ / 16; kk++) {
-                        const uint64_t ap = ptx::make_sdesc(ptx::smem_u32(sP) + kk * 32, 16, 1024, sw128);
                         const uint64_t ad = ptx::make_sdesc(ptx::smem_u32(sDS) + kk * 32, 16, 1024, sw128);
                         const uint64_t bo =
                             ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
                         const uint64_t bq =
                             ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QQ) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                        ptx::mma_f16_ss(tmem + C::DV_COL, ap, bo, idesc_dv, acc);
+                        ptx::mma_f16_ts(tmem + C::DV_COL, tmem + C::P_COL + kk * 8, bo, idesc_dv, acc);
                         ptx::mma_f16_ss(tmem + C::DK_COL, ad, bq, idesc_dk, acc);
                     }
                     if (g > 0 && !wait_phase(dq_free, (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
@@ -409,11 +413,12 @@ __global__ void __launch_bounds__(384, 1)
             drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
-        // ------------------------------------------------------------ gradient warpgroup
-        const int kr = (warp - 4) * 32 + lane;     // key row of the item = TMEM lane
-        const uint32_t lane_off = static_cast<uint32_t>((warp - 4) * 32) << 16;
-        const float c = args.scale_log2;
+    } else if (warp >= 4 && warp < 12) {
+        // ------------------------------------------------------------ gradient warpgroups
+        const int h = (warp - 4) / 4;              // queries [32h, 32h + 32) of each step
+        const int kr = (warp % 4) * 32 + lane;     // key row of the item = TMEM lane
+        const uint32_t lane_off = static_cast<uint32_t>((warp % 4) * 32) << 16;
+        const float c = args.scale_log2, sc = args.scale;
         int g = 0;
         bool ok = true;
         for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
@@ -427,11 +432,9 @@ __global__ void __launch_bounds__(384, 1)
                 const int qs = g % C::QST;
                 if (!__all_sync(0xffffffffu, wait_phase(s_full, g & 1, wctx, kSiteSFull))) { ok = false; break; }
                 ptx::tc_fence_after();
-                uint32_t sr[2][32], dr[2][32];
-                ptx::tmem_ld32(tmem + lane_off + C::S_COL, sr[0]);
-                ptx::tmem_ld32(tmem + lane_off + C::S_COL + 32, sr[1]);
-                ptx::tmem_ld32(tmem + lane_off + C::DP_COL, dr[0]);
-                ptx::tmem_ld32(tmem + lane_off + C::DP_COL + 32, dr[1]);
+                uint32_t sr[32], dr[32];
+                ptx::tmem_ld32(tmem + lane_off + C::S_COL + 32 * h, sr);
+                ptx::tmem_ld32(tmem + lane_off + C::DP_COL + 32 * h, dr);
                 ptx::tc_wait_ld();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(s_free);
@@ -441,24 +444,25 @@ __global__ void __launch_bounds__(384, 1)
                     break;
                 }
                 const uint8_t* st = sStage + qs * C::STAGE_BYTES;
-                const float4* lse4 = reinterpret_cast<const float4*>(st + C::SQ_LSE);
-                const float4* dd4 = reinterpret_cast<const float4*>(st + C::SQ_DD);
-                const int q0 = qi * C::BQ;
-                uint32_t pk[32], dk[32];
+                const float4* lse4 = reinterpret_cast<const float4*>(st + C::SQ_LSE) + 8 * h;
+                const float4* dd4 = reinterpret_cast<const float4*>(st + C::SQ_DD) + 8 * h;
+                const int q0 = qi * C::BQ + 32 * h;
+                // Every query of this warp's slice of the step sees every key of
+                // the warp (no mask work), or not.
+                const bool full = __all_sync(0xffffffffu, key_ok && q0 >= lim);
+                uint32_t pk[16], dk[16];
 #pragma unroll
-                for (int c4 = 0; c4 < 16; c4++) {
+                for (int c4 = 0; c4 < 8; c4++) {
                     const float4 L = lse4[c4], Dv = dd4[c4];
                     const float Ls[4] = {L.x, L.y, L.z, L.w}, Ds[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
                     float pv[4], dv[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const int q = 4 * c4 + e;
-                        const float s = __uint_as_float(sr[q / 32][q % 32]);
-                        const float dpv = __uint_as_float(dr[q / 32][q % 32]);
-                        float p = ptx::ex2_approx(fmaf(s, c, -Ls[e]));
-                        if (!key_ok || q0 + q < lim) p = 0.f;
+                        float p = ptx::ex2_approx(fmaf(__uint_as_float(sr[q]), c, -Ls[e]));
+                        if (!full && (!key_ok || q0 + q < lim)) p = 0.f;
                         pv[e] = p;
-                        dv[e] = p * (dpv - Ds[e]);
+                        dv[e] = (p * sc) * (__uint_as_float(dr[q]) - Ds[e]);
                     }
                     pk[2 * c4] = ptx::pack_half2(pv[0], pv[1]);
                     pk[2 * c4 + 1] = ptx::pack_half2(pv[2], pv[3]);
@@ -470,26 +474,28 @@ __global__ void __launch_bounds__(384, 1)
                     ok = false;
                     break;
                 }
-                // Row kr: 128 bytes, 16-byte unit u at (u ^ (kr & 7)) (128-byte swizzle).
+                ptx::tc_fence_after();
+                ptx::tmem_st16(tmem + lane_off + C::P_COL + 16 * h, pk);
+                // dZ row kr: 128 bytes, 16-byte unit u at (u ^ (kr & 7)) (128-byte
+                // swizzle); this warpgroup's queries are units 4h .. 4h + 3.
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const int pu = u ^ (kr & 7);
-                    *reinterpret_cast<uint4*>(sP + kr * 128 + pu * 16) =
-                        make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                for (int u = 0; u < 4; u++) {
+                    const int pu = (4 * h + u) ^ (kr & 7);
                     *reinterpret_cast<uint4*>(sDS + kr * 128 + pu * 16) =
                         make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
                 }
                 ptx::fence_proxy_async_smem();
+                ptx::tc_wait_st();
+                ptx::tc_fence_before();
                 ptx::mbar_arrive(ds_full);
                 ptx::mbar_arrive(&q_empty[qs]);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 12) {
         // ------------------------------------------------------------ dQ warpgroup
-        const int wq = warp - 8;
+        const int wq = warp - 12;
         const int tr = wq * 32 + lane;             // TMEM lane: head-dim row of dQ^T, key row of dV / dK
         const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-        uint8_t* stg = smem + C::OFF_DQST + wq * C::DQW_BYTES;
         int g = 0, it = 0;
         bool ok = true;
         for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
@@ -516,23 +522,14 @@ __global__ void __launch_bounds__(384, 1)
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(dq_free);
                 if (D == 128 || wq < 2) {
-                    // The previous step's reductions must be done reading the staging.
-                    if (lane == 0) ptx::bulk_wait_group_read<0>();
-                    __syncwarp();
+                    // Query row q0 + j of dQ gets column tr of the tile: the warp's
+                    // 32 lanes add 32 consecutive floats of that row.
+                    const int q0 = qi * C::BQ;
+                    const int nrow = min(C::BQ, args.seq_q - q0);
+                    float* dst = args.dq + (static_cast<size_t>(item.slice) * args.seq_q + q0) * D + tr;
 #pragma unroll
-                    for (int b = 0; b < 2; b++)
-#pragma unroll
-                        for (int u = 0; u < 8; u++) {
-                            const int pu = u ^ (lane & 7);
-                            *reinterpret_cast<uint4*>(stg + b * 32 * 128 + lane * 128 + pu * 16) =
-                                make_uint4(v[b][4 * u], v[b][4 * u + 1], v[b][4 * u + 2], v[b][4 * u + 3]);
-                        }
-                    ptx::fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        ptx::tma_reduce_add_3d(&tm_dq, stg, qi * C::BQ, wq * 32, item.slice);
-                        ptx::tma_reduce_add_3d(&tm_dq, stg + 32 * 128, qi * C::BQ + 32, wq * 32, item.slice);
-                        ptx::bulk_commit_group();
+                    for (int j = 0; j < 64; j++) {
+                        if (j < nrow) atomicAdd(dst + static_cast<size_t>(j) * D, __uint_as_float(v[j / 32][j % 32]));
                     }
                 }
             }
@@ -553,8 +550,8 @@ __global__ void __launch_bounds__(384, 1)
                             make_float4(__uint_as_float(a[i]), __uint_as_float(a[i + 1]), __uint_as_float(a[i + 2]),
                                         __uint_as_float(a[i + 3]));
                         *reinterpret_cast<float4*>(args.dk + orow + 32 * k + i) =
-                            make_float4(__uint_as_float(b[i]) * args.scale, __uint_as_float(b[i + 1]) * args.scale,
-                                        __uint_as_float(b[i + 2]) * args.scale, __uint_as_float(b[i + 3]) * args.scale);
+                            make_float4(__uint_as_float(b[i]), __uint_as_float(b[i + 1]), __uint_as_float(b[i + 2]),
+                                        __uint_as_float(b[i + 3]));
                     }
                 }
             }
@@ -562,9 +559,6 @@ __global__ void __launch_bounds__(384, 1)
             ptx::mbar_arrive(acc_free);
             it++;
         }
-        // Shared memory must outlive the reductions that read it.
-        if (lane == 0) ptx::bulk_wait_group<0>();
-        __syncwarp();
     }
 
     ptx::tc_fence_before();
@@ -669,23 +663,6 @@ __global__ void __launch_bounds__(256) bwd_rows_kernel(const __half* __restrict_
     if (lane == 0) {
         dd[o] = acc;
         lse2[o] = lse[slice * seq_q + row] * 1.4426950408889634f;
-    }
-}
-
-// dQ[slice][q][c] = scale * acc[slice][c][q] for q < seq_q: 32 x 32 tiles
-// transposed through shared memory.
-__global__ void __launch_bounds__(256) bwd_dq_kernel(const float* __restrict__ acc, float* __restrict__ dq, int seq_q,
-                                                      int sq_pad, int d, float scale)
-{
-    __shared__ float t[32][33];
-    const int64_t slice = blockIdx.z;
-    const int q0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
-    for (int i = ty; i < 32; i += 8) t[i][tx] = acc[(slice * d + c0 + i) * sq_pad + q0 + tx];
-    __syncthreads();
-    for (int i = ty; i < 32; i += 8) {
-        const int q = q0 + i;
-        if (q < seq_q) dq[(slice * seq_q + q) * d + c0 + tx] = t[tx][i] * scale;
     }
 }
 

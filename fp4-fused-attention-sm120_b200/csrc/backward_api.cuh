@@ -5,9 +5,9 @@
 // helpers (fp4attn::host).
 //
 // Launches, in stream order: the quantiser with dequantised BF16 copies of Q
-// and K, the per-row Dd / lse2 pass, a clear of the dQ accumulator, the
-// backward kernel, and the dQ transpose.  The workspace holds everything but
-// the caller's inputs and outputs.
+// and K, the per-row Dd / lse2 pass, a clear of dQ (the kernel adds every key
+// tile's contribution into it), and the backward kernel.  The workspace holds
+// the quantised operands and the per-row statistics.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -42,7 +42,7 @@ int failf(int code, const char* fmt, ...)
     } while (0)
 
 struct BwdWorkspace {
-    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, dq_acc, total;
+    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, total;
 };
 
 struct BwdShape {
@@ -81,7 +81,6 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s)
     w.kq = take(n * s.sk * s.d * 2);
     w.lse2 = take(n * s.sq_pad * 4);
     w.dd = take(n * s.sq_pad * 4);
-    w.dq_acc = take(n * s.d * s.sq_pad * 4);
     w.total = off;
     return w;
 }
@@ -117,11 +116,10 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
                 static_cast<const __half*>(dOut), static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
         BWD_CUDA(cudaGetLastError());
     }
-    // 3. The dQ accumulator starts at zero.
-    float* dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
-    BWD_CUDA(cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(s.slices) * D * s.sq_pad * 4, st));
+    // 3. dQ starts at zero.
+    BWD_CUDA(cudaMemsetAsync(dQ, 0, static_cast<size_t>(s.slices) * s.sq * D * 4, st));
     // 4. The backward kernel.
-    CUtensorMap tk, tq, tv, tkq, tdo, tqq, tdq;
+    CUtensorMap tk, tq, tv, tkq, tdo, tqq;
     int rc;
     const uint64_t n = static_cast<uint64_t>(s.slices);
     if ((rc = host::map3d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, D / 2, s.sk, n, D / 2, 128, D / 2)) ||
@@ -129,8 +127,7 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
         (rc = host::map3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, V, D, s.sk, n, 64, 128, 128)) ||
         (rc = host::map3d(&tkq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.kq, D, s.sk, n, 64, 128, 128)) ||
         (rc = host::map3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dOut, D, s.sq, n, 64, 64, 128)) ||
-        (rc = host::map3d(&tqq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.qq, D, s.sq, n, 64, 64, 128)) ||
-        (rc = host::map3d(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dq_acc, s.sq_pad, D, n, 32, 32, 128)))
+        (rc = host::map3d(&tqq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.qq, D, s.sq, n, 64, 64, 128)))
         return rc;
     fp4attn::BwdArgs a;
     a.seq_q = s.sq;
@@ -148,6 +145,7 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
     a.k_sf = ws + w.k_sf;
     a.lse2 = lse2;
     a.dd = dd;
+    a.dq = dQ;
     a.dk = dK;
     a.dv = dV;
     a.timeout_ns = host::timeout_ns();
@@ -164,11 +162,7 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
         smem_ctx[dev].store(ctx, std::memory_order_release);
     }
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, host::sms()));
-    kern<<<grid, 384, C::SMEM_BYTES, st>>>(tk, tq, tv, tkq, tdo, tqq, tdq, a);
-    BWD_CUDA(cudaGetLastError());
-    // 5. dQ = scale * transpose(accumulator).
-    fp4attn::bwd_dq_kernel<<<dim3(s.sq_pad / 32, D / 32, static_cast<unsigned>(s.slices)), 256, 0, st>>>(
-        dq_acc, dQ, s.sq, s.sq_pad, D, scale);
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, st>>>(tk, tq, tv, tkq, tdo, tqq, a);
     BWD_CUDA(cudaGetLastError());
     return FP4ATTN_OK;
 }
