@@ -12,6 +12,12 @@ of a job with 64*N slices (weak scaling, no collective on the data path; NCCL
 only carries the barrier and the max-over-ranks of the timings).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --pass backward [--workload prefill_4k]   (the backward pass, one GPU)
+
+The backward line (fp4attn_backward: dQ, dK, dV of the same workload) counts
+10 * B * H * seq_q * seq_k * head_dim FLOPs per pass (S recomputed, dP, dV,
+dK, dQ: 2.5x the forward's) against the mixed roofline with S at the FP4 rate
+and the other four products at the FP16 rate.
 """
 from __future__ import annotations
 
@@ -46,6 +52,8 @@ def parse():
                     help="quantise Q inside the attention kernel (fp4attn_forward_fused_q) in the timed step")
     ap.add_argument("--box-steps", type=int, default=5,
                     help="steps of this rank's share of the box-scale job (0: skip)")
+    ap.add_argument("--pass", dest="direction", choices=["forward", "backward"], default="forward",
+                    help="forward (the headline) or the backward pass of the workload")
     return ap.parse_args()
 
 
@@ -313,8 +321,111 @@ def reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def bench_backward(args):
+    """One backward pass (fp4attn_backward: quantise Q and K with their BF16
+    dequantised copies, the per-row Dd / lse2 pass, and the backward kernel)
+    per step, inputs and the forward's output and log-sum-exp resident in
+    HBM; one JSON line."""
+    import torch
+    import fp4attn_b200 as fa
+    import fp4attn_b200.workloads as wl
+    w = wl.WORKLOADS[args.workload]
+    if w.head_dim not in (64, 128):
+        raise SystemExit("the backward pass covers head_dim 64 and 128")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Q, K, V = (t[None] for t in wl.make_inputs(w, args.seed, device=dev))
+    n = w.slices
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    dO = torch.randn(Q.shape, device=dev, generator=g).half()
+    odt = torch.float16 if w.out_dtype == "float16" else torch.float32
+    out, lse = fa.fused_fp4_attention_lse(Q, K, V, out_dtype=odt)
+    ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim), dtype=torch.uint8, device=dev)
+    dq, dk, dv = (torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (Q, K, V))
+    L = fa.lib()
+    stream = torch.cuda.current_stream(dev)
+    sh = (1, n, w.seq_q, w.seq_k, w.head_dim)
+
+    def step(ev_a=None, ev_b=None):
+        rc = L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), out.data_ptr(), dO.data_ptr(), lse.data_ptr(),
+                                        dq.data_ptr(), fa._dtype_code(out), *sh, fa.SCALE_REFERENCE, ws.data_ptr(),
+                                        ws.numel(), stream.cuda_stream)
+        if ev_a is not None:
+            ev_a.record(stream)
+        rc = rc or L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                             dv.data_ptr(), *sh, 0.0, fa.MASK_NONE, ws.data_ptr(), ws.numel(),
+                                             stream.cuda_stream)
+        if ev_b is not None:
+            ev_b.record(stream)
+        if rc != fa.OK:
+            raise SystemExit(f"fp4attn_backward failed: {fa.lib().fp4attn_last_error().decode()}")
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    io_bytes = sum(t.numel() * t.element_size() for t in (Q, K, V, out, dO, dq, dk, dv))
+    flush, l2 = l2_note(io_bytes)
+    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush else None
+    props = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else "0")
+    sampler.start()
+    time.sleep(0.5)
+    sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_wall0 = time.time()
+    for i in range(args.steps):  # whole passes
+        if flush:
+            flush_buf.zero_()
+        sev[i][0].record(stream)
+        step()
+        sev[i][1].record(stream)
+    for i in range(args.steps):  # the backward kernel alone
+        if flush:
+            flush_buf.zero_()
+        step(*kev[i])
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    torch.cuda.synchronize()
+    time.sleep(0.3)
+    sampler.stop()
+    status = fa.status_query()
+    ms_step = sum(a.elapsed_time(b) for a, b in sev) / args.steps
+    kern_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+    flops = 10.0 * n * w.seq_q * w.seq_k * w.head_dim
+    value = flops / (ms_step * 1e-3) / 1e12
+    burst, sustained, hbm, peak_src = measured_peaks()
+    clocks = sampler.summary(t_wall0, t_wall1)
+    basis = peak_basis(ms_step * args.steps * 1e-3, clocks["reasons"])
+    bf16 = burst if basis == "burst" else sustained
+    # S (2/10 of the FLOPs) at 4x the FP16 rate, the other 8/10 at 1x.
+    peak = flops / (0.2 * flops / (4 * bf16) + 0.8 * flops / bf16)
+    line = {
+        "metric": "fused FP4 attention backward TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (S) + f16/bf16 (dP, dV, dK, dQ)",
+        "data": "synthetic (seeded N(0,1) FP16 on device)",
+        "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "l2": l2},
+        "roofline": {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (kern_ms * 1e-3) / 1e12 / peak, "traffic": profile_traffic(w.name, "fp4_attention_bwd_kernel"),
+                     "peak_basis": f"mixed: S at 4x and dP, dV, dK, dQ at 1x the {peak_src} {basis} bf16 dense "
+                                   f"{bf16:g} TFLOP/s",
+                     "kernel": "fp4_attention_bwd_kernel", "kernel_ms": kern_ms},
+        "frac_of_mixed_roofline_step": value / peak,
+        "gpu_launches": 3 * args.steps,  # per pass: quantise, rows, backward kernel (plus one memset of dQ)
+        "clocks": clocks,
+        "device_status": int(status),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.direction == "backward":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no backward pass"}), flush=True)
+            return
+        bench_backward(args)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         reference_arm(args, world, rank)

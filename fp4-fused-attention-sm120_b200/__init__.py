@@ -85,6 +85,10 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_backward_workspace_size.restype = sz
     L.fp4attn_backward.argtypes = [vp] * 9 + [i32] * 6 + [f32, i32, i32, vp, sz, vp]
     L.fp4attn_backward.restype = i32
+    L.fp4attn_backward_prepare.argtypes = [vp] * 6 + [i32] * 7 + [vp, sz, vp]
+    L.fp4attn_backward_prepare.restype = i32
+    L.fp4attn_backward_attend.argtypes = [vp] * 5 + [i32] * 5 + [f32, i32, vp, sz, vp]
+    L.fp4attn_backward_attend.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
     L.fp4attn_status_query.restype = i32
     L.fp4attn_selftest_timeout.argtypes = [ctypes.c_uint, vp]

@@ -4,10 +4,12 @@
 // translation unit's device error word (fp4attn_status_query) and its host
 // helpers (fp4attn::host).
 //
-// Launches, in stream order: the quantiser with dequantised BF16 copies of Q
-// and K, the per-row Dd / lse2 pass, a clear of dQ (the kernel adds every key
-// tile's contribution into it), and the backward kernel.  The workspace holds
-// the quantised operands and the per-row statistics.
+// fp4attn_backward_prepare launches, in stream order, the quantiser with
+// dequantised BF16 copies of Q and K, the per-row Dd / lse2 pass and a clear
+// of dQ (the kernel adds every key tile's contribution into it);
+// fp4attn_backward_attend launches the backward kernel; fp4attn_backward is
+// the two.  The workspace holds the quantised operands and the per-row
+// statistics.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -85,40 +87,45 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s)
     return w;
 }
 
+// Everything before the backward kernel: Q and K codes, scale tiles and BF16
+// dequantised copies; Dd and lse2 per query row; dQ cleared.
 template <int D>
-int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, const void* Out, int out_dtype,
-               const void* dOut, const float* lse, float* dQ, float* dK, float* dV, float scale, int ocp, bool causal,
-               uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+int bwd_prepare(const BwdShape& s, const void* Q, const void* K, const void* Out, int out_dtype, const void* dOut,
+                const float* lse, float* dQ, int ocp, uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
 {
-    using C = fp4attn::BwdCfg<D>;
-    // 1. Q and K: codes, scale tiles and BF16 dequantised copies.
     fp4attn::BwdQuantJob jq{static_cast<const __half*>(Q), ws + w.q_codes, ws + w.q_sf,
                             reinterpret_cast<__nv_bfloat16*>(ws + w.qq), s.sq, 64, 6, s.nq};
     fp4attn::BwdQuantJob jk{static_cast<const __half*>(K), ws + w.k_codes, ws + w.k_sf,
                             reinterpret_cast<__nv_bfloat16*>(ws + w.kq), s.sk, 128, 7, s.nk};
     {
-        const int64_t per_slice = std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (D / 32);
+        const int64_t per_slice =
+            std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (D / 32);
         const int gx = static_cast<int>(
             std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / s.slices + 1)));
         fp4attn::bwd_quantize_kernel<D / 32><<<dim3(gx, static_cast<unsigned>(s.slices), 2), 256, 0, st>>>(jq, jk, ocp);
         BWD_CUDA(cudaGetLastError());
     }
-    // 2. Dd and lse2 per query row.
     float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
     float* dd = reinterpret_cast<float*>(ws + w.dd);
-    {
-        const dim3 grid((s.sq_pad + 7) / 8, static_cast<unsigned>(s.slices));
-        if (out_dtype == FP4ATTN_F32)
-            fp4attn::bwd_rows_kernel<D, float><<<grid, 256, 0, st>>>(
-                static_cast<const __half*>(dOut), static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
-        else
-            fp4attn::bwd_rows_kernel<D, __half><<<grid, 256, 0, st>>>(
-                static_cast<const __half*>(dOut), static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
-        BWD_CUDA(cudaGetLastError());
-    }
-    // 3. dQ starts at zero.
+    const dim3 grid((s.sq_pad + 7) / 8, static_cast<unsigned>(s.slices));
+    if (out_dtype == FP4ATTN_F32)
+        fp4attn::bwd_rows_kernel<D, float><<<grid, 256, 0, st>>>(
+            static_cast<const __half*>(dOut), static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+    else
+        fp4attn::bwd_rows_kernel<D, __half><<<grid, 256, 0, st>>>(
+            static_cast<const __half*>(dOut), static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+    BWD_CUDA(cudaGetLastError());
+    // The kernel adds every key tile's contribution into dQ.
     BWD_CUDA(cudaMemsetAsync(dQ, 0, static_cast<size_t>(s.slices) * s.sq * D * 4, st));
-    // 4. The backward kernel.
+    return FP4ATTN_OK;
+}
+
+// The backward kernel on a prepared workspace.
+template <int D>
+int bwd_attend(const BwdShape& s, const void* V, const void* dOut, float* dQ, float* dK, float* dV, float scale,
+               bool causal, const uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+{
+    using C = fp4attn::BwdCfg<D>;
     CUtensorMap tk, tq, tv, tkq, tdo, tqq;
     int rc;
     const uint64_t n = static_cast<uint64_t>(s.slices);
@@ -143,8 +150,8 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
     a.scale_log2 = scale * 1.4426950408889634f;
     a.q_sf = ws + w.q_sf;
     a.k_sf = ws + w.k_sf;
-    a.lse2 = lse2;
-    a.dd = dd;
+    a.lse2 = reinterpret_cast<const float*>(ws + w.lse2);
+    a.dd = reinterpret_cast<const float*>(ws + w.dd);
     a.dq = dQ;
     a.dk = dK;
     a.dv = dV;
@@ -167,6 +174,25 @@ int launch_bwd(const BwdShape& s, const void* Q, const void* K, const void* V, c
     return FP4ATTN_OK;
 }
 
+// Argument and workspace checks shared by the entry points.
+int bwd_check(int batch, int heads, int seq_q, int seq_k, int head_dim, const void* workspace, size_t workspace_bytes,
+              BwdShape* s, BwdWorkspace* w)
+{
+    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1)
+        return failf(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads,
+                     seq_q, seq_k);
+    if (head_dim != 64 && head_dim != 128)
+        return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 64 and 128 (got %d)", head_dim);
+    if (static_cast<int64_t>(batch) * heads > 65535) return failf(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
+    *s = bwd_shape(batch, heads, seq_q, seq_k, head_dim);
+    *w = plan_bwd_workspace(*s);
+    if (!workspace || workspace_bytes < w->total)
+        return failf(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w->total,
+                     workspace ? workspace_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return failf(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
+    return FP4ATTN_OK;
+}
+
 }  // namespace fp4attn_bwd
 
 extern "C" {
@@ -178,6 +204,55 @@ size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_
     return plan_bwd_workspace(bwd_shape(batch, heads, seq_q, seq_k, head_dim)).total;
 }
 
+int fp4attn_backward_prepare(const void* Q, const void* K, const void* Out, const void* dOut, const float* lse,
+                             float* dQ, int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim,
+                             int scale_mode, void* workspace, size_t workspace_bytes, void* stream)
+{
+    using namespace fp4attn_bwd;
+    fp4attn::set_error_detail("");
+    if (!Q || !K || !Out || !dOut || !lse || !dQ) return failf(FP4ATTN_EINVAL, "null pointer");
+    if (!bwd_aligned16(Q) || !bwd_aligned16(K) || !bwd_aligned16(Out) || !bwd_aligned16(dOut) ||
+        !bwd_aligned16(dQ) || (reinterpret_cast<uintptr_t>(lse) & 3u))
+        return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned (lse 4-byte)");
+    if (out_dtype != FP4ATTN_F32 && out_dtype != FP4ATTN_F16) return failf(FP4ATTN_EINVAL, "out_dtype %d", out_dtype);
+    if (scale_mode != FP4ATTN_SCALE_REFERENCE && scale_mode != FP4ATTN_SCALE_OCP)
+        return failf(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
+    BwdShape s;
+    BwdWorkspace w;
+    int rc = bwd_check(batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
+    if (rc) return rc;
+    if ((rc = host::ready())) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
+    if (head_dim == 64) return bwd_prepare<64>(s, Q, K, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    return bwd_prepare<128>(s, Q, K, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+}
+
+int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int batch, int heads,
+                            int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
+                            const void* workspace, size_t workspace_bytes, void* stream)
+{
+    using namespace fp4attn_bwd;
+    fp4attn::set_error_detail("");
+    if (!V || !dOut || !dQ || !dK || !dV) return failf(FP4ATTN_EINVAL, "null pointer");
+    if (!bwd_aligned16(V) || !bwd_aligned16(dOut) || !bwd_aligned16(dQ) || !bwd_aligned16(dK) || !bwd_aligned16(dV))
+        return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned");
+    if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
+        return failf(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
+    BwdShape s;
+    BwdWorkspace w;
+    int rc = bwd_check(batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
+    if (rc) return rc;
+    if ((rc = host::ready())) return rc;
+    const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+    const bool causal = mask_mode == FP4ATTN_MASK_CAUSAL;
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (head_dim == 64) return bwd_attend<64>(s, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+    return bwd_attend<128>(s, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+}
+
 int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
                      float* dQ, float* dK, float* dV, int out_dtype, int batch, int heads, int seq_q, int seq_k,
                      int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
@@ -185,37 +260,16 @@ int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Ou
 {
     using namespace fp4attn_bwd;
     fp4attn::set_error_detail("");
-    if (!Q || !K || !V || !Out || !dOut || !lse || !dQ || !dK || !dV) return failf(FP4ATTN_EINVAL, "null pointer");
-    if (!bwd_aligned16(Q) || !bwd_aligned16(K) || !bwd_aligned16(V) || !bwd_aligned16(Out) || !bwd_aligned16(dOut) || !bwd_aligned16(dQ) ||
-        !bwd_aligned16(dK) || !bwd_aligned16(dV) || (reinterpret_cast<uintptr_t>(lse) & 3u))
-        return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned (lse 4-byte)");
-    if (out_dtype != FP4ATTN_F32 && out_dtype != FP4ATTN_F16) return failf(FP4ATTN_EINVAL, "out_dtype %d", out_dtype);
-    if (scale_mode != FP4ATTN_SCALE_REFERENCE && scale_mode != FP4ATTN_SCALE_OCP)
-        return failf(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
+    if (!V || !dK || !dV) return failf(FP4ATTN_EINVAL, "null pointer");
+    if (!bwd_aligned16(V) || !bwd_aligned16(dK) || !bwd_aligned16(dV))
+        return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned");
     if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
         return failf(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
-    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1)
-        return failf(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads,
-                     seq_q, seq_k);
-    if (head_dim != 64 && head_dim != 128)
-        return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 64 and 128 (got %d)", head_dim);
-    if (static_cast<int64_t>(batch) * heads > 65535) return failf(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
-    const BwdShape s = bwd_shape(batch, heads, seq_q, seq_k, head_dim);
-    const BwdWorkspace w = plan_bwd_workspace(s);
-    if (!workspace || workspace_bytes < w.total)
-        return failf(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w.total,
-                     workspace ? workspace_bytes : 0);
-    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return failf(FP4ATTN_EINVAL, "workspace must be 256-byte aligned");
-    int rc = host::ready();
+    int rc = fp4attn_backward_prepare(Q, K, Out, dOut, lse, dQ, out_dtype, batch, heads, seq_q, seq_k, head_dim,
+                                      scale_mode, workspace, workspace_bytes, stream);
     if (rc) return rc;
-    const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
-    const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
-    const bool causal = mask_mode == FP4ATTN_MASK_CAUSAL;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (head_dim == 64)
-        return launch_bwd<64>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, dK, dV, scale, ocp, causal, ws, w, st);
-    return launch_bwd<128>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, dK, dV, scale, ocp, causal, ws, w, st);
+    return fp4attn_backward_attend(V, dOut, dQ, dK, dV, batch, heads, seq_q, seq_k, head_dim, softmax_scale,
+                                   mask_mode, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

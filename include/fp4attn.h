@@ -206,6 +206,20 @@ int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Ou
                      int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* The two halves of fp4attn_backward (as fp4attn_prepare / fp4attn_attend
+ * are of fp4attn_forward).  fp4attn_backward_prepare quantises Q and K into
+ * the workspace (codes, scale tiles and the dequantised values as BF16), forms
+ * the per-row statistics of dOut, Out and lse, and clears dQ;
+ * fp4attn_backward_attend runs the backward kernel on that workspace, adding
+ * into dQ and writing dK and dV.  Same shapes, alignment and workspace as
+ * fp4attn_backward. */
+int fp4attn_backward_prepare(const void* Q, const void* K, const void* Out, const void* dOut, const float* lse,
+                             float* dQ, int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim,
+                             int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
+int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int batch, int heads,
+                            int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
+                            const void* workspace, size_t workspace_bytes, void* stream);
+
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
  * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
  * power-of-two scales are exact, S is checkable bit for bit.

@@ -131,3 +131,58 @@ def test_masked_entry_points_reject_bad_mask(fa):
                                     None) == fa.EINVAL
     assert b"mask_mode" in L.fp4attn_last_error()
     assert L.fp4attn_attend_masked(16, 16, fa.F16, fa.F32, 1, 1, 64, 128, 128, 0.0, -1, 256, 1 << 30, None) == fa.EINVAL
+
+
+def test_backward_workspace_size_host_only(fa):
+    # Q codes, K codes (64 B per row), Q scale tiles per 64 rows, K scale tiles
+    # per 128 rows, BF16 copies of Q and K, and two FP32 values per padded
+    # query row (lse2, Dd).
+    B, H, S, d = 2, 32, 4096, 128
+    n = B * H
+    want = n * S * 64 * 2 + n * (S // 64 + S // 128) * 512 + n * S * d * 2 * 2 + n * S * 4 * 2
+    assert fa.backward_workspace_size(B, H, S, S, d) == want
+    assert fa.backward_workspace_size(1, 1, 64, 64, 96) == 0
+    assert fa.backward_workspace_size(0, 1, 64, 64, 64) == 0
+
+
+def _bwd(fa, **kw):
+    args = dict(Q=16, K=16, V=16, O=16, dO=16, lse=16, dQ=16, dK=16, dV=16, outd=fa.F16, B=1, H=1, sq=64, sk=128,
+                d=128, scale=0.0, mode=0, mask=0, ws=256, wsb=1 << 30, stream=None)
+    args.update(kw)
+    a = args
+    return fa.lib().fp4attn_backward(a["Q"], a["K"], a["V"], a["O"], a["dO"], a["lse"], a["dQ"], a["dK"], a["dV"],
+                                     a["outd"], a["B"], a["H"], a["sq"], a["sk"], a["d"], a["scale"], a["mode"],
+                                     a["mask"], a["ws"], a["wsb"], a["stream"])
+
+
+def test_backward_rejects_bad_arguments_before_the_device(fa):
+    assert _bwd(fa, dQ=None) == fa.EINVAL
+    assert _bwd(fa, lse=18) == fa.EINVAL          # lse must be 4-byte aligned
+    assert _bwd(fa, dK=24) == fa.EINVAL           # misaligned
+    assert _bwd(fa, outd=5) == fa.EINVAL
+    assert _bwd(fa, mode=3) == fa.EINVAL
+    assert _bwd(fa, mask=2) == fa.EINVAL
+    assert _bwd(fa, sq=0) == fa.EINVAL
+    assert _bwd(fa, d=96) == fa.EUNSUPPORTED
+    assert b"head_dim 64 and 128" in fa.lib().fp4attn_last_error()
+    assert _bwd(fa, B=300, H=300) == fa.EINVAL
+    assert _bwd(fa, wsb=100) == fa.EWORKSPACE
+    assert _bwd(fa, ws=272) == fa.EINVAL          # workspace not 256-byte aligned
+    L = fa.lib()
+    assert L.fp4attn_backward_attend(16, 16, 16, 16, 16, 1, 1, 64, 128, 64, 0.0, 9, 256, 1 << 30, None) == fa.EINVAL
+    assert L.fp4attn_backward_prepare(16, 16, 16, 16, 16, 16, fa.F16, 1, 1, 64, 128, 32, 0, 256, 1 << 30,
+                                      None) == fa.EUNSUPPORTED
+
+
+def test_forward_lse_rejects_bad_arguments_before_the_device(fa):
+    L = fa.lib()
+    args = [16, 16, 16, 16, 16, fa.F16, fa.F32, 1, 1, 64, 128, 128, 0.0, 0, 0, 256, 1 << 30, None]
+    bad = list(args)
+    bad[4] = None  # lse
+    assert L.fp4attn_forward_lse(*bad) == fa.EINVAL
+    bad = list(args)
+    bad[11] = 96   # head_dim outside the backward's dims
+    assert L.fp4attn_forward_lse(*bad) == fa.EUNSUPPORTED
+    bad = list(args)
+    bad[14] = 5    # mask
+    assert L.fp4attn_forward_lse(*bad) == fa.EINVAL

@@ -163,3 +163,25 @@ def test_backward_rejects_bad_arguments(fa, cuda):
     with pytest.raises(fa.Fp4AttnError) as e:
         fa.fp4_attention_backward(Q, K, V, out, dO, lse, workspace=ws)
     assert e.value.code == fa.EWORKSPACE
+
+
+def test_prepare_then_attend_is_the_backward(fa, cuda):
+    """fp4attn_backward_prepare + fp4attn_backward_attend (as bench.py times
+    them) give fp4attn_backward's dK and dV bytes; dQ is a sum of reductions
+    whose order may vary between runs."""
+    B, H, sq, sk, d = 1, 2, 320, 384, 64
+    Q, K, V, dO = (t.cuda() for t in _inputs(5, B, H, sq, sk, d))
+    out, lse = fa.fused_fp4_attention_lse(Q, K, V)
+    dq, dk, dv = fa.fp4_attention_backward(Q, K, V, out, dO, lse)
+    ws = torch.empty(fa.backward_workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+    g = [torch.full(t.shape, float("nan"), dtype=torch.float32, device="cuda") for t in (Q, K, V)]
+    L = fa.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), out.data_ptr(), dO.data_ptr(), lse.data_ptr(),
+                                      g[0].data_ptr(), fa.F16, B, H, sq, sk, d, 0, ws.data_ptr(), ws.numel(),
+                                      st) == fa.OK
+    assert L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), g[0].data_ptr(), g[1].data_ptr(), g[2].data_ptr(),
+                                     B, H, sq, sk, d, 0.0, 0, ws.data_ptr(), ws.numel(), st) == fa.OK
+    assert fa.status_query() == fa.OK
+    assert torch.equal(g[1], dk) and torch.equal(g[2], dv)
+    assert float((g[0] - dq).abs().max()) <= 1e-5 * float(dq.abs().max())
