@@ -340,21 +340,22 @@ def bench_backward(args):
     dO = torch.randn(Q.shape, device=dev, generator=g).half()
     odt = torch.float16 if w.out_dtype == "float16" else torch.float32
     out, lse = fa.fused_fp4_attention_lse(Q, K, V, out_dtype=odt)
-    ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim), dtype=torch.uint8, device=dev)
+    ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim, fa.F16), dtype=torch.uint8,
+                     device=dev)
     dq, dk, dv = (torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (Q, K, V))
     L = fa.lib()
     stream = torch.cuda.current_stream(dev)
     sh = (1, n, w.seq_q, w.seq_k, w.head_dim)
 
     def step(ev_a=None, ev_b=None):
-        rc = L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), out.data_ptr(), dO.data_ptr(), lse.data_ptr(),
-                                        dq.data_ptr(), fa._dtype_code(out), *sh, fa.SCALE_REFERENCE, ws.data_ptr(),
-                                        ws.numel(), stream.cuda_stream)
+        rc = L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dO.data_ptr(),
+                                        lse.data_ptr(), dq.data_ptr(), fa.F16, fa._dtype_code(out), *sh,
+                                        fa.SCALE_REFERENCE, ws.data_ptr(), ws.numel(), stream.cuda_stream)
         if ev_a is not None:
             ev_a.record(stream)
         rc = rc or L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                             dv.data_ptr(), *sh, 0.0, fa.MASK_NONE, ws.data_ptr(), ws.numel(),
-                                             stream.cuda_stream)
+                                             dv.data_ptr(), fa.F16, *sh, 0.0, fa.MASK_NONE, ws.data_ptr(),
+                                             ws.numel(), stream.cuda_stream)
         if ev_b is not None:
             ev_b.record(stream)
         if rc != fa.OK:

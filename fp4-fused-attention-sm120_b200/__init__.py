@@ -81,13 +81,13 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_debug_scores.restype = i32
     L.fp4attn_forward_lse.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, f32, i32, i32, vp, sz, vp]
     L.fp4attn_forward_lse.restype = i32
-    L.fp4attn_backward_workspace_size.argtypes = [i32] * 5
+    L.fp4attn_backward_workspace_size.argtypes = [i32] * 6
     L.fp4attn_backward_workspace_size.restype = sz
-    L.fp4attn_backward.argtypes = [vp] * 9 + [i32] * 6 + [f32, i32, i32, vp, sz, vp]
+    L.fp4attn_backward.argtypes = [vp] * 9 + [i32] * 7 + [f32, i32, i32, vp, sz, vp]
     L.fp4attn_backward.restype = i32
-    L.fp4attn_backward_prepare.argtypes = [vp] * 6 + [i32] * 7 + [vp, sz, vp]
+    L.fp4attn_backward_prepare.argtypes = [vp] * 7 + [i32] * 8 + [vp, sz, vp]
     L.fp4attn_backward_prepare.restype = i32
-    L.fp4attn_backward_attend.argtypes = [vp] * 5 + [i32] * 5 + [f32, i32, vp, sz, vp]
+    L.fp4attn_backward_attend.argtypes = [vp] * 5 + [i32] * 6 + [f32, i32, vp, sz, vp]
     L.fp4attn_backward_attend.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
     L.fp4attn_status_query.restype = i32
@@ -279,20 +279,21 @@ def fused_fp4_attention_lse(Q, K, V, out_dtype=None, softmax_scale=None, scale_m
     return out, lse
 
 
-def backward_workspace_size(batch: int, heads: int, seq_q: int, seq_k: int, head_dim: int) -> int:
-    return int(lib().fp4attn_backward_workspace_size(batch, heads, seq_q, seq_k, head_dim))
+def backward_workspace_size(batch: int, heads: int, seq_q: int, seq_k: int, head_dim: int, in_dtype: int = F16) -> int:
+    return int(lib().fp4attn_backward_workspace_size(batch, heads, seq_q, seq_k, head_dim, in_dtype))
 
 
 def fp4_attention_backward(Q, K, V, out, dout, lse, softmax_scale=None, scale_mode="reference", stream=None,
                            causal=False, workspace=None):
     """Gradients (dQ, dK, dV), FP32, of the FP4 fused attention
-    (fp4attn_backward): FP16 Q, K, V and dout, the forward's `out` (FP16 or
-    FP32) and `lse` from fused_fp4_attention_lse with the same scale, scale
-    mode and mask.  The quantiser is a straight-through estimator."""
+    (fp4attn_backward): Q, K, V and dout of one dtype (float16 or float32),
+    the forward's `out` (FP16 or FP32) and `lse` from fused_fp4_attention_lse
+    with the same scale, scale mode and mask.  The quantiser is a
+    straight-through estimator."""
     torch = _torch()
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
-    if Q.dtype != torch.float16 or dout.dtype != torch.float16:
-        raise TypeError("the backward pass takes float16 Q, K, V and dout")
+    if dout.dtype != Q.dtype:
+        raise TypeError("dout must have Q's dtype")
     if out.shape != Q.shape or dout.shape != Q.shape or not out.is_contiguous() or not dout.is_contiguous():
         raise ValueError("out and dout must be contiguous with Q's shape")
     if lse.shape != (B, H, Sq) or lse.dtype != torch.float32 or not lse.is_contiguous():
@@ -301,9 +302,11 @@ def fp4_attention_backward(Q, K, V, out, dout, lse, softmax_scale=None, scale_mo
     dk = torch.empty(K.shape, dtype=torch.float32, device=Q.device)
     dv = torch.empty(V.shape, dtype=torch.float32, device=Q.device)
     if workspace is None:
-        workspace = torch.empty(backward_workspace_size(B, H, Sq, Sk, D), dtype=torch.uint8, device=Q.device)
+        workspace = torch.empty(backward_workspace_size(B, H, Sq, Sk, D, _dtype_code(Q)), dtype=torch.uint8,
+                                device=Q.device)
     rc = lib().fp4attn_backward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dout.data_ptr(),
-                                lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _dtype_code(out), B, H,
+                                lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _dtype_code(Q),
+                                _dtype_code(out), B, H,
                                 Sq, Sk, D, float(softmax_scale or 0.0), _scale_mode(scale_mode),
                                 MASK_CAUSAL if causal else MASK_NONE, workspace.data_ptr(), workspace.numel(),
                                 _stream_ptr(stream))
@@ -334,7 +337,7 @@ def _autograd_function():
         @staticmethod
         def backward(ctx, dout):
             Q, K, V, out, lse = ctx.saved_tensors
-            dq, dk, dv = fp4_attention_backward(Q, K, V, out, dout.to(torch.float16).contiguous(), lse,
+            dq, dk, dv = fp4_attention_backward(Q, K, V, out, dout.to(Q.dtype).contiguous(), lse,
                                                 softmax_scale=ctx.softmax_scale, causal=ctx.causal)
             return dq.to(Q.dtype), dk.to(K.dtype), dv.to(V.dtype), None, None
 
@@ -350,7 +353,7 @@ def __getattr__(name):
 
 def fp4_attention(Q, K, V, softmax_scale=None, causal=False):
     """softmax(Q K^T * scale) V with FP4 Q, K that autograd can differentiate
-    (float16 [batch, heads, seq, head_dim], head_dim 64 or 128)."""
+    (float16 or float32 [batch, heads, seq, head_dim], head_dim 64 or 128)."""
     return _autograd_function().apply(Q, K, V, softmax_scale, causal)
 
 

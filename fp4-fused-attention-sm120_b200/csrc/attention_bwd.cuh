@@ -574,24 +574,24 @@ __global__ void __launch_bounds__(512, 1)
 // tiles) quantised exactly as the forward's pre-pass does (codes, scale
 // tiles with scale 127 on padding rows), plus the dequantised values -- the
 // numbers the forward's MMA multiplied -- as BF16 (exact: 3 significant bits
-// and an exponent inside BF16's range for FP16 input).  One lane per block of
-// 32 elements.
+// and an exponent inside BF16's range; FP32 input whose block maximum reaches
+// 2^126 would saturate).  One lane per block of 32 elements.
 struct BwdQuantJob {
-    const __half* x;        // [slices][seq][D]
+    const void* x;          // [slices][seq][D] of InT
     uint8_t* codes;         // [slices][seq][D/2]
     uint8_t* sf;            // [slices][ntiles][512]
     __nv_bfloat16* deq;     // [slices][seq][D]
     int seq, tile_rows, tile_shift, ntiles;
 };
 
-template <int kNB>
+template <typename InT, int kNB>
 __global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq, const BwdQuantJob jk, int ocp_mode)
 {
     const BwdQuantJob& j = blockIdx.z == 0 ? jq : jk;
     constexpr int D = kNB * 32;
     const int64_t slice = blockIdx.y;
     const int total = j.ntiles * j.tile_rows * kNB;
-    const __half* xs = j.x + slice * j.seq * D;
+    const InT* xs = static_cast<const InT*>(j.x) + slice * j.seq * D;
     uint8_t* cs = j.codes + slice * j.seq * (D / 2);
     uint8_t* fs = j.sf + slice * j.ntiles * 512;
     __nv_bfloat16* ds = j.deq + slice * j.seq * D;
@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq,
         uint32_t sb = 127u;
         if (r < j.seq) {
             uint4 packed;
-            sb = quantize32<__half>(xs + static_cast<int64_t>(r) * D + b * 32, ocp_mode, packed);
+            sb = quantize32<InT>(xs + static_cast<int64_t>(r) * D + b * 32, ocp_mode, packed);
             if (sb == 255u) sb = 254u;  // as the forward stores it (codes are all zero then)
             *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (D / 2) + b * 16) = packed;
             // 2^(sb - 127) exactly (sb 0 is the subnormal 2^-127).
@@ -629,11 +629,31 @@ __global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq,
     }
 }
 
-// Per query row: Dd = sum_c dO_c O_c (FP32) and lse2 = lse * log2(e); padding
-// rows up to sq_pad get Dd = 0 and lse2 = +inf (their probabilities are 0).
-// One warp per row, D / 32 elements per lane.
-template <int D, typename OT>
-__global__ void __launch_bounds__(256) bwd_rows_kernel(const __half* __restrict__ dout, const OT* __restrict__ out,
+// FP32 input: V and dO rounded to the FP16 copies the kernel's MMAs read
+// (V as the forward rounds it).  Job blockIdx.y, n4 float4 each.
+struct BwdConvJob {
+    const float4* src;
+    uint2* dst;
+    int64_t n4;
+};
+
+__global__ void __launch_bounds__(256) bwd_convert_kernel(const BwdConvJob jv, const BwdConvJob jo)
+{
+    const BwdConvJob& j = blockIdx.y == 0 ? jv : jo;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < j.n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 f = j.src[i];
+        __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+        j.dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+}
+
+// Per query row: Dd = sum_c dO_c O_c (FP32, dO as the FP16 value the MMAs
+// read) and lse2 = lse * log2(e); padding rows up to sq_pad get Dd = 0 and
+// lse2 = +inf (their probabilities are 0).  One warp per row, D / 32 elements
+// per lane.
+template <int D, typename OT, typename IT>
+__global__ void __launch_bounds__(256) bwd_rows_kernel(const IT* __restrict__ dout, const OT* __restrict__ out,
                                                         const float* __restrict__ lse, float* __restrict__ lse2,
                                                         float* __restrict__ dd, int seq_q, int sq_pad)
 {
@@ -656,7 +676,10 @@ __global__ void __launch_bounds__(256) bwd_rows_kernel(const __half* __restrict_
         float ov;
         if constexpr (sizeof(OT) == 4) ov = out[base + col];
         else ov = __half2float(out[base + col]);
-        acc = fmaf(__half2float(dout[base + col]), ov, acc);
+        float gv;
+        if constexpr (sizeof(IT) == 4) gv = __half2float(__float2half_rn(dout[base + col]));
+        else gv = __half2float(dout[base + col]);
+        acc = fmaf(gv, ov, acc);
     }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);

@@ -44,7 +44,7 @@ int failf(int code, const char* fmt, ...)
     } while (0)
 
 struct BwdWorkspace {
-    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, total;
+    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, v16, do16, total;
 };
 
 struct BwdShape {
@@ -65,7 +65,8 @@ BwdShape bwd_shape(int batch, int heads, int sq, int sk, int d)
     return s;
 }
 
-BwdWorkspace plan_bwd_workspace(const BwdShape& s)
+// FP32 input adds the FP16 copies of V and dO.
+BwdWorkspace plan_bwd_workspace(const BwdShape& s, int in_dtype)
 {
     BwdWorkspace w{};
     size_t off = 0;
@@ -83,48 +84,79 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s)
     w.kq = take(n * s.sk * s.d * 2);
     w.lse2 = take(n * s.sq_pad * 4);
     w.dd = take(n * s.sq_pad * 4);
+    w.v16 = w.do16 = off;
+    if (in_dtype == FP4ATTN_F32) {
+        w.v16 = take(n * s.sk * s.d * 2);
+        w.do16 = take(n * s.sq * s.d * 2);
+    }
     w.total = off;
     return w;
 }
 
 // Everything before the backward kernel: Q and K codes, scale tiles and BF16
 // dequantised copies; Dd and lse2 per query row; dQ cleared.
-template <int D>
-int bwd_prepare(const BwdShape& s, const void* Q, const void* K, const void* Out, int out_dtype, const void* dOut,
-                const float* lse, float* dQ, int ocp, uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+template <int D, typename IT>
+int bwd_prepare_t(const BwdShape& s, const void* Q, const void* K, const void* V, const void* Out, int out_dtype,
+                  const void* dOut, const float* lse, float* dQ, int ocp, uint8_t* ws, const BwdWorkspace& w,
+                  cudaStream_t st)
 {
-    fp4attn::BwdQuantJob jq{static_cast<const __half*>(Q), ws + w.q_codes, ws + w.q_sf,
-                            reinterpret_cast<__nv_bfloat16*>(ws + w.qq), s.sq, 64, 6, s.nq};
-    fp4attn::BwdQuantJob jk{static_cast<const __half*>(K), ws + w.k_codes, ws + w.k_sf,
-                            reinterpret_cast<__nv_bfloat16*>(ws + w.kq), s.sk, 128, 7, s.nk};
+    fp4attn::BwdQuantJob jq{Q, ws + w.q_codes, ws + w.q_sf, reinterpret_cast<__nv_bfloat16*>(ws + w.qq), s.sq, 64, 6,
+                            s.nq};
+    fp4attn::BwdQuantJob jk{K, ws + w.k_codes, ws + w.k_sf, reinterpret_cast<__nv_bfloat16*>(ws + w.kq), s.sk, 128, 7,
+                            s.nk};
     {
         const int64_t per_slice =
             std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (D / 32);
         const int gx = static_cast<int>(
             std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / s.slices + 1)));
-        fp4attn::bwd_quantize_kernel<D / 32><<<dim3(gx, static_cast<unsigned>(s.slices), 2), 256, 0, st>>>(jq, jk, ocp);
+        fp4attn::bwd_quantize_kernel<IT, D / 32>
+            <<<dim3(gx, static_cast<unsigned>(s.slices), 2), 256, 0, st>>>(jq, jk, ocp);
+        BWD_CUDA(cudaGetLastError());
+    }
+    if constexpr (sizeof(IT) == 4) {
+        const int64_t nv = static_cast<int64_t>(s.slices) * s.sk * D / 4, no = static_cast<int64_t>(s.slices) * s.sq * D / 4;
+        const fp4attn::BwdConvJob jv{static_cast<const float4*>(V), reinterpret_cast<uint2*>(ws + w.v16), nv};
+        const fp4attn::BwdConvJob jo{static_cast<const float4*>(dOut), reinterpret_cast<uint2*>(ws + w.do16), no};
+        const int gx = static_cast<int>(std::min<int64_t>((std::max(nv, no) + 255) / 256, 148 * 16));
+        fp4attn::bwd_convert_kernel<<<dim3(gx, 2), 256, 0, st>>>(jv, jo);
         BWD_CUDA(cudaGetLastError());
     }
     float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
     float* dd = reinterpret_cast<float*>(ws + w.dd);
     const dim3 grid((s.sq_pad + 7) / 8, static_cast<unsigned>(s.slices));
+    const IT* go = static_cast<const IT*>(dOut);
     if (out_dtype == FP4ATTN_F32)
-        fp4attn::bwd_rows_kernel<D, float><<<grid, 256, 0, st>>>(
-            static_cast<const __half*>(dOut), static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+        fp4attn::bwd_rows_kernel<D, float, IT>
+            <<<grid, 256, 0, st>>>(go, static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
     else
-        fp4attn::bwd_rows_kernel<D, __half><<<grid, 256, 0, st>>>(
-            static_cast<const __half*>(dOut), static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+        fp4attn::bwd_rows_kernel<D, __half, IT>
+            <<<grid, 256, 0, st>>>(go, static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
     BWD_CUDA(cudaGetLastError());
     // The kernel adds every key tile's contribution into dQ.
     BWD_CUDA(cudaMemsetAsync(dQ, 0, static_cast<size_t>(s.slices) * s.sq * D * 4, st));
     return FP4ATTN_OK;
 }
 
-// The backward kernel on a prepared workspace.
 template <int D>
-int bwd_attend(const BwdShape& s, const void* V, const void* dOut, float* dQ, float* dK, float* dV, float scale,
-               bool causal, const uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+int bwd_prepare(const BwdShape& s, int in_dtype, const void* Q, const void* K, const void* V, const void* Out,
+                int out_dtype, const void* dOut, const float* lse, float* dQ, int ocp, uint8_t* ws,
+                const BwdWorkspace& w, cudaStream_t st)
 {
+    if (in_dtype == FP4ATTN_F32)
+        return bwd_prepare_t<D, float>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    return bwd_prepare_t<D, __half>(s, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+}
+
+// The backward kernel on a prepared workspace (FP32 input: V and dO from
+// their FP16 copies there).
+template <int D>
+int bwd_attend(const BwdShape& s, int in_dtype, const void* V, const void* dOut, float* dQ, float* dK, float* dV,
+               float scale, bool causal, const uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+{
+    if (in_dtype == FP4ATTN_F32) {
+        V = ws + w.v16;
+        dOut = ws + w.do16;
+    }
     using C = fp4attn::BwdCfg<D>;
     CUtensorMap tk, tq, tv, tkq, tdo, tqq;
     int rc;
@@ -175,9 +207,10 @@ int bwd_attend(const BwdShape& s, const void* V, const void* dOut, float* dQ, fl
 }
 
 // Argument and workspace checks shared by the entry points.
-int bwd_check(int batch, int heads, int seq_q, int seq_k, int head_dim, const void* workspace, size_t workspace_bytes,
-              BwdShape* s, BwdWorkspace* w)
+int bwd_check(int in_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim, const void* workspace,
+              size_t workspace_bytes, BwdShape* s, BwdWorkspace* w)
 {
+    if (in_dtype != FP4ATTN_F32 && in_dtype != FP4ATTN_F16) return failf(FP4ATTN_EINVAL, "in_dtype %d", in_dtype);
     if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1)
         return failf(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads,
                      seq_q, seq_k);
@@ -185,7 +218,7 @@ int bwd_check(int batch, int heads, int seq_q, int seq_k, int head_dim, const vo
         return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 64 and 128 (got %d)", head_dim);
     if (static_cast<int64_t>(batch) * heads > 65535) return failf(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
     *s = bwd_shape(batch, heads, seq_q, seq_k, head_dim);
-    *w = plan_bwd_workspace(*s);
+    *w = plan_bwd_workspace(*s, in_dtype);
     if (!workspace || workspace_bytes < w->total)
         return failf(FP4ATTN_EWORKSPACE, "workspace of %zu bytes needed, %zu given", w->total,
                      workspace ? workspace_bytes : 0);
@@ -197,21 +230,23 @@ int bwd_check(int batch, int heads, int seq_q, int seq_k, int head_dim, const vo
 
 extern "C" {
 
-size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim)
+size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype)
 {
     using namespace fp4attn_bwd;
     if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || (head_dim != 64 && head_dim != 128)) return 0;
-    return plan_bwd_workspace(bwd_shape(batch, heads, seq_q, seq_k, head_dim)).total;
+    if (in_dtype != FP4ATTN_F32 && in_dtype != FP4ATTN_F16) return 0;
+    return plan_bwd_workspace(bwd_shape(batch, heads, seq_q, seq_k, head_dim), in_dtype).total;
 }
 
-int fp4attn_backward_prepare(const void* Q, const void* K, const void* Out, const void* dOut, const float* lse,
-                             float* dQ, int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim,
-                             int scale_mode, void* workspace, size_t workspace_bytes, void* stream)
+int fp4attn_backward_prepare(const void* Q, const void* K, const void* V, const void* Out, const void* dOut,
+                             const float* lse, float* dQ, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                             int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes,
+                             void* stream)
 {
     using namespace fp4attn_bwd;
     fp4attn::set_error_detail("");
-    if (!Q || !K || !Out || !dOut || !lse || !dQ) return failf(FP4ATTN_EINVAL, "null pointer");
-    if (!bwd_aligned16(Q) || !bwd_aligned16(K) || !bwd_aligned16(Out) || !bwd_aligned16(dOut) ||
+    if (!Q || !K || !V || !Out || !dOut || !lse || !dQ) return failf(FP4ATTN_EINVAL, "null pointer");
+    if (!bwd_aligned16(Q) || !bwd_aligned16(K) || !bwd_aligned16(V) || !bwd_aligned16(Out) || !bwd_aligned16(dOut) ||
         !bwd_aligned16(dQ) || (reinterpret_cast<uintptr_t>(lse) & 3u))
         return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned (lse 4-byte)");
     if (out_dtype != FP4ATTN_F32 && out_dtype != FP4ATTN_F16) return failf(FP4ATTN_EINVAL, "out_dtype %d", out_dtype);
@@ -219,18 +254,18 @@ int fp4attn_backward_prepare(const void* Q, const void* K, const void* Out, cons
         return failf(FP4ATTN_EINVAL, "scale_mode %d", scale_mode);
     BwdShape s;
     BwdWorkspace w;
-    int rc = bwd_check(batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
+    int rc = bwd_check(in_dtype, batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
     if (rc) return rc;
     if ((rc = host::ready())) return rc;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
-    if (head_dim == 64) return bwd_prepare<64>(s, Q, K, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
-    return bwd_prepare<128>(s, Q, K, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    if (head_dim == 64) return bwd_prepare<64>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    return bwd_prepare<128>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
 }
 
-int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int batch, int heads,
-                            int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
+int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int in_dtype, int batch,
+                            int heads, int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
                             const void* workspace, size_t workspace_bytes, void* stream)
 {
     using namespace fp4attn_bwd;
@@ -242,20 +277,20 @@ int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* d
         return failf(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
     BwdShape s;
     BwdWorkspace w;
-    int rc = bwd_check(batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
+    int rc = bwd_check(in_dtype, batch, heads, seq_q, seq_k, head_dim, workspace, workspace_bytes, &s, &w);
     if (rc) return rc;
     if ((rc = host::ready())) return rc;
     const float scale = softmax_scale > 0.f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
     const bool causal = mask_mode == FP4ATTN_MASK_CAUSAL;
     const uint8_t* ws = static_cast<const uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (head_dim == 64) return bwd_attend<64>(s, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
-    return bwd_attend<128>(s, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+    if (head_dim == 64) return bwd_attend<64>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+    return bwd_attend<128>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
 }
 
 int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
-                     float* dQ, float* dK, float* dV, int out_dtype, int batch, int heads, int seq_q, int seq_k,
-                     int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
+                     float* dQ, float* dK, float* dV, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                     int seq_k, int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
                      size_t workspace_bytes, void* stream)
 {
     using namespace fp4attn_bwd;
@@ -265,11 +300,11 @@ int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Ou
         return failf(FP4ATTN_EINVAL, "tensor pointers must be 16-byte aligned");
     if (mask_mode != FP4ATTN_MASK_NONE && mask_mode != FP4ATTN_MASK_CAUSAL)
         return failf(FP4ATTN_EINVAL, "mask_mode %d", mask_mode);
-    int rc = fp4attn_backward_prepare(Q, K, Out, dOut, lse, dQ, out_dtype, batch, heads, seq_q, seq_k, head_dim,
-                                      scale_mode, workspace, workspace_bytes, stream);
+    int rc = fp4attn_backward_prepare(Q, K, V, Out, dOut, lse, dQ, in_dtype, out_dtype, batch, heads, seq_q, seq_k,
+                                      head_dim, scale_mode, workspace, workspace_bytes, stream);
     if (rc) return rc;
-    return fp4attn_backward_attend(V, dOut, dQ, dK, dV, batch, heads, seq_q, seq_k, head_dim, softmax_scale,
-                                   mask_mode, workspace, workspace_bytes, stream);
+    return fp4attn_backward_attend(V, dOut, dQ, dK, dV, in_dtype, batch, heads, seq_q, seq_k, head_dim,
+                                   softmax_scale, mask_mode, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -188,13 +188,15 @@ int fp4attn_forward_lse(const void* Q, const void* K, const void* V, void* Out, 
                         int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim, float softmax_scale,
                         int scale_mode, int mask_mode, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Workspace bytes fp4attn_backward needs for this shape (0 if unsupported). */
-size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim);
+/* Workspace bytes fp4attn_backward needs for this shape and input type (0 if
+ * unsupported). */
+size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype);
 
-/* Gradient of the FP4 fused attention.  Inputs: the forward's FP16 Q, K, V
- * and dOut (the gradient of Out), its output Out (out_dtype FP16 or FP32) and
- * the lse rows of fp4attn_forward_lse (same shape, scale, scale_mode and
- * mask).  Outputs: FP32 dQ, dK, dV in the layout of Q, K, V.  The quantiser
+/* Gradient of the FP4 fused attention.  Inputs: the forward's Q, K, V and
+ * dOut (the gradient of Out), all of in_dtype (FP16 or FP32; FP32 V and dOut
+ * are rounded to FP16 for the tensor cores, as the forward rounds V), its
+ * output Out (out_dtype FP16 or FP32) and the lse rows of
+ * fp4attn_forward_lse (same shape, scale, scale_mode and mask).  Outputs: FP32 dQ, dK, dV in the layout of Q, K, V.  The quantiser
  * is treated as a straight-through estimator: with Qq, Kq the dequantised
  * codes the forward multiplied and P its probabilities,
  *   dV = P^T dOut,  dZ = P o (dOut V^T - rowsum(dOut o Out)),
@@ -202,22 +204,24 @@ size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_
  * head_dim 64 and 128.  Every byte of dQ, dK and dV is written.  No
  * counterpart in the reference, which is inference-only. */
 int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
-                     float* dQ, float* dK, float* dV, int out_dtype, int batch, int heads, int seq_q, int seq_k,
-                     int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
+                     float* dQ, float* dK, float* dV, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                     int seq_k, int head_dim, float softmax_scale, int scale_mode, int mask_mode, void* workspace,
                      size_t workspace_bytes, void* stream);
 
 /* The two halves of fp4attn_backward (as fp4attn_prepare / fp4attn_attend
  * are of fp4attn_forward).  fp4attn_backward_prepare quantises Q and K into
- * the workspace (codes, scale tiles and the dequantised values as BF16), forms
- * the per-row statistics of dOut, Out and lse, and clears dQ;
+ * the workspace (codes, scale tiles and the dequantised values as BF16), for
+ * FP32 input stores FP16 copies of V and dOut there, forms the per-row
+ * statistics of dOut, Out and lse, and clears dQ;
  * fp4attn_backward_attend runs the backward kernel on that workspace, adding
  * into dQ and writing dK and dV.  Same shapes, alignment and workspace as
  * fp4attn_backward. */
-int fp4attn_backward_prepare(const void* Q, const void* K, const void* Out, const void* dOut, const float* lse,
-                             float* dQ, int out_dtype, int batch, int heads, int seq_q, int seq_k, int head_dim,
-                             int scale_mode, void* workspace, size_t workspace_bytes, void* stream);
-int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int batch, int heads,
-                            int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
+int fp4attn_backward_prepare(const void* Q, const void* K, const void* V, const void* Out, const void* dOut,
+                             const float* lse, float* dQ, int in_dtype, int out_dtype, int batch, int heads, int seq_q,
+                             int seq_k, int head_dim, int scale_mode, void* workspace, size_t workspace_bytes,
+                             void* stream);
+int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int in_dtype, int batch,
+                            int heads, int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
                             const void* workspace, size_t workspace_bytes, void* stream);
 
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,

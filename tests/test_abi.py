@@ -141,18 +141,21 @@ def test_backward_workspace_size_host_only(fa):
     n = B * H
     want = n * S * 64 * 2 + n * (S // 64 + S // 128) * 512 + n * S * d * 2 * 2 + n * S * 4 * 2
     assert fa.backward_workspace_size(B, H, S, S, d) == want
+    # FP32 input adds the FP16 copies of V and dO.
+    assert fa.backward_workspace_size(B, H, S, S, d, fa.F32) == want + 2 * n * S * d * 2
     assert fa.backward_workspace_size(1, 1, 64, 64, 96) == 0
     assert fa.backward_workspace_size(0, 1, 64, 64, 64) == 0
+    assert fa.backward_workspace_size(1, 1, 64, 64, 64, 7) == 0
 
 
 def _bwd(fa, **kw):
-    args = dict(Q=16, K=16, V=16, O=16, dO=16, lse=16, dQ=16, dK=16, dV=16, outd=fa.F16, B=1, H=1, sq=64, sk=128,
-                d=128, scale=0.0, mode=0, mask=0, ws=256, wsb=1 << 30, stream=None)
+    args = dict(Q=16, K=16, V=16, O=16, dO=16, lse=16, dQ=16, dK=16, dV=16, ind=fa.F16, outd=fa.F16, B=1, H=1,
+                sq=64, sk=128, d=128, scale=0.0, mode=0, mask=0, ws=256, wsb=1 << 30, stream=None)
     args.update(kw)
     a = args
     return fa.lib().fp4attn_backward(a["Q"], a["K"], a["V"], a["O"], a["dO"], a["lse"], a["dQ"], a["dK"], a["dV"],
-                                     a["outd"], a["B"], a["H"], a["sq"], a["sk"], a["d"], a["scale"], a["mode"],
-                                     a["mask"], a["ws"], a["wsb"], a["stream"])
+                                     a["ind"], a["outd"], a["B"], a["H"], a["sq"], a["sk"], a["d"], a["scale"],
+                                     a["mode"], a["mask"], a["ws"], a["wsb"], a["stream"])
 
 
 def test_backward_rejects_bad_arguments_before_the_device(fa):
@@ -160,6 +163,7 @@ def test_backward_rejects_bad_arguments_before_the_device(fa):
     assert _bwd(fa, lse=18) == fa.EINVAL          # lse must be 4-byte aligned
     assert _bwd(fa, dK=24) == fa.EINVAL           # misaligned
     assert _bwd(fa, outd=5) == fa.EINVAL
+    assert _bwd(fa, ind=5) == fa.EINVAL
     assert _bwd(fa, mode=3) == fa.EINVAL
     assert _bwd(fa, mask=2) == fa.EINVAL
     assert _bwd(fa, sq=0) == fa.EINVAL
@@ -169,8 +173,9 @@ def test_backward_rejects_bad_arguments_before_the_device(fa):
     assert _bwd(fa, wsb=100) == fa.EWORKSPACE
     assert _bwd(fa, ws=272) == fa.EINVAL          # workspace not 256-byte aligned
     L = fa.lib()
-    assert L.fp4attn_backward_attend(16, 16, 16, 16, 16, 1, 1, 64, 128, 64, 0.0, 9, 256, 1 << 30, None) == fa.EINVAL
-    assert L.fp4attn_backward_prepare(16, 16, 16, 16, 16, 16, fa.F16, 1, 1, 64, 128, 32, 0, 256, 1 << 30,
+    assert L.fp4attn_backward_attend(16, 16, 16, 16, 16, fa.F16, 1, 1, 64, 128, 64, 0.0, 9, 256, 1 << 30,
+                                     None) == fa.EINVAL
+    assert L.fp4attn_backward_prepare(16, 16, 16, 16, 16, 16, 16, fa.F16, fa.F16, 1, 1, 64, 128, 32, 0, 256, 1 << 30,
                                       None) == fa.EUNSUPPORTED
 
 

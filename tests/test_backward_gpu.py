@@ -177,11 +177,35 @@ def test_prepare_then_attend_is_the_backward(fa, cuda):
     g = [torch.full(t.shape, float("nan"), dtype=torch.float32, device="cuda") for t in (Q, K, V)]
     L = fa.lib()
     st = torch.cuda.current_stream().cuda_stream
-    assert L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), out.data_ptr(), dO.data_ptr(), lse.data_ptr(),
-                                      g[0].data_ptr(), fa.F16, B, H, sq, sk, d, 0, ws.data_ptr(), ws.numel(),
-                                      st) == fa.OK
+    assert L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dO.data_ptr(),
+                                      lse.data_ptr(), g[0].data_ptr(), fa.F16, fa.F16, B, H, sq, sk, d, 0,
+                                      ws.data_ptr(), ws.numel(), st) == fa.OK
     assert L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), g[0].data_ptr(), g[1].data_ptr(), g[2].data_ptr(),
-                                     B, H, sq, sk, d, 0.0, 0, ws.data_ptr(), ws.numel(), st) == fa.OK
+                                     fa.F16, B, H, sq, sk, d, 0.0, 0, ws.data_ptr(), ws.numel(), st) == fa.OK
     assert fa.status_query() == fa.OK
     assert torch.equal(g[1], dk) and torch.equal(g[2], dv)
     assert float((g[0] - dq).abs().max()) <= 1e-5 * float(dq.abs().max())
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", [(1, 2, 200, 333, 64), (1, 2, 256, 384, 128)])
+def test_backward_fp32_inputs(fa, cuda, shape, causal):
+    """FP32 Q, K, V and dO (the reference's input type): Q and K quantised from
+    FP32, V and dO rounded to FP16 for the tensor cores.  The oracle takes the
+    same FP32 values (V unrounded)."""
+    B, H, sq, sk, d = shape
+    g = torch.Generator().manual_seed(13)
+    Q, K, V = (torch.randn(B, H, s, d, generator=g) for s in (sq, sk, sk))
+    dO = torch.randn(B, H, sq, d, generator=g)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, out_dtype=torch.float32, causal=causal)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse, causal=causal)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO), causal=causal)
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, name)
+    # The forward's log-sum-exp from FP32 input.
+    wl = oracle.fp4_attention_lse(_np(Q), _np(K), causal=causal).reshape(B, H, sq)
+    gl = lse.cpu().numpy()
+    fin = np.isfinite(wl)
+    assert float(np.abs(gl[fin] - wl[fin]).max()) <= LSE_ABS
