@@ -20,7 +20,7 @@ __all__ = [
     "fused_fp4_attention", "fused_fp4_attention_into", "debug_scores", "status_query",
     "selftest_timeout", "selftest_abort", "supported_head_dims", "prepare", "attend", "shard_range", "SCALE_REFERENCE", "SCALE_OCP",
     "F32", "F16", "MASK_NONE", "MASK_CAUSAL", "fused_fp4_attention_lse", "backward_workspace_size",
-    "fp4_attention_backward", "FP4Attention", "fp4_attention",
+    "fp4_attention_backward", "FP4Attention", "fp4_attention", "selftest_backward_abort",
 ]
 
 BLOCK_ELEMENT = 32  # common.h:15
@@ -89,6 +89,8 @@ def lib() -> ctypes.CDLL:
     L.fp4attn_backward_prepare.restype = i32
     L.fp4attn_backward_attend.argtypes = [vp] * 5 + [i32] * 6 + [f32, i32, vp, sz, vp]
     L.fp4attn_backward_attend.restype = i32
+    L.fp4attn_selftest_backward_abort.argtypes = [vp] * 9 + [i32] * 4 + [vp, sz, ctypes.c_uint, vp]
+    L.fp4attn_selftest_backward_abort.restype = i32
     L.fp4attn_status_query.argtypes = [vp]
     L.fp4attn_status_query.restype = i32
     L.fp4attn_selftest_timeout.argtypes = [ctypes.c_uint, vp]
@@ -393,6 +395,20 @@ def selftest_abort(V, out, workspace, batch, heads, seq_q, seq_k, timeout_us: in
     _check(lib().fp4attn_selftest_abort(V.data_ptr(), out.data_ptr(), batch, heads, seq_q, seq_k,
                                         workspace.data_ptr(), workspace.numel(), timeout_us, _stream_ptr(stream)),
            "fp4attn_selftest_abort")
+    return status_query(stream)
+
+
+def selftest_backward_abort(Q, K, V, out, dout, lse, dq, dk, dv, workspace, timeout_us: int = 20000,
+                            stream=None) -> int:
+    """Run the backward kernel's abort self-test (fp4attn_selftest_backward_abort)
+    on a head_dim-64 FP16 problem; returns status_query() (FP4ATTN_ETIMEOUT
+    when the failure path ran)."""
+    B, H, Sq, Sk, D = _check_qkv(Q, K, V)
+    _check(lib().fp4attn_selftest_backward_abort(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(),
+                                                 dout.data_ptr(), lse.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                                 dv.data_ptr(), B, H, Sq, Sk, workspace.data_ptr(), workspace.numel(),
+                                                 timeout_us, _stream_ptr(stream)),
+           "fp4attn_selftest_backward_abort")
     return status_query(stream)
 
 

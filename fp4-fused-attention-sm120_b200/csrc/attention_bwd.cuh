@@ -187,7 +187,10 @@ __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi)
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int D>
+// kWithhold (test instantiation only, fp4attn_selftest_backward_abort): the
+// first gradient thread never makes its first s_free arrival, so the MMA
+// issuer's bounded wait for step 1 runs out and the abort path runs.
+template <int D, bool kWithhold = false>
 __global__ void __launch_bounds__(512, 1)
     fp4_attention_bwd_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kq,
@@ -437,7 +440,7 @@ __global__ void __launch_bounds__(512, 1)
                 ptx::tmem_ld32(tmem + lane_off + C::DP_COL + 32 * h, dr);
                 ptx::tc_wait_ld();
                 ptx::tc_fence_before();
-                ptx::mbar_arrive(s_free);
+                if (!kWithhold || threadIdx.x != 128 || g != 0) ptx::mbar_arrive(s_free);
                 // lse2 and Dd of this stage (the TMA's writes are visible after the wait).
                 if (!__all_sync(0xffffffffu, wait_phase(&q_full[qs], (g / C::QST) & 1, wctx, kSiteQFull))) {
                     ok = false;

@@ -148,10 +148,12 @@ int bwd_prepare(const BwdShape& s, int in_dtype, const void* Q, const void* K, c
 }
 
 // The backward kernel on a prepared workspace (FP32 input: V and dO from
-// their FP16 copies there).
-template <int D>
+// their FP16 copies there).  test_timeout_ns > 0 runs the abort self-test
+// instantiation with its waits bounded by that.
+template <int D, bool kWithhold = false>
 int bwd_attend(const BwdShape& s, int in_dtype, const void* V, const void* dOut, float* dQ, float* dK, float* dV,
-               float scale, bool causal, const uint8_t* ws, const BwdWorkspace& w, cudaStream_t st)
+               float scale, bool causal, const uint8_t* ws, const BwdWorkspace& w, cudaStream_t st,
+               unsigned long long test_timeout_ns = 0)
 {
     if (in_dtype == FP4ATTN_F32) {
         V = ws + w.v16;
@@ -187,10 +189,10 @@ int bwd_attend(const BwdShape& s, int in_dtype, const void* V, const void* dOut,
     a.dq = dQ;
     a.dk = dK;
     a.dv = dV;
-    a.timeout_ns = host::timeout_ns();
+    a.timeout_ns = kWithhold ? test_timeout_ns : host::timeout_ns();
     a.causal = causal ? 1 : 0;
     a.causal_off = s.sk - s.sq;
-    auto kern = fp4attn::fp4_attention_bwd_kernel<D>;
+    auto kern = fp4attn::fp4_attention_bwd_kernel<D, kWithhold>;
     static std::atomic<unsigned long long> smem_ctx[kBwdMaxDevices]{};
     int dev = 0;
     BWD_CUDA(cudaGetDevice(&dev));
@@ -286,6 +288,27 @@ int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* d
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (head_dim == 64) return bwd_attend<64>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
     return bwd_attend<128>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+}
+
+int fp4attn_selftest_backward_abort(const void* Q, const void* K, const void* V, const void* Out, const void* dOut,
+                                    const float* lse, float* dQ, float* dK, float* dV, int batch, int heads, int seq_q,
+                                    int seq_k, void* workspace, size_t workspace_bytes, unsigned timeout_us,
+                                    void* stream)
+{
+    using namespace fp4attn_bwd;
+    fp4attn::set_error_detail("");
+    if (timeout_us < 1 || timeout_us > 10000000u) return failf(FP4ATTN_EINVAL, "timeout_us in [1, 1e7]");
+    if (seq_q <= 64) return failf(FP4ATTN_EINVAL, "the abort self-test needs seq_q > 64 (a second step)");
+    int rc = fp4attn_backward_prepare(Q, K, V, Out, dOut, lse, dQ, FP4ATTN_F16, FP4ATTN_F16, batch, heads, seq_q,
+                                      seq_k, 64, FP4ATTN_SCALE_REFERENCE, workspace, workspace_bytes, stream);
+    if (rc) return rc;
+    if (!dK || !dV || !bwd_aligned16(dK) || !bwd_aligned16(dV)) return failf(FP4ATTN_EINVAL, "dK, dV");
+    BwdShape s;
+    BwdWorkspace w;
+    if ((rc = bwd_check(FP4ATTN_F16, batch, heads, seq_q, seq_k, 64, workspace, workspace_bytes, &s, &w))) return rc;
+    return bwd_attend<64, true>(s, FP4ATTN_F16, V, dOut, dQ, dK, dV, 0.125f, false,
+                                static_cast<const uint8_t*>(workspace), w, static_cast<cudaStream_t>(stream),
+                                static_cast<unsigned long long>(timeout_us) * 1000ull);
 }
 
 int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,

@@ -224,6 +224,19 @@ int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* d
                             int heads, int seq_q, int seq_k, int head_dim, float softmax_scale, int mask_mode,
                             const void* workspace, size_t workspace_bytes, void* stream);
 
+/* Self-test of the backward kernel's failure path (the counterpart of
+ * fp4attn_selftest_abort): fp4attn_backward_prepare, then the head_dim 64
+ * backward kernel in a test instantiation where one gradient thread withholds
+ * its first arrival, with every wait bounded by timeout_us.  The wait runs
+ * out, every role of every CTA leaves its loop, in-flight copies and MMAs are
+ * drained, TMEM is freed; fp4attn_status_query then reports
+ * FP4ATTN_ETIMEOUT and the context stays usable.  FP16 inputs, seq_q > 64.
+ * dQ, dK and dV hold no result afterwards. */
+int fp4attn_selftest_backward_abort(const void* Q, const void* K, const void* V, const void* Out, const void* dOut,
+                                    const float* lse, float* dQ, float* dK, float* dV, int batch, int heads, int seq_q,
+                                    int seq_k, void* workspace, size_t workspace_bytes, unsigned timeout_us,
+                                    void* stream);
+
 /* S = Q K^T (no softmax scale) on the FP4-quantised Q and K of one problem,
  * written as FP32 [batch, heads, seq_q, seq_k].  Because FP4 products with
  * power-of-two scales are exact, S is checkable bit for bit.

@@ -209,3 +209,25 @@ def test_backward_fp32_inputs(fa, cuda, shape, causal):
     gl = lse.cpu().numpy()
     fin = np.isfinite(wl)
     assert float(np.abs(gl[fin] - wl[fin]).max()) <= LSE_ABS
+
+
+def test_backward_kernel_abort_path_drains_and_recovers(fa, cuda):
+    """The backward kernel's own failure path: a test instantiation withholds
+    one gradient thread's first arrival, the MMA issuer's bounded wait (20 ms)
+    runs out, and every role of every CTA leaves, drains its copies and MMAs
+    and frees TMEM.  The device reports FP4ATTN_ETIMEOUT; the same context
+    then runs the normal backward on the same workspace, matching the
+    oracle."""
+    B, H, sq, sk, d = 1, 4, 256, 384, 64
+    Q, K, V, dO = _inputs(17, B, H, sq, sk, d)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc)
+    ws = torch.empty(fa.backward_workspace_size(B, H, sq, sk, d), dtype=torch.uint8, device="cuda")
+    g = [torch.empty(t.shape, dtype=torch.float32, device="cuda") for t in (Q, K, V)]
+    assert fa.selftest_backward_abort(Qc, Kc, Vc, out, dOc, lse, *g, ws, timeout_us=20000) == fa.ETIMEOUT
+    assert fa.status_query() == fa.OK  # the word was read and cleared
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse, workspace=ws)
+    assert fa.status_query() == fa.OK
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO))
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, name)
