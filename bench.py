@@ -321,20 +321,28 @@ def reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def bench_backward(args):
+def bench_backward(args, world, rank, local):
     """One backward pass (fp4attn_backward: quantise Q and K with their BF16
     dequantised copies, the per-row Dd / lse2 pass, and the backward kernel)
     per step, inputs and the forward's output and log-sum-exp resident in
-    HBM; one JSON line."""
+    HBM; one JSON line.  Under torchrun each rank runs the workload's slices
+    as its shard of a world-times larger batch (weak scaling; NCCL carries
+    only the barriers and the max over ranks of the timings)."""
     import torch
     import fp4attn_b200 as fa
     import fp4attn_b200.workloads as wl
     w = wl.WORKLOADS[args.workload]
     if w.head_dim not in (64, 128):
         raise SystemExit("the backward pass covers head_dim 64 and 128")
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    Q, K, V = (t[None] for t in wl.make_inputs(w, args.seed, device=dev))
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    Q, K, V = (t[None] for t in wl.make_inputs(w, args.seed + rank, device=dev))
     n = w.slices
     g = torch.Generator(device=dev).manual_seed(args.seed + 1)
     dO = torch.randn(Q.shape, device=dev, generator=g).half()
@@ -373,6 +381,8 @@ def bench_backward(args):
     time.sleep(0.5)
     sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
     t_wall0 = time.time()
     for i in range(args.steps):  # whole passes
         if flush:
@@ -385,6 +395,7 @@ def bench_backward(args):
             flush_buf.zero_()
         step(*kev[i])
     torch.cuda.synchronize()
+    barrier()
     t_wall1 = time.time()
     torch.cuda.synchronize()
     time.sleep(0.3)
@@ -392,8 +403,15 @@ def bench_backward(args):
     status = fa.status_query()
     ms_step = sum(a.elapsed_time(b) for a, b in sev) / args.steps
     kern_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
-    flops = 10.0 * n * w.seq_q * w.seq_k * w.head_dim
-    value = flops / (ms_step * 1e-3) / 1e12
+    times = torch.tensor([ms_step, kern_ms, float(status)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms_step, kern_ms, status = times.tolist()
+    if rank != 0:
+        return
+    flops = 10.0 * n * w.seq_q * w.seq_k * w.head_dim  # per rank
+    value = world * flops / (ms_step * 1e-3) / 1e12
     burst, sustained, hbm, peak_src = measured_peaks()
     clocks = sampler.summary(t_wall0, t_wall1)
     basis = peak_basis(ms_step * args.steps * 1e-3, clocks["reasons"])
@@ -401,17 +419,18 @@ def bench_backward(args):
     # S (2/10 of the FLOPs) at 4x the FP16 rate, the other 8/10 at 1x.
     peak = flops / (0.2 * flops / (4 * bf16) + 0.8 * flops / bf16)
     line = {
-        "metric": "fused FP4 attention backward TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": 1,
+        "metric": "fused FP4 attention backward TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (S) + f16/bf16 (dP, dV, dK, dQ)",
         "data": "synthetic (seeded N(0,1) FP16 on device)",
-        "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "l2": l2},
+        "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "l2": l2,
+                   "slices_per_gpu": n, "job_slices": n * world, "parallelism": f"slice-shard x{world}"},
         "roofline": {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": flops / (kern_ms * 1e-3) / 1e12 / peak, "traffic": profile_traffic(w.name, "fp4_attention_bwd_kernel"),
                      "peak_basis": f"mixed: S at 4x and dP, dV, dK, dQ at 1x the {peak_src} {basis} bf16 dense "
                                    f"{bf16:g} TFLOP/s",
                      "kernel": "fp4_attention_bwd_kernel", "kernel_ms": kern_ms},
-        "frac_of_mixed_roofline_step": value / peak,
+        "frac_of_mixed_roofline_step": value / world / peak,
         "gpu_launches": 3 * args.steps,  # per pass: quantise, rows, backward kernel (plus one memset of dQ)
         "clocks": clocks,
         "device_status": int(status),
@@ -421,13 +440,17 @@ def bench_backward(args):
 
 def main():
     args = parse()
-    if args.direction == "backward":
-        if args.impl == "reference":
+    if args.direction == "backward" and args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps({"impl": "reference", "unavailable": "the reference has no backward pass"}), flush=True)
-            return
-        bench_backward(args)
         return
     world, rank, local = dist_setup(args)
+    if args.direction == "backward":
+        bench_backward(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     if args.impl == "reference":
         reference_arm(args, world, rank)
         if world > 1:
