@@ -332,8 +332,8 @@ def bench_backward(args, world, rank, local):
     import fp4attn_b200 as fa
     import fp4attn_b200.workloads as wl
     w = wl.WORKLOADS[args.workload]
-    if w.head_dim not in (64, 128):
-        raise SystemExit("the backward pass covers head_dim 64 and 128")
+    if w.head_dim not in (32, 64, 96, 128):
+        raise SystemExit("the backward pass covers head_dim 32 to 128")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
 

@@ -267,7 +267,7 @@ def fused_fp4_attention_lse(Q, K, V, out_dtype=None, softmax_scale=None, scale_m
                             causal=False):
     """fused_fp4_attention that also returns, per query row, the natural-log
     log-sum-exp of the scaled scores (FP32 [batch, heads, seq_q];
-    fp4attn_forward_lse) -- what the backward pass needs.  head_dim 64, 128."""
+    fp4attn_forward_lse) -- what the backward pass needs.  head_dim 32 to 128."""
     torch = _torch()
     B, H, Sq, Sk, D = _check_qkv(Q, K, V)
     out = torch.empty((B, H, Sq, D), dtype=out_dtype or Q.dtype, device=Q.device)
@@ -355,7 +355,7 @@ def __getattr__(name):
 
 def fp4_attention(Q, K, V, softmax_scale=None, causal=False):
     """softmax(Q K^T * scale) V with FP4 Q, K that autograd can differentiate
-    (float16 or float32 [batch, heads, seq, head_dim], head_dim 64 or 128)."""
+    (float16 or float32 [batch, heads, seq, head_dim], head_dim 32 to 128)."""
     return _autograd_function().apply(Q, K, V, softmax_scale, causal)
 
 

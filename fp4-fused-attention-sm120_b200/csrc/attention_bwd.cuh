@@ -1,5 +1,5 @@
 // attention_bwd.cuh -- backward pass of the FP4 fused attention on sm_100a
-// (head_dim 64 and 128).
+// (head_dim 32, 64, 96 and 128).
 //
 // The forward (attention_pair.cuh, attention.cuh) computes, per slice,
 //     z = scale * Qq Kq^T,   P = softmax(z) (row-wise),   O = P V
@@ -74,13 +74,21 @@ namespace fp4attn {
 
 template <int D>
 struct BwdCfg {
-    static_assert(D == 64 || D == 128, "the backward kernel covers head_dim 64 and 128");
+    static_assert(D == 32 || D == 64 || D == 96 || D == 128, "the backward kernel covers head_dim 32 to 128");
     static constexpr int THREADS = 512;
     static constexpr int BK = 128;                  // keys per item (MMA M)
     static constexpr int BQ = 64;                   // queries per step
-    static constexpr int QK_ROW = D / 2;            // bytes per packed code row (swizzle = row)
-    static constexpr int KSTEPS = D / 64;           // mxf4 MMAs per S^T tile (K = 64 each)
-    static constexpr int DCH = D / 64;              // 64-column (128-byte) chunks of a 16-bit row
+    static constexpr int DP = (D + 63) / 64 * 64;   // head_dim padded to the mxf4 K step (zero codes beyond D)
+    static constexpr int QK_ROW = DP / 2;           // bytes per packed code row (swizzle = row)
+    static constexpr int KSTEPS = DP / 64;          // mxf4 MMAs per S^T tile (K = 64 each)
+    // 16-bit operands (V, dO, Qq, Kq) in chunks of CHE columns, CB-byte
+    // swizzled rows: 64 columns (128-byte swizzle) where 64 divides head_dim,
+    // else 32 (64-byte swizzle).
+    static constexpr int CHE = D % 64 == 0 ? 64 : 32;
+    static constexpr int CB = 2 * CHE;
+    static constexpr uint32_t CSW = CB == 128 ? ptx::kSwizzle128B : ptx::kSwizzle64B;
+    static constexpr int DCH = D / CHE;             // chunks of a 16-bit row
+    static constexpr int KPC = CHE / 16;            // K = 16 MMA steps per chunk
     static constexpr int QST = 3;                   // query stages
     // TMEM
     static constexpr int S_COL = 0;
@@ -102,18 +110,19 @@ struct BwdCfg {
     static constexpr int OFF_K = 0;
     static constexpr int OFF_KSF = align1k(K_BYTES);
     static constexpr int OFF_V = align1k(OFF_KSF + SF_BYTES);
-    static constexpr int V_BYTES = DCH * BK * 128;
+    static constexpr int V_BYTES = DCH * BK * CB;
     static constexpr int OFF_KQ = OFF_V + V_BYTES;
-    // Kq: two 64-column chunks, the M of the dQ^T MMA (head_dim 64: the
-    // second chunk is zero and so are dQ^T rows 64..127).
-    static constexpr int KQ_BYTES = 2 * BK * 128;
+    // Kq: 128 / CHE chunks, the M = 128 of the dQ^T MMA; chunks past head_dim
+    // are zero and so are those dQ^T rows.
+    static constexpr int KQ_CHUNKS = 128 / CHE;
+    static constexpr int KQ_BYTES = KQ_CHUNKS * BK * CB;
     static constexpr int OFF_STAGE = OFF_KQ + KQ_BYTES;
     // one query stage
     static constexpr int SQ_Q = 0;
     static constexpr int Q_BYTES = BQ * QK_ROW;
     static constexpr int SQ_QSF = align1k(Q_BYTES);
     static constexpr int SQ_DO = align1k(SQ_QSF + SF_BYTES);
-    static constexpr int DO_BYTES = DCH * BQ * 128;
+    static constexpr int DO_BYTES = DCH * BQ * CB;
     static constexpr int SQ_QQ = SQ_DO + DO_BYTES;
     static constexpr int SQ_LSE = SQ_QQ + DO_BYTES;
     static constexpr int SQ_DD = SQ_LSE + BQ * 4;
@@ -256,10 +265,11 @@ __global__ void __launch_bounds__(512, 1)
         ptx::tmem_alloc(&tmem_base_sh, 512);
         ptx::tmem_relinquish();
     }
-    if constexpr (D == 64) {
-        // The second Kq chunk (head-dim rows 64..127 of the dQ^T MMA's A) is zero.
-        for (int u = threadIdx.x; u < C::BK * 128 / 16; u += blockDim.x)
-            *reinterpret_cast<uint4*>(sKq + C::BK * 128 + 16 * u) = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (C::DCH < C::KQ_CHUNKS) {
+        // Kq chunks past head_dim (rows D..127 of the dQ^T MMA's A) are zero.
+        constexpr int kPad = (C::KQ_CHUNKS - C::DCH) * C::BK * C::CB / 16;
+        for (int u = threadIdx.x; u < kPad; u += blockDim.x)
+            *reinterpret_cast<uint4*>(sKq + C::DCH * C::BK * C::CB + 16 * u) = make_uint4(0u, 0u, 0u, 0u);
         ptx::fence_proxy_async_smem();
     }
     ptx::tc_fence_before();
@@ -286,8 +296,8 @@ __global__ void __launch_bounds__(512, 1)
                                C::SF_BYTES, kv_full);
 #pragma unroll
                 for (int c = 0; c < C::DCH; c++) {
-                    ptx::tma_load_3d(sV + c * C::BK * 128, &tm_v, kv_full, 64 * c, item.kt * C::BK, item.slice);
-                    ptx::tma_load_3d(sKq + c * C::BK * 128, &tm_kq, kv_full, 64 * c, item.kt * C::BK, item.slice);
+                    ptx::tma_load_3d(sV + c * C::BK * C::CB, &tm_v, kv_full, C::CHE * c, item.kt * C::BK, item.slice);
+                    ptx::tma_load_3d(sKq + c * C::BK * C::CB, &tm_kq, kv_full, C::CHE * c, item.kt * C::BK, item.slice);
                 }
                 it++;
                 for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
@@ -304,10 +314,10 @@ __global__ void __launch_bounds__(512, 1)
                                    C::SF_BYTES, &q_full[qs]);
 #pragma unroll
                     for (int c = 0; c < C::DCH; c++) {
-                        ptx::tma_load_3d(st + C::SQ_DO + c * C::BQ * 128, &tm_do, &q_full[qs], 64 * c, qi * C::BQ,
-                                         item.slice);
-                        ptx::tma_load_3d(st + C::SQ_QQ + c * C::BQ * 128, &tm_qq, &q_full[qs], 64 * c, qi * C::BQ,
-                                         item.slice);
+                        ptx::tma_load_3d(st + C::SQ_DO + c * C::BQ * C::CB, &tm_do, &q_full[qs], C::CHE * c,
+                                         qi * C::BQ, item.slice);
+                        ptx::tma_load_3d(st + C::SQ_QQ + c * C::BQ * C::CB, &tm_qq, &q_full[qs], C::CHE * c,
+                                         qi * C::BQ, item.slice);
                     }
                     const size_t row = static_cast<size_t>(item.slice) * args.sq_pad + qi * C::BQ;
                     ptx::bulk_load(st + C::SQ_LSE, args.lse2 + row, C::BQ * 4, &q_full[qs]);
@@ -354,10 +364,11 @@ __global__ void __launch_bounds__(512, 1)
                 // dP^T = V dO^T: both K-major (K = head_dim), 16 columns per MMA.
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = (kk % 4) * 32;  // 16 columns = 32 bytes into the chunk's rows
-                    const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sV + (kk / 4) * C::BK * 128) + off, 16, 1024, sw128);
-                    const uint64_t b =
-                        ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO + (kk / 4) * C::BQ * 128) + off, 16, 1024, sw128);
+                    const uint32_t off = (kk % C::KPC) * 32;  // 16 columns = 32 bytes into the chunk's rows
+                    const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sV + (kk / C::KPC) * C::BK * C::CB) + off, 16,
+                                                       8 * C::CB, C::CSW);
+                    const uint64_t b = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO + (kk / C::KPC) * C::BQ * C::CB) + off,
+                                                       16, 8 * C::CB, C::CSW);
                     ptx::mma_f16_ss(tmem + C::DP_COL, a, b, idesc_dp, kk > 0 ? 1u : 0u);
                 }
                 ptx::tc_commit(s_full);
@@ -380,25 +391,26 @@ __global__ void __launch_bounds__(512, 1)
                     ptx::tc_fence_after();
                     // dV += P^T dO (P from TMEM: lanes = keys, columns = queries),
                     // dK += dZ^T Qq (dZ K-major in shared memory); B MN-major
-                    // (N = head_dim in 64-column chunks, K = queries).
+                    // (N = head_dim in CHE-column chunks, K = queries).
 #pragma unroll
                     for (int kk = 0; kk < C::BQ / 16; kk++) {
                         const uint64_t ad = ptx::make_sdesc(ptx::smem_u32(sDS) + kk * 32, 16, 1024, sw128);
-                        const uint64_t bo =
-                            ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
-                        const uint64_t bq =
-                            ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QQ) + kk * 16 * 128, C::BQ * 128, 1024, sw128);
+                        const uint64_t bo = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO) + kk * 16 * C::CB,
+                                                            C::BQ * C::CB, 8 * C::CB, C::CSW);
+                        const uint64_t bq = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QQ) + kk * 16 * C::CB,
+                                                            C::BQ * C::CB, 8 * C::CB, C::CSW);
                         const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
                         ptx::mma_f16_ts(tmem + C::DV_COL, tmem + C::P_COL + kk * 8, bo, idesc_dv, acc);
                         ptx::mma_f16_ss(tmem + C::DK_COL, ad, bq, idesc_dk, acc);
                     }
                     if (g > 0 && !wait_phase(dq_free, (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
                     ptx::tc_fence_after();
-                    // dQ^T = Kq^T dZ^T: A MN-major (M = head_dim in 64-row chunks, K = keys),
+                    // dQ^T = Kq^T dZ^T: A MN-major (M = head_dim in CHE-row chunks, K = keys),
                     // B MN-major (N = queries, K = keys).
 #pragma unroll
                     for (int kk = 0; kk < C::BK / 16; kk++) {
-                        const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sKq) + kk * 16 * 128, C::BK * 128, 1024, sw128);
+                        const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sKq) + kk * 16 * C::CB, C::BK * C::CB, 8 * C::CB,
+                                                           C::CSW);
                         const uint64_t b = ptx::make_sdesc(ptx::smem_u32(sDS) + kk * 16 * 128, C::BK * 128, 1024, sw128);
                         ptx::mma_f16_ss(tmem + C::DQ_COL, a, b, idesc_dq, kk > 0 ? 1u : 0u);
                     }
@@ -524,7 +536,7 @@ __global__ void __launch_bounds__(512, 1)
                 ptx::tc_wait_ld();
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(dq_free);
-                if (D == 128 || wq < 2) {
+                if (tr < D) {  // (rows past head_dim are the zero Kq chunks' products)
                     // Query row q0 + j of dQ gets column tr of the tile: the warp's
                     // 32 lanes add 32 consecutive floats of that row.
                     const int q0 = qi * C::BQ;
@@ -581,21 +593,22 @@ __global__ void __launch_bounds__(512, 1)
 // 2^126 would saturate).  One lane per block of 32 elements.
 struct BwdQuantJob {
     const void* x;          // [slices][seq][D] of InT
-    uint8_t* codes;         // [slices][seq][D/2]
+    uint8_t* codes;         // [slices][seq][DP/2] (blocks past D zero)
     uint8_t* sf;            // [slices][ntiles][512]
     __nv_bfloat16* deq;     // [slices][seq][D]
     int seq, tile_rows, tile_shift, ntiles;
 };
 
-template <typename InT, int kNB>
+template <typename InT, int D>
 __global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq, const BwdQuantJob jk, int ocp_mode)
 {
     const BwdQuantJob& j = blockIdx.z == 0 ? jq : jk;
-    constexpr int D = kNB * 32;
+    constexpr int DP = (D + 63) / 64 * 64;
+    constexpr int kNB = DP / 32;  // blocks of 32 per code row (those past D: zero codes, scale 127)
     const int64_t slice = blockIdx.y;
     const int total = j.ntiles * j.tile_rows * kNB;
     const InT* xs = static_cast<const InT*>(j.x) + slice * j.seq * D;
-    uint8_t* cs = j.codes + slice * j.seq * (D / 2);
+    uint8_t* cs = j.codes + slice * j.seq * (DP / 2);
     uint8_t* fs = j.sf + slice * j.ntiles * 512;
     __nv_bfloat16* ds = j.deq + slice * j.seq * D;
     // Twice the E2M1 magnitude of code bits 0-2 (0, 1, 2, 3, 4, 6, 8, 12), one
@@ -605,11 +618,13 @@ __global__ void __launch_bounds__(256) bwd_quantize_kernel(const BwdQuantJob jq,
     for (int blk = blockIdx.x * blockDim.x + threadIdx.x; blk < total; blk += gridDim.x * blockDim.x) {
         const int b = blk % kNB, r = blk / kNB;
         uint32_t sb = 127u;
-        if (r < j.seq) {
+        if (r < j.seq && b * 32 >= D) {
+            *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (DP / 2) + b * 16) = make_uint4(0u, 0u, 0u, 0u);
+        } else if (r < j.seq) {
             uint4 packed;
             sb = quantize32<InT>(xs + static_cast<int64_t>(r) * D + b * 32, ocp_mode, packed);
             if (sb == 255u) sb = 254u;  // as the forward stores it (codes are all zero then)
-            *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (D / 2) + b * 16) = packed;
+            *reinterpret_cast<uint4*>(cs + static_cast<int64_t>(r) * (DP / 2) + b * 16) = packed;
             // 2^(sb - 127) exactly (sb 0 is the subnormal 2^-127).
             const float sc = sb ? __uint_as_float(sb << 23) : __uint_as_float(1u << 22);
             const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};

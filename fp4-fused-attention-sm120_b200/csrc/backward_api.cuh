@@ -76,8 +76,9 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s, int in_dtype)
         return at;
     };
     const size_t n = static_cast<size_t>(s.slices);
-    w.q_codes = take(n * s.sq * (s.d / 2));
-    w.k_codes = take(n * s.sk * (s.d / 2));
+    const int dp = (s.d + 63) / 64 * 64;  // code rows padded to the mxf4 K step
+    w.q_codes = take(n * s.sq * (dp / 2));
+    w.k_codes = take(n * s.sk * (dp / 2));
     w.q_sf = take(n * s.nq * 512);
     w.k_sf = take(n * s.nk * 512);
     w.qq = take(n * s.sq * s.d * 2);
@@ -100,16 +101,17 @@ int bwd_prepare_t(const BwdShape& s, const void* Q, const void* K, const void* V
                   const void* dOut, const float* lse, float* dQ, int ocp, uint8_t* ws, const BwdWorkspace& w,
                   cudaStream_t st)
 {
+    using C = fp4attn::BwdCfg<D>;
     fp4attn::BwdQuantJob jq{Q, ws + w.q_codes, ws + w.q_sf, reinterpret_cast<__nv_bfloat16*>(ws + w.qq), s.sq, 64, 6,
                             s.nq};
     fp4attn::BwdQuantJob jk{K, ws + w.k_codes, ws + w.k_sf, reinterpret_cast<__nv_bfloat16*>(ws + w.kq), s.sk, 128, 7,
                             s.nk};
     {
         const int64_t per_slice =
-            std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (D / 32);
+            std::max<int64_t>(static_cast<int64_t>(s.nq) * 64, static_cast<int64_t>(s.nk) * 128) * (C::DP / 32);
         const int gx = static_cast<int>(
             std::min<int64_t>((per_slice + 255) / 256, std::max<int64_t>(1, 148 * 32 / s.slices + 1)));
-        fp4attn::bwd_quantize_kernel<IT, D / 32>
+        fp4attn::bwd_quantize_kernel<IT, D>
             <<<dim3(gx, static_cast<unsigned>(s.slices), 2), 256, 0, st>>>(jq, jk, ocp);
         BWD_CUDA(cudaGetLastError());
     }
@@ -163,12 +165,13 @@ int bwd_attend(const BwdShape& s, int in_dtype, const void* V, const void* dOut,
     CUtensorMap tk, tq, tv, tkq, tdo, tqq;
     int rc;
     const uint64_t n = static_cast<uint64_t>(s.slices);
-    if ((rc = host::map3d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, D / 2, s.sk, n, D / 2, 128, D / 2)) ||
-        (rc = host::map3d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.q_codes, D / 2, s.sq, n, D / 2, 64, D / 2)) ||
-        (rc = host::map3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, V, D, s.sk, n, 64, 128, 128)) ||
-        (rc = host::map3d(&tkq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.kq, D, s.sk, n, 64, 128, 128)) ||
-        (rc = host::map3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dOut, D, s.sq, n, 64, 64, 128)) ||
-        (rc = host::map3d(&tqq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.qq, D, s.sq, n, 64, 64, 128)))
+    constexpr int QR = C::QK_ROW, CHE = C::CHE, CB = C::CB;
+    if ((rc = host::map3d(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.k_codes, QR, s.sk, n, QR, 128, QR)) ||
+        (rc = host::map3d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws + w.q_codes, QR, s.sq, n, QR, 64, QR)) ||
+        (rc = host::map3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, V, D, s.sk, n, CHE, 128, CB)) ||
+        (rc = host::map3d(&tkq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.kq, D, s.sk, n, CHE, 128, CB)) ||
+        (rc = host::map3d(&tdo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dOut, D, s.sq, n, CHE, 64, CB)) ||
+        (rc = host::map3d(&tqq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ws + w.qq, D, s.sq, n, CHE, 64, CB)))
         return rc;
     fp4attn::BwdArgs a;
     a.seq_q = s.sq;
@@ -216,8 +219,8 @@ int bwd_check(int in_dtype, int batch, int heads, int seq_q, int seq_k, int head
     if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1)
         return failf(FP4ATTN_EINVAL, "batch, heads, seq_q and seq_k must be >= 1 (got %d, %d, %d, %d)", batch, heads,
                      seq_q, seq_k);
-    if (head_dim != 64 && head_dim != 128)
-        return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 64 and 128 (got %d)", head_dim);
+    if (head_dim != 32 && head_dim != 64 && head_dim != 96 && head_dim != 128)
+        return failf(FP4ATTN_EUNSUPPORTED, "the backward pass covers head_dim 32, 64, 96 and 128 (got %d)", head_dim);
     if (static_cast<int64_t>(batch) * heads > 65535) return failf(FP4ATTN_EINVAL, "batch*heads exceeds 65535");
     *s = bwd_shape(batch, heads, seq_q, seq_k, head_dim);
     *w = plan_bwd_workspace(*s, in_dtype);
@@ -235,7 +238,9 @@ extern "C" {
 size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_k, int head_dim, int in_dtype)
 {
     using namespace fp4attn_bwd;
-    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 || (head_dim != 64 && head_dim != 128)) return 0;
+    if (batch < 1 || heads < 1 || seq_q < 1 || seq_k < 1 ||
+        (head_dim != 32 && head_dim != 64 && head_dim != 96 && head_dim != 128))
+        return 0;
     if (in_dtype != FP4ATTN_F32 && in_dtype != FP4ATTN_F16) return 0;
     return plan_bwd_workspace(bwd_shape(batch, heads, seq_q, seq_k, head_dim), in_dtype).total;
 }
@@ -262,8 +267,12 @@ int fp4attn_backward_prepare(const void* Q, const void* K, const void* V, const 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int ocp = scale_mode == FP4ATTN_SCALE_OCP;
-    if (head_dim == 64) return bwd_prepare<64>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
-    return bwd_prepare<128>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    switch (head_dim) {
+        case 32: return bwd_prepare<32>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+        case 64: return bwd_prepare<64>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+        case 96: return bwd_prepare<96>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+        default: return bwd_prepare<128>(s, in_dtype, Q, K, V, Out, out_dtype, dOut, lse, dQ, ocp, ws, w, st);
+    }
 }
 
 int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* dK, float* dV, int in_dtype, int batch,
@@ -286,8 +295,12 @@ int fp4attn_backward_attend(const void* V, const void* dOut, float* dQ, float* d
     const bool causal = mask_mode == FP4ATTN_MASK_CAUSAL;
     const uint8_t* ws = static_cast<const uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (head_dim == 64) return bwd_attend<64>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
-    return bwd_attend<128>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+    switch (head_dim) {
+        case 32: return bwd_attend<32>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+        case 64: return bwd_attend<64>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+        case 96: return bwd_attend<96>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+        default: return bwd_attend<128>(s, in_dtype, V, dOut, dQ, dK, dV, scale, causal, ws, w, st);
+    }
 }
 
 int fp4attn_selftest_backward_abort(const void* Q, const void* K, const void* V, const void* Out, const void* dOut,

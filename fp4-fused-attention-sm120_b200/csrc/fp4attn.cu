@@ -575,16 +575,15 @@ template <int D, typename OutT>
 int launch_pair(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fp4attn::FwdArgs& a,
                 int64_t slices, cudaStream_t st)
 {
-    // The forward that also writes the log-sum-exp rows (head_dim 64 and 128,
-    // the backward pass's head dims).
-    if constexpr (D == 64 || D == 128) {
+    // The forward that also writes the log-sum-exp rows (the backward pass's
+    // head dims: all of this kernel's).
+    {
         if (a.lse) {
             if (a.qtiles == 1 || a.kparts > 1)
                 return launch_pair_poly<D, OutT, 3, true, true, false, false, true>(tq, tk, tv, a, slices, st);
             return launch_pair_poly<D, OutT, 3, true, false, false, false, true>(tq, tk, tv, a, slices, st);
         }
     }
-    if (a.lse) return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128");
     // Q quantised inside the attention kernel (the large-problem schedule).
     if (a.q_in) return launch_pair_poly<D, OutT, 3, true, false, false, true>(tq, tk, tv, a, slices, st);
     // One query tile per item or key partitions: the small-problem kernel.
@@ -771,8 +770,8 @@ int do_attend(const void* V, void* Out, int in_dtype, int out_dtype, int batch, 
     a.q_in = q_in;
     a.ocp_mode = ocp_mode;
     a.lse = lse;
-    if (lse && !(d == 64 || d == 128))
-        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128 (got %d)", d);
+    if (lse && !paired(d))
+        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 32 to 128 (got %d)", d);
     if (scores) return dispatch_dim<true>(d, FP4ATTN_F32, tq, tk, tv, a, p.slices, st);
     if (test_timeout_ns) {
         if (d != 64 || out_dtype != FP4ATTN_F32 || a.qtiles != 2 || a.kparts != 1 || a.causal)
@@ -938,8 +937,8 @@ int fp4attn_forward_lse(const void* Q, const void* K, const void* V, void* Out, 
     if (!lse || (reinterpret_cast<uintptr_t>(lse) & 3u)) return fail(FP4ATTN_EINVAL, "lse must be a 4-byte aligned pointer");
     int rc = check_problem(Q, K, V, Out, in_dtype, out_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, true);
     if (rc) return rc;
-    if (head_dim != 64 && head_dim != 128)
-        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 64 and 128 (got %d)", head_dim);
+    if (!paired(head_dim))
+        return fail(FP4ATTN_EUNSUPPORTED, "the log-sum-exp output covers head_dim 32 to 128 (got %d)", head_dim);
     if ((rc = do_prepare(Q, K, V, in_dtype, batch, heads, seq_q, seq_k, head_dim, scale_mode, workspace,
                          workspace_bytes, stream, true)))
         return rc;

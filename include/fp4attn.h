@@ -181,7 +181,7 @@ int fp4attn_forward_noalloc(const void* Q, const void* K, const void* V, void* O
  * log-sum-exp of the scaled scores, lse[b][h][i] = ln(sum_j exp(scale * S_ij))
  * over the keys the row sees (FP32 [batch, heads, seq_q]; +inf for a row that
  * sees no key) -- the statistic the backward pass rebuilds the probabilities
- * from.  head_dim 64 and 128.  Same workspace as fp4attn_forward.  No
+ * from.  head_dim 32, 64, 96 and 128.  Same workspace as fp4attn_forward.  No
  * counterpart in the reference (forward only; its row max and sum stay in
  * registers, common.h:228-265). */
 int fp4attn_forward_lse(const void* Q, const void* K, const void* V, void* Out, float* lse, int in_dtype,
@@ -201,7 +201,7 @@ size_t fp4attn_backward_workspace_size(int batch, int heads, int seq_q, int seq_
  * codes the forward multiplied and P its probabilities,
  *   dV = P^T dOut,  dZ = P o (dOut V^T - rowsum(dOut o Out)),
  *   dQ = scale * dZ Kq,  dK = scale * dZ^T Qq.
- * head_dim 64 and 128.  Every byte of dQ, dK and dV is written.  No
+ * head_dim 32, 64, 96 and 128.  Every byte of dQ, dK and dV is written.  No
  * counterpart in the reference, which is inference-only. */
 int fp4attn_backward(const void* Q, const void* K, const void* V, const void* Out, const void* dOut, const float* lse,
                      float* dQ, float* dK, float* dV, int in_dtype, int out_dtype, int batch, int heads, int seq_q,

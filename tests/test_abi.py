@@ -143,7 +143,8 @@ def test_backward_workspace_size_host_only(fa):
     assert fa.backward_workspace_size(B, H, S, S, d) == want
     # FP32 input adds the FP16 copies of V and dO.
     assert fa.backward_workspace_size(B, H, S, S, d, fa.F32) == want + 2 * n * S * d * 2
-    assert fa.backward_workspace_size(1, 1, 64, 64, 96) == 0
+    assert fa.backward_workspace_size(1, 1, 64, 64, 160) == 0
+    assert fa.backward_workspace_size(1, 1, 64, 64, 96) > 0
     assert fa.backward_workspace_size(0, 1, 64, 64, 64) == 0
     assert fa.backward_workspace_size(1, 1, 64, 64, 64, 7) == 0
 
@@ -167,15 +168,15 @@ def test_backward_rejects_bad_arguments_before_the_device(fa):
     assert _bwd(fa, mode=3) == fa.EINVAL
     assert _bwd(fa, mask=2) == fa.EINVAL
     assert _bwd(fa, sq=0) == fa.EINVAL
-    assert _bwd(fa, d=96) == fa.EUNSUPPORTED
-    assert b"head_dim 64 and 128" in fa.lib().fp4attn_last_error()
+    assert _bwd(fa, d=160) == fa.EUNSUPPORTED
+    assert b"head_dim 32, 64, 96 and 128" in fa.lib().fp4attn_last_error()
     assert _bwd(fa, B=300, H=300) == fa.EINVAL
     assert _bwd(fa, wsb=100) == fa.EWORKSPACE
     assert _bwd(fa, ws=272) == fa.EINVAL          # workspace not 256-byte aligned
     L = fa.lib()
     assert L.fp4attn_backward_attend(16, 16, 16, 16, 16, fa.F16, 1, 1, 64, 128, 64, 0.0, 9, 256, 1 << 30,
                                      None) == fa.EINVAL
-    assert L.fp4attn_backward_prepare(16, 16, 16, 16, 16, 16, 16, fa.F16, fa.F16, 1, 1, 64, 128, 32, 0, 256, 1 << 30,
+    assert L.fp4attn_backward_prepare(16, 16, 16, 16, 16, 16, 16, fa.F16, fa.F16, 1, 1, 64, 128, 256, 0, 256, 1 << 30,
                                       None) == fa.EUNSUPPORTED
 
 
@@ -186,7 +187,7 @@ def test_forward_lse_rejects_bad_arguments_before_the_device(fa):
     bad[4] = None  # lse
     assert L.fp4attn_forward_lse(*bad) == fa.EINVAL
     bad = list(args)
-    bad[11] = 96   # head_dim outside the backward's dims
+    bad[11] = 160  # head_dim outside the backward's dims
     assert L.fp4attn_forward_lse(*bad) == fa.EUNSUPPORTED
     bad = list(args)
     bad[14] = 5    # mask

@@ -64,6 +64,8 @@ SHAPES = [
     (1, 2, 320, 130, 128),    # seq_k just past one key tile
     (1, 1, 1, 1, 64),         # one query, one key (dQ = dK = 0)
     (1, 1, 1, 3, 64),         # one query, three keys
+    (1, 2, 200, 333, 96),     # head_dim 96: 32-column operand chunks, codes padded to 128
+    (2, 1, 130, 260, 32),     # head_dim 32: codes padded to 64
 ]
 
 
@@ -86,7 +88,7 @@ def test_backward_with_fp32_forward_output(fa, cuda):
 
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("shape", [(1, 4, 256, 512, 128), (2, 2, 100, 300, 64), (1, 2, 64, 2048, 128),
-                                   (1, 1, 300, 100, 64)])
+                                   (1, 1, 300, 100, 64), (1, 2, 300, 500, 96), (1, 2, 200, 200, 32)])
 def test_forward_lse(fa, cuda, shape, causal):
     """The log-sum-exp variant writes the same output bytes as the plain
     forward and the oracle's per-row log-sum-exp (+inf where a row sees no
@@ -152,7 +154,7 @@ def test_full_size_prefill_slices(fa, cuda):
 
 
 def test_backward_rejects_bad_arguments(fa, cuda):
-    Q, K, V, dO = (t.cuda() for t in _inputs(1, 1, 1, 64, 64, 96))
+    Q, K, V, dO = (t.cuda() for t in _inputs(1, 1, 1, 64, 64, 160))
     out, lse = torch.zeros_like(Q), torch.zeros(1, 1, 64, device="cuda")
     with pytest.raises(fa.Fp4AttnError) as e:
         fa.fp4_attention_backward(Q, K, V, out, dO, lse)
@@ -188,7 +190,7 @@ def test_prepare_then_attend_is_the_backward(fa, cuda):
 
 
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("shape", [(1, 2, 200, 333, 64), (1, 2, 256, 384, 128)])
+@pytest.mark.parametrize("shape", [(1, 2, 200, 333, 64), (1, 2, 256, 384, 128), (1, 2, 100, 200, 96)])
 def test_backward_fp32_inputs(fa, cuda, shape, causal):
     """FP32 Q, K, V and dO (the reference's input type): Q and K quantised from
     FP32, V and dO rounded to FP16 for the tensor cores.  The oracle takes the
