@@ -233,3 +233,23 @@ def test_backward_kernel_abort_path_drains_and_recovers(fa, cuda):
     want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO))
     for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
         _assert_grad(got, w, name)
+
+
+@pytest.mark.parametrize("scale_mode,softmax_scale", [("ocp", None), ("reference", 0.05), ("ocp", 0.2)])
+def test_backward_scale_rule_and_explicit_scale(fa, cuda, scale_mode, softmax_scale):
+    """The OCP "/6" scale rule and an explicit softmax scale reach the
+    backward's quantiser and kernel the way they reach the forward's."""
+    B, H, sq, sk, d = 1, 2, 192, 320, 128
+    Q, K, V, dO = _inputs(29, B, H, sq, sk, d)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, softmax_scale=softmax_scale, scale_mode=scale_mode)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse, softmax_scale=softmax_scale,
+                                           scale_mode=scale_mode)
+    assert fa.status_query() == fa.OK
+    mode = 1 if scale_mode == "ocp" else 0
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO), scale=softmax_scale or 0.0,
+                                         scale_mode=mode)
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, name)
+    wl = oracle.fp4_attention_lse(_np(Q), _np(K), scale=softmax_scale or 0.0, scale_mode=mode).reshape(B, H, sq)
+    assert float(np.abs(lse.cpu().numpy() - wl).max()) <= LSE_ABS
