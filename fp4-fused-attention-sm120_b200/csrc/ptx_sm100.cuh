@@ -111,19 +111,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
                  : "memory");
 }
 
-// 3-D tiled reduction from this CTA's shared memory into global memory:
-// global += tile, element-wise, in the tensor map's type (FP32 add here);
-// elements outside the tensor are skipped.  Completion is tracked per thread
-// with bulk groups, like tma_store_3d.
-__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const void* src, int c0, int c1, int c2)
-{
-    asm volatile(
-        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-            reinterpret_cast<uint64_t>(m)),
-        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
-}
-
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until at most N of this thread's bulk groups still read shared memory.
