@@ -66,6 +66,7 @@
 #include <cuda_bf16.h>
 
 #include <climits>
+#include <type_traits>
 
 #include "attention.cuh"
 #include "quantize.cuh"
@@ -666,6 +667,30 @@ __global__ void __launch_bounds__(256) bwd_convert_kernel(const BwdConvJob jv, c
     }
 }
 
+// E consecutive elements of T at p as floats, with one vector load when E
+// elements span 4, 8 or 16 bytes (p is then aligned to that span).
+template <typename T, int E>
+__device__ __forceinline__ void load_floats(const T* __restrict__ p, float (&v)[E])
+{
+    constexpr int kBytes = E * static_cast<int>(sizeof(T));
+    if constexpr (kBytes == 16 || kBytes == 8 || kBytes == 4) {
+        using V = std::conditional_t<kBytes == 16, uint4, std::conditional_t<kBytes == 8, uint2, uint32_t>>;
+        const V raw = *reinterpret_cast<const V*>(p);
+        const T* t = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            if constexpr (sizeof(T) == 4) v[e] = t[e];
+            else v[e] = __half2float(t[e]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            if constexpr (sizeof(T) == 4) v[e] = p[e];
+            else v[e] = __half2float(p[e]);
+        }
+    }
+}
+
 // Per query row: Dd = sum_c dO_c O_c (FP32, dO as the FP16 value the MMAs
 // read) and lse2 = lse * log2(e); padding rows up to sq_pad get Dd = 0 and
 // lse2 = +inf (their probabilities are 0).  One warp per row, D / 32 elements
@@ -687,18 +712,20 @@ __global__ void __launch_bounds__(256) bwd_rows_kernel(const IT* __restrict__ do
         return;
     }
     const int64_t base = (slice * seq_q + row) * D;
+    // Lane l takes the D/32 consecutive elements starting at l * D/32 (one
+    // contiguous transaction per warp and tensor).
+    constexpr int E = D / 32;
+    float gv[E], ov[E];
+    const int64_t at = base + lane * E;
+    load_floats<IT, E>(dout + at, gv);
+    load_floats<OT, E>(out + at, ov);
+    if constexpr (sizeof(IT) == 4) {
+#pragma unroll
+        for (int e = 0; e < E; e++) gv[e] = __half2float(__float2half_rn(gv[e]));
+    }
     float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < D / 32; k++) {
-        const int col = lane + 32 * k;
-        float ov;
-        if constexpr (sizeof(OT) == 4) ov = out[base + col];
-        else ov = __half2float(out[base + col]);
-        float gv;
-        if constexpr (sizeof(IT) == 4) gv = __half2float(__float2half_rn(dout[base + col]));
-        else gv = __half2float(dout[base + col]);
-        acc = fmaf(gv, ov, acc);
-    }
+    for (int e = 0; e < E; e++) acc = fmaf(gv[e], ov[e], acc);
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
     if (lane == 0) {
