@@ -253,3 +253,32 @@ def test_backward_scale_rule_and_explicit_scale(fa, cuda, scale_mode, softmax_sc
         _assert_grad(got, w, name)
     wl = oracle.fp4_attention_lse(_np(Q), _np(K), scale=softmax_scale or 0.0, scale_mode=mode).reshape(B, H, sq)
     assert float(np.abs(lse.cpu().numpy() - wl).max()) <= LSE_ABS
+
+
+@pytest.mark.parametrize("case", range(16))
+def test_random_shapes_forward_lse_and_backward(fa, cuda, case):
+    """Seeded random problems (head_dim 32-128, ragged seq_q and seq_k from 1
+    to 300, both masks, both output types, both scale rules): the log-sum-exp
+    forward and the backward against the oracle."""
+    rng = np.random.default_rng(1000 + case)
+    d = int(rng.choice([32, 64, 96, 128]))
+    B, H = int(rng.integers(1, 3)), int(rng.integers(1, 4))
+    sq, sk = int(rng.integers(1, 301)), int(rng.integers(1, 301))
+    causal = bool(rng.integers(0, 2))
+    odt = torch.float16 if rng.integers(0, 2) else torch.float32
+    mode = "ocp" if rng.integers(0, 4) == 0 else "reference"
+    Q, K, V, dO = _inputs(2000 + case, B, H, sq, sk, d)
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, out_dtype=odt, causal=causal, scale_mode=mode)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse, causal=causal, scale_mode=mode)
+    assert fa.status_query() == fa.OK
+    m = 1 if mode == "ocp" else 0
+    wl = oracle.fp4_attention_lse(_np(Q), _np(K), causal=causal, scale_mode=m).reshape(B, H, sq)
+    gl = lse.cpu().numpy()
+    fin = np.isfinite(wl)
+    assert np.array_equal(np.isfinite(gl), fin)
+    if fin.any():
+        assert float(np.abs(gl[fin] - wl[fin]).max()) <= LSE_ABS
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO), causal=causal, scale_mode=m)
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, f"{name} case {case} d{d} B{B} H{H} sq{sq} sk{sk} causal {causal}")
