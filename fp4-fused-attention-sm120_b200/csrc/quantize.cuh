@@ -272,6 +272,11 @@ struct VConvJob {
 template <typename InT, int kNB>
 __global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, const QuantJob jk, const VConvJob jv)
 {
+    // The attention kernel (launched as this grid's programmatic dependent)
+    // may be scheduled once every CTA of this grid has started, so its launch
+    // and prologue overlap this grid's last wave; it waits for this grid's
+    // completion (griddepcontrol.wait) before it reads the workspace.
+    ptx::grid_launch_dependents();
     if (jv.n_zero > 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
         for (int i = threadIdx.x; i < jv.n_zero; i += blockDim.x) jv.zero[i] = 0u;
     if (blockIdx.z == 2) {
@@ -313,10 +318,6 @@ __global__ void __launch_bounds__(256) quantize_tiles_kernel(const QuantJob jq, 
         const int tile = r >> a.tile_shift, rr = r & (a.tile_rows - 1);
         fs[static_cast<int64_t>(tile) * a.sf_tile_bytes + sf_tile_offset(a.tile_rows, rr, b)] = static_cast<uint8_t>(sb);
     }
-    // This CTA's stores are issued: the attention kernel (launched as this
-    // grid's programmatic dependent) may be scheduled; it waits for this
-    // grid's completion before it reads the workspace.
-    ptx::grid_launch_dependents();
 }
 
 // Row-major quantisation for the public fp4attn_quantize: codes rows x D/2,
