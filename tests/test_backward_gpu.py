@@ -282,3 +282,33 @@ def test_random_shapes_forward_lse_and_backward(fa, cuda, case):
     want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO), causal=causal, scale_mode=m)
     for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
         _assert_grad(got, w, f"{name} case {case} d{d} B{B} H{H} sq{sq} sk{sk} causal {causal}")
+
+
+@pytest.mark.parametrize("std", [16.0, 1e-4])
+def test_extreme_input_magnitudes(fa, cuda, std):
+    """Inputs scaled far from N(0, 1): sigma 16 (scaled scores in the
+    thousands, a nearly one-hot softmax, the lazy rescale firing often) and
+    sigma 1e-4 (scales near the bottom of the FP16 range, a nearly uniform
+    softmax).  Forward output, log-sum-exp and gradients against the oracle.
+    (The log-sum-exp is one FP32 number per row: once the scaled scores reach
+    about 2^20 its rounding alone moves the backward's probabilities by
+    percents, so far larger scores are not a backward case.)"""
+    B, H, sq, sk, d = 1, 2, 192, 320, 64
+    g = torch.Generator().manual_seed(31)
+    Q, K, V = ((torch.randn(B, H, s, d, generator=g) * std).half() for s in (sq, sk, sk))
+    dO = torch.randn(B, H, sq, d, generator=g).half()
+    Qc, Kc, Vc, dOc = (t.cuda() for t in (Q, K, V, dO))
+    out, lse = fa.fused_fp4_attention_lse(Qc, Kc, Vc, out_dtype=torch.float32)
+    dq, dk, dv = fa.fp4_attention_backward(Qc, Kc, Vc, out, dOc, lse)
+    assert fa.status_query() == fa.OK
+    want_o = oracle.fp4_attention(_np(Q), _np(K), _np(V))
+    got_o = out.cpu().numpy().reshape(want_o.shape)
+    assert np.isfinite(got_o).all()
+    scale_o = max(float(np.abs(want_o).max()), 1e-30)
+    assert oracle.cosine(got_o, want_o) >= COS_MIN
+    assert float(np.abs(got_o - want_o).max()) <= REL_MAX * scale_o
+    wl = oracle.fp4_attention_lse(_np(Q), _np(K)).reshape(B, H, sq)
+    assert float(np.abs(lse.cpu().numpy() - wl).max()) <= LSE_ABS * max(1.0, float(np.abs(wl).max()) * 1e-3)
+    want = oracle.fp4_attention_backward(_np(Q), _np(K), _np(V), _np(dO))
+    for got, w, name in zip((dq, dk, dv), want, ("dQ", "dK", "dV")):
+        _assert_grad(got, w, f"{name} std {std}")
