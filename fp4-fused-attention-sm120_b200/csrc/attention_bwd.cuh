@@ -36,11 +36,22 @@
 // Roles (512 threads):
 //   warp 0       TMA producer: per item K codes + scale tile, V, Kq; per step
 //                (QST-stage ring) Q codes + scale tile, dO, Qq, lse2, Dd.
-//   warp 1       MMA issuer (one thread).  S^T and dP^T of step g+1 are issued
-//                as soon as the gradient warpgroups hold step g's in
-//                registers, before step g's dV, dK and dQ^T, so the tensor core
-//                computes them while the warpgroups work on step g.
-//   warps 2-3    idle.
+//   warp 1       S issuer (one thread): S^T and dP^T of step g+1, issued as
+//                soon as the gradient warpgroups hold step g's in registers,
+//                so the tensor core computes them while the warpgroups work
+//                on step g.
+//   warp 2       gradient issuer (one thread): dV, dK and dQ^T of step g once
+//                its P and dZ are stored.
+//                A tcgen05.mma waits at issue until the tensor pipe takes it,
+//                and the pipe holds about one instruction beyond the one it
+//                runs, so each next MMA must be issued within a few cycles of
+//                the last one leaving.  One issuing thread, sharing its
+//                sub-partition's issue slots with two gradient warps and the
+//                dQ warp, misses that window often enough to leave the pipe
+//                idle a third of the time; two issuers keep two instructions
+//                waiting.  The two streams touch disjoint TMEM columns and
+//                their order is set by the barriers below.
+//   warp 3       idle.
 //   warps 4-11   two gradient warpgroups; thread = key row = TMEM lane, and
 //                warpgroup h owns queries [32h, 32h + 32) of the step.  Each
 //                reads its S^T and dP^T columns, forms P and dZ, stores P into
@@ -134,8 +145,9 @@ struct BwdCfg {
     static constexpr int OFF_DS = OFF_STAGE + QST * STAGE_BYTES;
     static constexpr int OFF_BAR = OFF_DS + BK * 128;
     // kv_full, kv_empty, q_full[QST], q_empty[QST], s_full, s_free, ds_full,
-    // ds_free, dq_full, dq_free, acc_full, acc_free, drain
-    static constexpr int NUM_BARS = 2 + 2 * QST + 9;
+    // ds_free, dq_full, dq_free, acc_full, acc_free, drain (S issuer), drain
+    // (gradient issuer)
+    static constexpr int NUM_BARS = 2 + 2 * QST + 10;
     static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 1024;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget exceeded");
 };
@@ -150,8 +162,8 @@ struct BwdArgs {
     float scale;               // softmax_scale
     const uint8_t* q_sf;       // [slices][nq_tiles][512]  (64-row scale tiles)
     const uint8_t* k_sf;       // [slices][nk_tiles][512]  (128-row scale tiles)
-    const float* lse2;         // [slices][sq_pad]: lse * log2(e); +inf on padding rows
-    const float* dd;           // [slices][sq_pad]: rowsum(dO o O); 0 on padding rows
+    const float* nlse2;        // [slices][sq_pad]: -lse * log2(e); -inf on padding rows
+    const float* ndd;          // [slices][sq_pad]: -rowsum(dO o O); 0 on padding rows
     float* dq;                 // [slices][seq_q][D] FP32, zero on entry (accumulated by reductions)
     float* dk;                 // [slices][seq_k][D] FP32
     float* dv;                 // [slices][seq_k][D] FP32
@@ -198,7 +210,7 @@ __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi)
 }
 
 // kWithhold (test instantiation only, fp4attn_selftest_backward_abort): the
-// first gradient thread never makes its first s_free arrival, so the MMA
+// first gradient thread never makes its first s_free arrival, so the S
 // issuer's bounded wait for step 1 runs out and the abort path runs.
 template <int D, bool kWithhold = false>
 __global__ void __launch_bounds__(512, 1)
@@ -229,7 +241,8 @@ __global__ void __launch_bounds__(512, 1)
     uint64_t* dq_free = dq_full + 1;           // dQ^T copied to registers (128)
     uint64_t* acc_full = dq_free + 1;          // the item's dV, dK complete (commit)
     uint64_t* acc_free = acc_full + 1;         // dV, dK copied out (128)
-    uint64_t* drain_bar = acc_free + 1;
+    uint64_t* drain_bar = acc_free + 1;        // the S issuer's MMAs complete (exit)
+    uint64_t* drain_bar2 = drain_bar + 1;      // the gradient issuer's MMAs complete (exit)
 
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_sh;
@@ -251,6 +264,7 @@ __global__ void __launch_bounds__(512, 1)
         ptx::mbar_init(acc_full, 1);
         ptx::mbar_init(acc_free, 128);
         ptx::mbar_init(drain_bar, 1);
+        ptx::mbar_init(drain_bar2, 1);
         abort_sh = 0;
         ptx::fence_mbar_init();
     }
@@ -321,8 +335,8 @@ __global__ void __launch_bounds__(512, 1)
                                          qi * C::BQ, item.slice);
                     }
                     const size_t row = static_cast<size_t>(item.slice) * args.sq_pad + qi * C::BQ;
-                    ptx::bulk_load(st + C::SQ_LSE, args.lse2 + row, C::BQ * 4, &q_full[qs]);
-                    ptx::bulk_load(st + C::SQ_DD, args.dd + row, C::BQ * 4, &q_full[qs]);
+                    ptx::bulk_load(st + C::SQ_LSE, args.nlse2 + row, C::BQ * 4, &q_full[qs]);
+                    ptx::bulk_load(st + C::SQ_DD, args.ndd + row, C::BQ * 4, &q_full[qs]);
                 }
             }
             // Every copy this thread issued lands before the CTA exits.
@@ -333,62 +347,86 @@ __global__ void __launch_bounds__(512, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ S issuer
         if (lane == 0) {
             constexpr uint32_t qk_layout = ptx::swizzle_mode_for_bytes(C::QK_ROW);
             const uint64_t kdesc0 = ptx::make_sdesc(ptx::smem_u32(sK), 16, 8 * C::QK_ROW, qk_layout);
             const uint64_t ksfdesc = ptx::make_sdesc(ptx::smem_u32(sKsf), 0, 128, ptx::kSwizzleNone);
             constexpr uint32_t idesc_dp = ptx::idesc_f16x(128, C::BQ, 0, false, false);
+            int it = 0, g = 0;
+            bool ok = true;
+            for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
+                const BwdItem item = bwd_item(args, r);
+                if (!item.valid || item.q_begin >= args.nq_tiles) continue;
+                if (!wait_phase(kv_full, it & 1, wctx, kSiteKFull)) break;
+                ptx::tc_fence_after();
+                // (the previous item's S^T MMAs, which read these columns, were
+                // issued before by this thread and run first)
+                ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL, ksfdesc);
+                for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
+                    // S^T and dP^T of step g (stage g % QST) into their TMEM columns,
+                    // once step g-1's are in the gradient warpgroups' registers.
+                    const int qs = g % C::QST;
+                    if (!wait_phase(&q_full[qs], (g / C::QST) & 1, wctx, kSiteQFull)) { ok = false; break; }
+                    if (g > 0 && !wait_phase(s_free, (g - 1) & 1, wctx, kSiteSFree)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    uint8_t* st = sStage + qs * C::STAGE_BYTES;
+                    const uint32_t sfb = tmem + C::SFB_COL;
+                    ptx::tc_cp_32x128b_warpx4(sfb, ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QSF), 0, 128, ptx::kSwizzleNone));
+                    const uint64_t qdesc = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_Q), 16, 8 * C::QK_ROW, qk_layout);
+#pragma unroll
+                    for (int kk = 0; kk < C::KSTEPS; kk++) {
+                        const uint32_t sf_id = 2u * (kk & 1);
+                        ptx::mma_mxf4(tmem + C::S_COL, kdesc0 + static_cast<uint64_t>((kk * 32) >> 4),
+                                      qdesc + static_cast<uint64_t>((kk * 32) >> 4),
+                                      ptx::idesc_mxf4(128, C::BQ, sf_id, sf_id), (tmem + C::SFA_COL) | (sf_id << 30),
+                                      sfb | (sf_id << 30), kk > 0 ? 1u : 0u);
+                    }
+                    // dP^T = V dO^T: both K-major (K = head_dim), 16 columns per MMA.
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t off = (kk % C::KPC) * 32;  // 16 columns = 32 bytes into the chunk's rows
+                        const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sV + (kk / C::KPC) * C::BK * C::CB) + off, 16,
+                                                           8 * C::CB, C::CSW);
+                        const uint64_t b = ptx::make_sdesc(
+                            ptx::smem_u32(st + C::SQ_DO + (kk / C::KPC) * C::BQ * C::CB) + off, 16, 8 * C::CB, C::CSW);
+                        ptx::mma_f16_ss(tmem + C::DP_COL, a, b, idesc_dp, kk > 0 ? 1u : 0u);
+                    }
+                    ptx::tc_commit(s_full);
+                }
+                it++;
+            }
+            // Every tcgen05 op this thread issued completes before TMEM is freed.
+            ptx::tc_commit(drain_bar);
+            drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ gradient issuer
+        // Its operands: P (TMEM) and dZ (shared memory) from the gradient
+        // warpgroups (ds_full), dO and Qq from the query stage, Kq from the
+        // item's tiles.  The stage and the item's tiles are waited for here as
+        // well, so that their copies are seen complete by this thread.
+        if (lane == 0) {
             constexpr uint32_t idesc_dv = ptx::idesc_f16x(128, D, 0, false, true);
             constexpr uint32_t idesc_dk = ptx::idesc_f16x(128, D, 1, false, true);
             constexpr uint32_t idesc_dq = ptx::idesc_f16x(128, C::BQ, 1, true, true);
             const uint32_t sw128 = ptx::kSwizzle128B;
             int it = 0, g = 0;
             bool ok = true;
-            // S^T and dP^T of global step gg (stage gg % QST) into their TMEM columns.
-            auto issue_sdp = [&](int gg) -> bool {
-                const int qs = gg % C::QST;
-                if (!wait_phase(&q_full[qs], (gg / C::QST) & 1, wctx, kSiteQFull)) return false;
-                if (gg > 0 && !wait_phase(s_free, (gg - 1) & 1, wctx, kSiteSFree)) return false;
-                ptx::tc_fence_after();
-                uint8_t* st = sStage + qs * C::STAGE_BYTES;
-                const uint32_t sfb = tmem + C::SFB_COL;
-                ptx::tc_cp_32x128b_warpx4(sfb, ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QSF), 0, 128, ptx::kSwizzleNone));
-                const uint64_t qdesc = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_Q), 16, 8 * C::QK_ROW, qk_layout);
-#pragma unroll
-                for (int kk = 0; kk < C::KSTEPS; kk++) {
-                    const uint32_t sf_id = 2u * (kk & 1);
-                    ptx::mma_mxf4(tmem + C::S_COL, kdesc0 + static_cast<uint64_t>((kk * 32) >> 4),
-                                  qdesc + static_cast<uint64_t>((kk * 32) >> 4), ptx::idesc_mxf4(128, C::BQ, sf_id, sf_id),
-                                  (tmem + C::SFA_COL) | (sf_id << 30), sfb | (sf_id << 30), kk > 0 ? 1u : 0u);
-                }
-                // dP^T = V dO^T: both K-major (K = head_dim), 16 columns per MMA.
-#pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = (kk % C::KPC) * 32;  // 16 columns = 32 bytes into the chunk's rows
-                    const uint64_t a = ptx::make_sdesc(ptx::smem_u32(sV + (kk / C::KPC) * C::BK * C::CB) + off, 16,
-                                                       8 * C::CB, C::CSW);
-                    const uint64_t b = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_DO + (kk / C::KPC) * C::BQ * C::CB) + off,
-                                                       16, 8 * C::CB, C::CSW);
-                    ptx::mma_f16_ss(tmem + C::DP_COL, a, b, idesc_dp, kk > 0 ? 1u : 0u);
-                }
-                ptx::tc_commit(s_full);
-                return true;
-            };
             for (int r = 0; ok && r * static_cast<int>(gridDim.x) < args.n_items; r++) {
                 const BwdItem item = bwd_item(args, r);
                 if (!item.valid || item.q_begin >= args.nq_tiles) continue;
-                const int n = args.nq_tiles - item.q_begin;
                 if (!wait_phase(kv_full, it & 1, wctx, kSiteKFull)) break;
-                ptx::tc_fence_after();
-                ptx::tc_cp_32x128b_warpx4(tmem + C::SFA_COL, ksfdesc);
-                if (!issue_sdp(g)) break;
-                for (int i = 0; i < n; i++, g++) {
+                for (int qi = item.q_begin; qi < args.nq_tiles; qi++, g++) {
                     const int qs = g % C::QST;
                     uint8_t* st = sStage + qs * C::STAGE_BYTES;
-                    if (i + 1 < n && !issue_sdp(g + 1)) { ok = false; break; }
+                    if (!wait_phase(&q_full[qs], (g / C::QST) & 1, wctx, kSiteQFull)) { ok = false; break; }
                     if (!wait_phase(ds_full, g & 1, wctx, kSitePFull)) { ok = false; break; }
-                    if (i == 0 && it > 0 && !wait_phase(acc_free, (it - 1) & 1, wctx, kSitePvDone)) { ok = false; break; }
+                    if (qi == item.q_begin && it > 0 && !wait_phase(acc_free, (it - 1) & 1, wctx, kSitePvDone)) {
+                        ok = false;
+                        break;
+                    }
                     ptx::tc_fence_after();
                     // dV += P^T dO (P from TMEM: lanes = keys, columns = queries),
                     // dK += dZ^T Qq (dZ K-major in shared memory); B MN-major
@@ -400,7 +438,7 @@ __global__ void __launch_bounds__(512, 1)
                                                             C::BQ * C::CB, 8 * C::CB, C::CSW);
                         const uint64_t bq = ptx::make_sdesc(ptx::smem_u32(st + C::SQ_QQ) + kk * 16 * C::CB,
                                                             C::BQ * C::CB, 8 * C::CB, C::CSW);
-                        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc = (qi > item.q_begin || kk > 0) ? 1u : 0u;
                         ptx::mma_f16_ts(tmem + C::DV_COL, tmem + C::P_COL + kk * 8, bo, idesc_dv, acc);
                         ptx::mma_f16_ss(tmem + C::DK_COL, ad, bq, idesc_dk, acc);
                     }
@@ -417,16 +455,20 @@ __global__ void __launch_bounds__(512, 1)
                     }
                     ptx::tc_commit(ds_free);
                     ptx::tc_commit(dq_full);
+                    // (step g's S^T and dP^T, the stage's other readers, completed
+                    // before its gradient warpgroups stored P and dZ)
                     ptx::tc_commit(&q_empty[qs]);
                 }
                 if (!ok) break;
+                // Every MMA of the item has been issued: this thread's dV, dK and
+                // dQ^T last, after the S issuer's (whose completion the gradient
+                // warpgroups saw before storing the last P and dZ).
                 ptx::tc_commit(acc_full);
                 ptx::tc_commit(kv_empty);
                 it++;
             }
-            // Every tcgen05 op this thread issued completes before TMEM is freed.
-            ptx::tc_commit(drain_bar);
-            drain_phase(drain_bar, 0, 2ull * args.timeout_ns);
+            ptx::tc_commit(drain_bar2);
+            drain_phase(drain_bar2, 0, 2ull * args.timeout_ns);
         }
         __syncwarp();
     } else if (warp >= 4 && warp < 12) {
@@ -454,36 +496,58 @@ __global__ void __launch_bounds__(512, 1)
                 ptx::tc_wait_ld();
                 ptx::tc_fence_before();
                 if (!kWithhold || threadIdx.x != 128 || g != 0) ptx::mbar_arrive(s_free);
-                // lse2 and Dd of this stage (the TMA's writes are visible after the wait).
+                // -lse2 and -Dd of this stage (the TMA's writes are visible after the wait).
                 if (!__all_sync(0xffffffffu, wait_phase(&q_full[qs], (g / C::QST) & 1, wctx, kSiteQFull))) {
                     ok = false;
                     break;
                 }
                 const uint8_t* st = sStage + qs * C::STAGE_BYTES;
-                const float4* lse4 = reinterpret_cast<const float4*>(st + C::SQ_LSE) + 8 * h;
-                const float4* dd4 = reinterpret_cast<const float4*>(st + C::SQ_DD) + 8 * h;
+                // -lse2 and -Dd of this warpgroup's 32 queries (4 per float4).
+                const float4* nl4 = reinterpret_cast<const float4*>(st + C::SQ_LSE) + 8 * h;
+                const float4* nd4 = reinterpret_cast<const float4*>(st + C::SQ_DD) + 8 * h;
                 const int q0 = qi * C::BQ + 32 * h;
-                // Every query of this warp's slice of the step sees every key of
-                // the warp (no mask work), or not.
+                // P = 2^(S c - lse2) and dZ = (P scale) (dP - Dd), two queries
+                // per packed FP32x2 operation.  Every query of this warp's slice
+                // of the step sees every key of the warp (no mask work), or not.
                 const bool full = __all_sync(0xffffffffu, key_ok && q0 >= lim);
                 uint32_t pk[16], dk[16];
+                if (full) {
 #pragma unroll
-                for (int c4 = 0; c4 < 8; c4++) {
-                    const float4 L = lse4[c4], Dv = dd4[c4];
-                    const float Ls[4] = {L.x, L.y, L.z, L.w}, Ds[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
-                    float pv[4], dv[4];
+                    for (int c4 = 0; c4 < 8; c4++) {
+                        const float4 L = nl4[c4], Dv = nd4[c4];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int q = 4 * c4 + e;
-                        float p = ptx::ex2_approx(fmaf(__uint_as_float(sr[q]), c, -Ls[e]));
-                        if (!full && (!key_ok || q0 + q < lim)) p = 0.f;
-                        pv[e] = p;
-                        dv[e] = (p * sc) * (__uint_as_float(dr[q]) - Ds[e]);
+                        for (int e = 0; e < 2; e++) {
+                            const int q = 4 * c4 + 2 * e;
+                            const float2 x = ptx::ffma2(make_float2(__uint_as_float(sr[q]), __uint_as_float(sr[q + 1])),
+                                                        make_float2(c, c),
+                                                        e ? make_float2(L.z, L.w) : make_float2(L.x, L.y));
+                            const float2 pr = make_float2(ptx::ex2_approx(x.x), ptx::ex2_approx(x.y));
+                            const float2 t = ptx::fadd2(make_float2(__uint_as_float(dr[q]), __uint_as_float(dr[q + 1])),
+                                                        e ? make_float2(Dv.z, Dv.w) : make_float2(Dv.x, Dv.y));
+                            const float2 z = ptx::fmul2(ptx::fmul2(pr, make_float2(sc, sc)), t);
+                            pk[q / 2] = ptx::pack_half2(pr.x, pr.y);
+                            dk[q / 2] = pack_bf162(z.x, z.y);
+                        }
                     }
-                    pk[2 * c4] = ptx::pack_half2(pv[0], pv[1]);
-                    pk[2 * c4 + 1] = ptx::pack_half2(pv[2], pv[3]);
-                    dk[2 * c4] = pack_bf162(dv[0], dv[1]);
-                    dk[2 * c4 + 1] = pack_bf162(dv[2], dv[3]);
+                } else {
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; c4++) {
+                        const float4 L = nl4[c4], Dv = nd4[c4];
+                        const float Ls[4] = {L.x, L.y, L.z, L.w}, Ds[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
+                        float pv[4], zv[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int q = 4 * c4 + e;
+                            float pr = ptx::ex2_approx(fmaf(__uint_as_float(sr[q]), c, Ls[e]));
+                            if (!key_ok || q0 + q < lim) pr = 0.f;
+                            pv[e] = pr;
+                            zv[e] = (pr * sc) * (__uint_as_float(dr[q]) + Ds[e]);
+                        }
+                        pk[2 * c4] = ptx::pack_half2(pv[0], pv[1]);
+                        pk[2 * c4 + 1] = ptx::pack_half2(pv[2], pv[3]);
+                        dk[2 * c4] = pack_bf162(zv[0], zv[1]);
+                        dk[2 * c4 + 1] = pack_bf162(zv[2], zv[3]);
+                    }
                 }
                 // The previous step's dV, dK and dQ^T MMAs must be done reading P and dZ.
                 if (g > 0 && !__all_sync(0xffffffffu, wait_phase(ds_free, (g - 1) & 1, wctx, kSitePvDone))) {
@@ -691,14 +755,14 @@ __device__ __forceinline__ void load_floats(const T* __restrict__ p, float (&v)[
     }
 }
 
-// Per query row: Dd = sum_c dO_c O_c (FP32, dO as the FP16 value the MMAs
-// read) and lse2 = lse * log2(e); padding rows up to sq_pad get Dd = 0 and
-// lse2 = +inf (their probabilities are 0).  One warp per row, D / 32 elements
-// per lane.
+// Per query row, negated for the kernel's fused adds: -Dd with Dd = sum_c
+// dO_c O_c (FP32, dO as the FP16 value the MMAs read) and -lse2 with lse2 =
+// lse * log2(e); padding rows up to sq_pad get 0 and -inf (their
+// probabilities are 0).  One warp per row, D / 32 elements per lane.
 template <int D, typename OT, typename IT>
 __global__ void __launch_bounds__(256) bwd_rows_kernel(const IT* __restrict__ dout, const OT* __restrict__ out,
-                                                        const float* __restrict__ lse, float* __restrict__ lse2,
-                                                        float* __restrict__ dd, int seq_q, int sq_pad)
+                                                        const float* __restrict__ lse, float* __restrict__ nlse2,
+                                                        float* __restrict__ ndd, int seq_q, int sq_pad)
 {
     const int row = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
     if (row >= sq_pad) return;
@@ -706,8 +770,8 @@ __global__ void __launch_bounds__(256) bwd_rows_kernel(const IT* __restrict__ do
     const int64_t o = slice * sq_pad + row;
     if (row >= seq_q) {
         if (lane == 0) {
-            dd[o] = 0.f;
-            lse2[o] = INFINITY;
+            ndd[o] = 0.f;
+            nlse2[o] = -INFINITY;
         }
         return;
     }
@@ -729,8 +793,8 @@ __global__ void __launch_bounds__(256) bwd_rows_kernel(const IT* __restrict__ do
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
     if (lane == 0) {
-        dd[o] = acc;
-        lse2[o] = lse[slice * seq_q + row] * 1.4426950408889634f;
+        ndd[o] = -acc;
+        nlse2[o] = lse[slice * seq_q + row] * -1.4426950408889634f;
     }
 }
 

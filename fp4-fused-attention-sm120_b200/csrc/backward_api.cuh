@@ -44,7 +44,7 @@ int failf(int code, const char* fmt, ...)
     } while (0)
 
 struct BwdWorkspace {
-    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, lse2, dd, v16, do16, total;
+    size_t q_codes, k_codes, q_sf, k_sf, qq, kq, nlse2, ndd, v16, do16, total;
 };
 
 struct BwdShape {
@@ -83,8 +83,8 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s, int in_dtype)
     w.k_sf = take(n * s.nk * 512);
     w.qq = take(n * s.sq * s.d * 2);
     w.kq = take(n * s.sk * s.d * 2);
-    w.lse2 = take(n * s.sq_pad * 4);
-    w.dd = take(n * s.sq_pad * 4);
+    w.nlse2 = take(n * s.sq_pad * 4);
+    w.ndd = take(n * s.sq_pad * 4);
     w.v16 = w.do16 = off;
     if (in_dtype == FP4ATTN_F32) {
         w.v16 = take(n * s.sk * s.d * 2);
@@ -95,7 +95,7 @@ BwdWorkspace plan_bwd_workspace(const BwdShape& s, int in_dtype)
 }
 
 // Everything before the backward kernel: Q and K codes, scale tiles and BF16
-// dequantised copies; Dd and lse2 per query row; dQ cleared.
+// dequantised copies; -Dd and -lse2 per query row; dQ cleared.
 template <int D, typename IT>
 int bwd_prepare_t(const BwdShape& s, const void* Q, const void* K, const void* V, const void* Out, int out_dtype,
                   const void* dOut, const float* lse, float* dQ, int ocp, uint8_t* ws, const BwdWorkspace& w,
@@ -123,16 +123,16 @@ int bwd_prepare_t(const BwdShape& s, const void* Q, const void* K, const void* V
         fp4attn::bwd_convert_kernel<<<dim3(gx, 2), 256, 0, st>>>(jv, jo);
         BWD_CUDA(cudaGetLastError());
     }
-    float* lse2 = reinterpret_cast<float*>(ws + w.lse2);
-    float* dd = reinterpret_cast<float*>(ws + w.dd);
+    float* nlse2 = reinterpret_cast<float*>(ws + w.nlse2);
+    float* ndd = reinterpret_cast<float*>(ws + w.ndd);
     const dim3 grid((s.sq_pad + 7) / 8, static_cast<unsigned>(s.slices));
     const IT* go = static_cast<const IT*>(dOut);
     if (out_dtype == FP4ATTN_F32)
         fp4attn::bwd_rows_kernel<D, float, IT>
-            <<<grid, 256, 0, st>>>(go, static_cast<const float*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+            <<<grid, 256, 0, st>>>(go, static_cast<const float*>(Out), lse, nlse2, ndd, s.sq, s.sq_pad);
     else
         fp4attn::bwd_rows_kernel<D, __half, IT>
-            <<<grid, 256, 0, st>>>(go, static_cast<const __half*>(Out), lse, lse2, dd, s.sq, s.sq_pad);
+            <<<grid, 256, 0, st>>>(go, static_cast<const __half*>(Out), lse, nlse2, ndd, s.sq, s.sq_pad);
     BWD_CUDA(cudaGetLastError());
     // The kernel adds every key tile's contribution into dQ.
     BWD_CUDA(cudaMemsetAsync(dQ, 0, static_cast<size_t>(s.slices) * s.sq * D * 4, st));
@@ -187,8 +187,8 @@ int bwd_attend(const BwdShape& s, int in_dtype, const void* V, const void* dOut,
     a.scale_log2 = scale * 1.4426950408889634f;
     a.q_sf = ws + w.q_sf;
     a.k_sf = ws + w.k_sf;
-    a.lse2 = reinterpret_cast<const float*>(ws + w.lse2);
-    a.dd = reinterpret_cast<const float*>(ws + w.dd);
+    a.nlse2 = reinterpret_cast<const float*>(ws + w.nlse2);
+    a.ndd = reinterpret_cast<const float*>(ws + w.ndd);
     a.dq = dQ;
     a.dk = dK;
     a.dv = dV;
