@@ -54,6 +54,8 @@ def parse():
                     help="steps of this rank's share of the box-scale job (0: skip)")
     ap.add_argument("--pass", dest="direction", choices=["forward", "backward"], default="forward",
                     help="forward (the headline) or the backward pass of the workload")
+    ap.add_argument("--in-dtype", choices=["float16", "float32"], default="float16",
+                    help="backward pass: Q, K, V and dO in FP16 or FP32 (FP32 adds the FP16 conversion of V and dO)")
     return ap.parse_args()
 
 
@@ -348,9 +350,12 @@ def bench_backward(args, world, rank, local):
     n = w.slices
     g = torch.Generator(device=dev).manual_seed(args.seed + 1)
     dO = torch.randn(Q.shape, device=dev, generator=g).half()
+    idt = fa.F32 if args.in_dtype == "float32" else fa.F16
+    if idt == fa.F32:  # the same values, widened
+        Q, K, V, dO = (t.float() for t in (Q, K, V, dO))
     odt = torch.float16 if w.out_dtype == "float16" else torch.float32
     out, lse = fa.fused_fp4_attention_lse(Q, K, V, out_dtype=odt)
-    ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim, fa.F16), dtype=torch.uint8,
+    ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim, idt), dtype=torch.uint8,
                      device=dev)
     dq, dk, dv = (torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (Q, K, V))
     L = fa.lib()
@@ -359,12 +364,12 @@ def bench_backward(args, world, rank, local):
 
     def step(ev_a=None, ev_b=None):
         rc = L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dO.data_ptr(),
-                                        lse.data_ptr(), dq.data_ptr(), fa.F16, fa._dtype_code(out), *sh,
+                                        lse.data_ptr(), dq.data_ptr(), idt, fa._dtype_code(out), *sh,
                                         fa.SCALE_REFERENCE, ws.data_ptr(), ws.numel(), stream.cuda_stream)
         if ev_a is not None:
             ev_a.record(stream)
         rc = rc or L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                             dv.data_ptr(), fa.F16, *sh, 0.0, fa.MASK_NONE, ws.data_ptr(),
+                                             dv.data_ptr(), idt, *sh, 0.0, fa.MASK_NONE, ws.data_ptr(),
                                              ws.numel(), stream.cuda_stream)
         if ev_b is not None:
             ev_b.record(stream)
@@ -429,8 +434,8 @@ def bench_backward(args, world, rank, local):
         "metric": "fused FP4 attention backward TFLOPS", "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (S) + f16/bf16 (dP, dV, dK, dQ)",
-        "data": "synthetic (seeded N(0,1) FP16 on device)",
-        "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "l2": l2,
+        "data": "synthetic (seeded N(0,1) FP16 on device" + (", widened to FP32)" if idt == fa.F32 else ")"),
+        "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "in_dtype": args.in_dtype, "l2": l2,
                    "slices_per_gpu": n, "job_slices": n * world, "parallelism": f"slice-shard x{world}"},
         "roofline": {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": flops / (kern_ms * 1e-3) / 1e12 / peak, "traffic": profile_traffic(w.name, "fp4_attention_bwd_kernel"),
@@ -438,7 +443,9 @@ def bench_backward(args, world, rank, local):
                                    f"{bf16:g} TFLOP/s",
                      "kernel": "fp4_attention_bwd_kernel", "kernel_ms": kern_ms},
         "frac_of_mixed_roofline_step": value / world / peak,
-        "gpu_launches": 3 * args.steps,  # per pass: quantise, rows, backward kernel (plus one memset of dQ)
+        # per pass: quantise, rows, backward kernel (plus one memset of dQ); FP32
+        # input adds the FP16 conversion of V and dO
+        "gpu_launches": (4 if idt == fa.F32 else 3) * args.steps,
         "clocks": clocks,
         "device_status": int(status),
     }
