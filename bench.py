@@ -54,6 +54,9 @@ def parse():
                     help="steps of this rank's share of the box-scale job (0: skip)")
     ap.add_argument("--pass", dest="direction", choices=["forward", "backward"], default="forward",
                     help="forward (the headline) or the backward pass of the workload")
+    ap.add_argument("--causal", action="store_true",
+                    help="bottom-right causal mask (not in the reference); FLOPs counted over the visible "
+                         "(query, key) pairs")
     ap.add_argument("--in-dtype", choices=["float16", "float32"], default="float16",
                     help="backward pass: Q, K, V and dO in FP16 or FP32 (FP32 adds the FP16 conversion of V and dO)")
     return ap.parse_args()
@@ -87,6 +90,16 @@ def mixed_roofline(w, bf16_tflops):
     f_half = w.flops() / 2
     t = f_half / (4 * bf16_tflops) + f_half / bf16_tflops
     return w.flops() / t
+
+
+def visible_fraction(seq_q, seq_k, causal):
+    """The share of (query, key) pairs a query sees: 1 without a mask; with
+    the bottom-right causal mask, query i sees keys j <= i + seq_k - seq_q."""
+    if not causal:
+        return 1.0
+    off = seq_k - seq_q
+    pairs = sum(max(0, min(seq_k, i + off + 1)) for i in range(seq_q))
+    return pairs / (seq_q * seq_k)
 
 
 class ClockSampler:
@@ -298,11 +311,16 @@ def job_config(args, world, rank):
     _, l2 = l2_note(io_bytes)
     config = {"workload": base.name, "shape": base.describe(), "slices_per_gpu": n, "job_slices": job.slices,
               "parallelism": f"slice-shard x{world}", "l2": l2}
+    if args.causal:
+        config["mask"] = "causal (FLOPs over the visible pairs)"
     return base, job, strong, lo, hi, config
 
 
 def reference_arm(args, world, rank):
     if rank != 0:
+        return
+    if args.causal:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference has no causal mask"}), flush=True)
         return
     base, _, strong, _, _, config = job_config(args, world, rank)
     cpu = CpuReference(base)
@@ -354,13 +372,14 @@ def bench_backward(args, world, rank, local):
     if idt == fa.F32:  # the same values, widened
         Q, K, V, dO = (t.float() for t in (Q, K, V, dO))
     odt = torch.float16 if w.out_dtype == "float16" else torch.float32
-    out, lse = fa.fused_fp4_attention_lse(Q, K, V, out_dtype=odt)
+    out, lse = fa.fused_fp4_attention_lse(Q, K, V, out_dtype=odt, causal=args.causal)
     ws = torch.empty(fa.backward_workspace_size(1, n, w.seq_q, w.seq_k, w.head_dim, idt), dtype=torch.uint8,
                      device=dev)
     dq, dk, dv = (torch.empty(t.shape, dtype=torch.float32, device=dev) for t in (Q, K, V))
     L = fa.lib()
     stream = torch.cuda.current_stream(dev)
     sh = (1, n, w.seq_q, w.seq_k, w.head_dim)
+    mask = fa.MASK_CAUSAL if args.causal else fa.MASK_NONE
 
     def step(ev_a=None, ev_b=None):
         rc = L.fp4attn_backward_prepare(Q.data_ptr(), K.data_ptr(), V.data_ptr(), out.data_ptr(), dO.data_ptr(),
@@ -369,8 +388,8 @@ def bench_backward(args, world, rank, local):
         if ev_a is not None:
             ev_a.record(stream)
         rc = rc or L.fp4attn_backward_attend(V.data_ptr(), dO.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-                                             dv.data_ptr(), idt, *sh, 0.0, fa.MASK_NONE, ws.data_ptr(),
-                                             ws.numel(), stream.cuda_stream)
+                                             dv.data_ptr(), idt, *sh, 0.0, mask, ws.data_ptr(), ws.numel(),
+                                             stream.cuda_stream)
         if ev_b is not None:
             ev_b.record(stream)
         if rc != fa.OK:
@@ -422,7 +441,7 @@ def bench_backward(args, world, rank, local):
     ms_step, kern_ms, status = times.tolist()
     if rank != 0:
         return
-    flops = 10.0 * n * w.seq_q * w.seq_k * w.head_dim  # per rank
+    flops = 10.0 * n * w.seq_q * w.seq_k * w.head_dim * visible_fraction(w.seq_q, w.seq_k, args.causal)  # per rank
     value = world * flops / (ms_step * 1e-3) / 1e12
     burst, sustained, hbm, peak_src = measured_peaks()
     clocks = sampler.summary(t_wall0, t_wall1)
@@ -436,7 +455,8 @@ def bench_backward(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (S) + f16/bf16 (dP, dV, dK, dQ)",
         "data": "synthetic (seeded N(0,1) FP16 on device" + (", widened to FP32)" if idt == fa.F32 else ")"),
         "config": {"workload": w.name, "shape": w.describe(), "pass": "backward", "in_dtype": args.in_dtype, "l2": l2,
-                   "slices_per_gpu": n, "job_slices": n * world, "parallelism": f"slice-shard x{world}"},
+                   "slices_per_gpu": n, "job_slices": n * world, "parallelism": f"slice-shard x{world}",
+                   **({"mask": "causal (FLOPs over the visible pairs)"} if args.causal else {})},
         "roofline": {"bound": "tensor", "achieved": flops / (kern_ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                      "frac": flops / (kern_ms * 1e-3) / 1e12 / peak, "traffic": profile_traffic(w.name, "fp4_attention_bwd_kernel"),
                      "peak_basis": f"mixed: S at 4x and dP, dV, dK, dQ at 1x the {peak_src} {basis} bf16 dense "
@@ -454,6 +474,8 @@ def bench_backward(args, world, rank, local):
 
 def main():
     args = parse()
+    if args.causal and args.fuse_q:
+        raise SystemExit("--fuse-q has no causal variant")
     if args.direction == "backward" and args.impl == "reference":
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps({"impl": "reference", "unavailable": "the reference has no backward pass"}), flush=True)
@@ -487,7 +509,7 @@ def main():
     ws = torch.empty(fa.workspace_size(1, n, base.seq_q, base.seq_k, base.head_dim), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     shard = wl.Workload(base.name, 1, n, base.seq_q, base.seq_k, base.head_dim)
-    flops_rank = shard.flops()
+    flops_rank = shard.flops() * visible_fraction(base.seq_q, base.seq_k, args.causal)
 
     def step(ev_q=None, ev_a=None, ev_b=None):
         if args.fuse_q:
@@ -505,7 +527,7 @@ def main():
         fa.prepare(Q, K, V, ws)
         if ev_a is not None:
             ev_a.record(stream)
-        fa.attend(V, out, ws, fa.F16, 1, n, base.seq_q, base.seq_k, base.head_dim)
+        fa.attend(V, out, ws, fa.F16, 1, n, base.seq_q, base.seq_k, base.head_dim, causal=args.causal)
         if ev_b is not None:
             ev_b.record(stream)
 
@@ -595,7 +617,7 @@ def main():
         ev_in[b].record(s_in)
         s_cp.wait_event(ev_in[b])
         s_cp.wait_event(ev_out[b])     # step i-2's output has left d_out[b]
-        fa.fused_fp4_attention_into(*d_in[b], d_out[b], ws, stream=s_cp)
+        fa.fused_fp4_attention_into(*d_in[b], d_out[b], ws, stream=s_cp, causal=args.causal)
         ev_cp[b].record(s_cp)
         s_out.wait_event(ev_cp[b])
         with torch.cuda.stream(s_out):
@@ -652,7 +674,7 @@ def main():
             kernel += " (Q quantised in the kernel; kernel_ms includes the K pre-pass)"
         traffic = profile_traffic(args.workload, kernel)
         cpu = None
-        if not args.no_cpu_baseline and world == 1:
+        if not args.no_cpu_baseline and world == 1 and not args.causal:  # the reference has no mask
             ref = CpuReference(base)
             ref.calibrate(10.0)
             r, _ = ref.run(ref.rows)
