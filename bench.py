@@ -464,8 +464,9 @@ def bench_backward(args, world, rank, local):
                      "kernel": "fp4_attention_bwd_kernel", "kernel_ms": kern_ms},
         "frac_of_mixed_roofline_step": value / world / peak,
         # per pass: quantise, rows, backward kernel (plus one memset of dQ); FP32
-        # input adds the FP16 conversion of V and dO
-        "gpu_launches": (4 if idt == fa.F32 else 3) * args.steps,
+        # input adds the FP16 conversion of V and dO; the timed region holds
+        # the timed passes and, interleaved, as many that time the kernel
+        "gpu_launches": 2 * (4 if idt == fa.F32 else 3) * args.steps,
         "clocks": clocks,
         "device_status": int(status),
     }
@@ -702,7 +703,9 @@ def main():
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
                     "overlap": "H2D, compute and D2H of consecutive steps on three streams, two buffer sets"},
-            "gpu_launches": 2 * args.steps,  # per step: one quantise launch (Q and K) + one attention launch
+            # per step: one quantise launch (Q and K) + one attention launch, in
+            # the timed steps and in the interleaved steps that time the kernel
+            "gpu_launches": 4 * args.steps,
             "clocks": clocks,
             "device_status": int(status_max),
         }
