@@ -39,3 +39,39 @@ def test_l2_rule_flushes_only_inputs_that_fit_twice_in_l2():
     assert flush and "flush" in text
     flush, text = bench.l2_note(256 << 20)
     assert not flush and "no flush" in text
+
+
+def _args(workload, causal=False):
+    import argparse
+    return argparse.Namespace(workload=workload, causal=causal)
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_weak_job_gives_each_rank_the_whole_workload(world):
+    base = wl.WORKLOADS["prefill_4k"]
+    seen = []
+    for rank in range(world):
+        b, job, strong, lo, hi, config = bench.job_config(_args("prefill_4k"), world, rank)
+        assert not strong and b is base
+        assert hi - lo == base.slices and job.slices == base.slices * world
+        assert config["slices_per_gpu"] == base.slices and config["job_slices"] == base.slices * world
+        seen.append((lo, hi))
+    assert seen == [(r * base.slices, (r + 1) * base.slices) for r in range(world)]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_box_scale_job_is_split_over_the_ranks(world):
+    ranges = [bench.job_config(_args("box_sharded_8k"), world, r)[3:5] for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == 512
+    assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))   # contiguous, no overlap, no gap
+    assert {hi - lo for lo, hi in ranges} == {512 // world}
+    assert bench.job_config(_args("box_sharded_8k"), world, 0)[2]   # strong scaling
+
+
+def test_both_arms_print_one_config():
+    # The reference arm prints job_config's dictionary as it is; the GPU arm
+    # prints the same object, so the keys and values agree by construction.
+    *_, config = bench.job_config(_args("prefill_4k"), 1, 0)
+    assert set(config) == {"workload", "shape", "slices_per_gpu", "job_slices", "parallelism", "l2"}
+    *_, causal = bench.job_config(_args("prefill_4k", causal=True), 1, 0)
+    assert causal["mask"].startswith("causal")
